@@ -1,0 +1,136 @@
+/*
+ * molten_rt.h -- C ABI of libmolten_rt.so, the runtime that loads the
+ * nvcc-built sm_100a cubins emitted by Molten's code generator and launches
+ * their kernels.  Plain pointers and sizes only; no torch or C++ types.
+ *
+ * It replaces, on the reference side (TxsharDev/molten v0.1.0):
+ *   - torch.utils.cpp_extension.load() of the generated .cu
+ *     (molten/runtime.py:72-79)                      -> molten_module_load*
+ *   - the per-kernel pybind launch wrapper "<name>_launch" emitted by
+ *     MoltenRuntime._make_extension (molten/runtime.py:96-199) and called by
+ *     CompiledKernel.__call__ (molten/runtime.py:31-36) -> molten_launch
+ *   - the implicit nvcc error path (molten/runtime.py:90-94)
+ *                                                    -> status + molten_last_error
+ *
+ * Every function returns MOLTEN_OK (0) or a nonzero MOLTEN_ERR_* code; the
+ * text of the last error of the calling thread is molten_last_error().
+ * Launches are asynchronous on the given stream (NULL = the legacy default
+ * stream) and never synchronise the device.
+ */
+#ifndef MOLTEN_RT_H
+#define MOLTEN_RT_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MOLTEN_OK 0
+#define MOLTEN_ERR_INVALID 1     /* bad argument: null pointer, size, alignment */
+#define MOLTEN_ERR_CUDA 2        /* a CUDA runtime / driver call failed */
+#define MOLTEN_ERR_NOT_FOUND 3   /* no such kernel in the module */
+#define MOLTEN_ERR_IO 4          /* cubin file missing or unreadable */
+
+#define MOLTEN_MAX_IO 8
+
+#ifdef __cplusplus
+#define MOLTEN_ALIGN64 alignas(64)
+#else
+#define MOLTEN_ALIGN64 _Alignas(64)
+#endif
+
+/* Launch geometry of one kernel.  cluster = {0,0,0} or {1,1,1}: no cluster. */
+typedef struct molten_launch_cfg {
+  uint32_t grid[3];
+  uint32_t block[3];
+  uint32_t cluster[3];
+  uint32_t smem_bytes;           /* dynamic shared memory per CTA */
+} molten_launch_cfg;
+
+/* Parameter block of every generated row / elementwise kernel
+ * (device side: molten::RowArgs in molten/row_engine.cuh). */
+typedef struct molten_row_args {
+  const void* in[MOLTEN_MAX_IO];
+  void* out[MOLTEN_MAX_IO];
+  long long rows;                /* rows of this launch (a shard may be fewer) */
+  long long row_offset;          /* global index of row 0 (masks, broadcasts) */
+  long long cols;
+  int* status;
+} molten_row_args;
+
+/* Parameter block of the generated tcgen05 GEMM kernels
+ * (device side: molten::GemmArgs in molten/gemm_sm100.cuh). */
+typedef struct molten_gemm_args {
+  MOLTEN_ALIGN64 unsigned char tmap_a[128];  /* from molten_encode_tma_2d */
+  MOLTEN_ALIGN64 unsigned char tmap_b[128];
+  const void* in[MOLTEN_MAX_IO];
+  void* out[MOLTEN_MAX_IO];
+  long long m, n, k;
+  long long row_offset;
+  int* status;
+  int pad_;
+} molten_gemm_args;
+
+/* Version of this ABI (major * 100 + minor). */
+int molten_version(void);
+
+/* Text of the last error on the calling thread ("" when none). */
+const char* molten_last_error(void);
+
+/* Number of CUDA devices visible to the process. */
+int molten_device_count(int* count);
+
+/* Wait for all work on `device`. */
+int molten_sync(int device);
+
+/* Load an sm_100a cubin into `device`'s primary context.
+ * Replaces torch.utils.cpp_extension.load (molten/runtime.py:72-79). */
+int molten_module_load(const char* cubin_path, int device, void** mod);
+
+/* Same from an in-memory cubin image. */
+int molten_module_load_data(const void* image, size_t nbytes, int device, void** mod);
+
+/* Unload a module; its kernels must no longer be running. */
+int molten_module_unload(void* mod);
+
+/* Registers per thread, max threads per block and static shared memory of
+ * a kernel (any output pointer may be NULL). */
+int molten_kernel_info(void* mod, const char* kernel, int* num_regs,
+                       int* max_threads, int* static_smem);
+
+/* Launch `kernel` of `mod` with one by-value parameter block of
+ * `params_bytes` bytes (molten_row_args or molten_gemm_args).
+ * Replaces the generated "<name>_launch" wrapper (molten/runtime.py:111-189)
+ * called from CompiledKernel.__call__ (molten/runtime.py:31-36). */
+int molten_launch(void* mod, const char* kernel, const molten_launch_cfg* cfg,
+                  const void* params, size_t params_bytes, void* stream);
+
+/* Element types for molten_encode_tma_2d. */
+#define MOLTEN_DT_BF16 0
+#define MOLTEN_DT_F16 1
+#define MOLTEN_DT_F32 2
+
+/* Encode a 2-D TMA descriptor (128 bytes, 64-byte aligned `tmap`) for a
+ * row-major matrix of `outer` rows of `inner` elements, rows
+ * `row_stride_bytes` apart, copied in boxes of box_inner x box_outer,
+ * with 128-byte swizzle when swizzle128 != 0.  Out-of-range box elements
+ * read as zero.  base must be 16-byte aligned and row_stride a multiple of
+ * 16 bytes. */
+int molten_encode_tma_2d(void* tmap, int dtype, const void* base,
+                         uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
+                         uint32_t box_inner, uint32_t box_outer, int swizzle128);
+
+/* Per-device error word that kernels with bounded waits set bits in
+ * (allocated on first use, then reused). */
+int molten_status_word(int device, int** dev_ptr);
+
+/* Read (and when reset != 0 clear) the device error word; synchronises. */
+int molten_read_status(int device, int* value, int reset);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOLTEN_RT_H */

@@ -1,0 +1,157 @@
+// Shared device helpers for every Molten sm_100a kernel: element types,
+// 16-byte vector slots with cache-hinted loads/stores, fp32 conversions.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include <type_traits>
+
+namespace molten {
+
+typedef __nv_bfloat16 bf16;
+typedef __half f16;
+
+// ---------------------------------------------------------------- conversion
+__device__ __forceinline__ float to_f32(float v) { return v; }
+__device__ __forceinline__ float to_f32(bf16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float to_f32(f16 v) { return __half2float(v); }
+
+template <typename T> __device__ __forceinline__ T from_f32(float v);
+template <> __device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ bf16 from_f32<bf16>(float v) { return __float2bfloat16_rn(v); }
+template <> __device__ __forceinline__ f16 from_f32<f16>(float v) { return __float2half_rn(v); }
+
+// ------------------------------------------------------------------- slots
+// A slot is VEC consecutive elements of one row, moved with the widest
+// aligned access that fits (16, 8, 4 or 2 bytes; 32-byte slots use two
+// 16-byte accesses).
+template <typename T, int VEC>
+struct alignas((sizeof(T) * VEC) >= 16 ? 16 : (sizeof(T) * VEC)) Slot {
+  T v[VEC];
+};
+
+enum LoadHint { kLoadDefault = 0, kLoadStream = 1 };
+enum StoreHint { kStoreDefault = 0, kStoreStream = 1 };
+
+template <int HINT>
+__device__ __forceinline__ uint4 ld16(const void* p) {
+  uint4 r;
+  if (HINT == kLoadStream) {
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  } else {
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  }
+  return r;
+}
+
+template <int HINT>
+__device__ __forceinline__ void st16(void* p, uint4 v) {
+  if (HINT == kStoreStream) {
+    asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};"
+                 :: "l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
+  } else {
+    asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};"
+                 :: "l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
+  }
+}
+
+template <int HINT, typename T, int VEC>
+__device__ __forceinline__ Slot<T, VEC> load_slot(const T* p) {
+  Slot<T, VEC> s;
+  constexpr int BYTES = sizeof(T) * VEC;
+  if constexpr (BYTES % 16 == 0) {
+#pragma unroll
+    for (int i = 0; i < BYTES / 16; ++i)
+      reinterpret_cast<uint4*>(&s)[i] = ld16<HINT>(reinterpret_cast<const char*>(p) + 16 * i);
+  } else if constexpr (BYTES == 8) {
+    *reinterpret_cast<uint2*>(&s) = __ldg(reinterpret_cast<const uint2*>(p));
+  } else if constexpr (BYTES == 4) {
+    *reinterpret_cast<uint32_t*>(&s) = __ldg(reinterpret_cast<const unsigned int*>(p));
+  } else {
+    static_assert(BYTES == 2, "unsupported slot size");
+    *reinterpret_cast<uint16_t*>(&s) = __ldg(reinterpret_cast<const unsigned short*>(p));
+  }
+  return s;
+}
+
+template <int HINT, typename T, int VEC>
+__device__ __forceinline__ void store_slot(T* p, const Slot<T, VEC>& s) {
+  constexpr int BYTES = sizeof(T) * VEC;
+  if constexpr (BYTES % 16 == 0) {
+#pragma unroll
+    for (int i = 0; i < BYTES / 16; ++i)
+      st16<HINT>(reinterpret_cast<char*>(p) + 16 * i, reinterpret_cast<const uint4*>(&s)[i]);
+  } else if constexpr (BYTES == 8) {
+    *reinterpret_cast<uint2*>(p) = *reinterpret_cast<const uint2*>(&s);
+  } else if constexpr (BYTES == 4) {
+    *reinterpret_cast<uint32_t*>(p) = *reinterpret_cast<const uint32_t*>(&s);
+  } else {
+    *reinterpret_cast<uint16_t*>(p) = *reinterpret_cast<const uint16_t*>(&s);
+  }
+}
+
+// Write VEC fp32 values into a slot of T, rounding to nearest even once.
+template <typename T, int VEC>
+__device__ __forceinline__ void pack_slot(Slot<T, VEC>& s, const float (&f)[VEC]) {
+  if constexpr (sizeof(T) == 2 && VEC % 2 == 0) {
+#pragma unroll
+    for (int e = 0; e < VEC; e += 2) {
+      if constexpr (std::is_same<T, bf16>::value) {
+        *reinterpret_cast<__nv_bfloat162*>(&s.v[e]) = __floats2bfloat162_rn(f[e], f[e + 1]);
+      } else {
+        *reinterpret_cast<__half2*>(&s.v[e]) = __floats2half2_rn(f[e], f[e + 1]);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) s.v[e] = from_f32<T>(f[e]);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ float load_scalar(const T* p) { return to_f32(p[0]); }
+
+template <typename T>
+__device__ __forceinline__ void store_scalar(T* p, float v) { p[0] = from_f32<T>(v); }
+
+// ------------------------------------------------------- elementwise math
+// Every function computes in fp32.  PRECISE selects CUDA's full-precision
+// library functions; otherwise the fast hardware intrinsics are used (the
+// host picks fast math only when the output precision is 16-bit).
+template <bool PRECISE> __device__ __forceinline__ float m_exp(float x) {
+  if constexpr (PRECISE) return expf(x); else return __expf(x);
+}
+template <bool PRECISE> __device__ __forceinline__ float m_log(float x) {
+  if constexpr (PRECISE) return logf(x); else return __logf(x);
+}
+template <bool PRECISE> __device__ __forceinline__ float m_div(float a, float b) {
+  if constexpr (PRECISE) return a / b; else return __fdividef(a, b);
+}
+// logistic function 1 / (1 + e^-x)
+template <bool PRECISE> __device__ __forceinline__ float m_sigmoid(float x) {
+  return m_div<PRECISE>(1.0f, 1.0f + m_exp<PRECISE>(-x));
+}
+// x * sigmoid(x)
+template <bool PRECISE> __device__ __forceinline__ float m_silu(float x) {
+  return m_div<PRECISE>(x, 1.0f + m_exp<PRECISE>(-x));
+}
+// tanh; the 16-bit path uses tanh(x) = 1 - 2 / (e^{2x} + 1), whose absolute
+// error stays near fp32 epsilon over the whole range.
+template <bool PRECISE> __device__ __forceinline__ float m_tanh(float x) {
+  if constexpr (PRECISE) return tanhf(x);
+  else return 1.0f - __fdividef(2.0f, __expf(2.0f * x) + 1.0f);
+}
+// tanh-form GELU, 0.5 v (1 + tanh(k (v + 0.044715 v^3))) with k = sqrt(2/pi),
+// evaluated through the identity 0.5 (1 + tanh(z)) = 1 / (1 + e^{-2z}), which
+// has no cancellation for large negative v.
+template <bool PRECISE> __device__ __forceinline__ float m_gelu_tanh(float v) {
+  const float k2 = 1.5957691216057308f;  // 2 * sqrt(2 / pi)
+  const float z2 = k2 * v * fmaf(0.044715f * v, v, 1.0f);
+  return m_div<PRECISE>(v, 1.0f + m_exp<PRECISE>(-z2));
+}
+
+}  // namespace molten

@@ -1,0 +1,346 @@
+// tcgen05 / TMEM / TMA GEMM engine for C[M,N] = epilogue(A[M,K] @ B[K,N]).
+//
+// A is row-major (K-major operand), B is row-major [K, N] (MN-major operand,
+// the layout the reference's matmul reads, codegen.py:354-355).  One CTA per
+// SM runs a persistent loop over BM x BN output tiles with three roles:
+//
+//   warp 0      TMA producer: A box {BK, BM} and BN/64 B boxes {64, BK},
+//               128-byte swizzle, into a STAGES-deep shared-memory ring;
+//   warp 1      TMEM owner + MMA issuer: one elected thread issues
+//               tcgen05.mma.cta_group::1.kind::f16 (bf16 in, fp32 in TMEM)
+//               and tcgen05.commit's the ring slots and accumulators back;
+//   warps 4..7  epilogue: tcgen05.ld 32 columns at a time, apply the
+//               generated elementwise epilogue (bias, GELU ...) in fp32,
+//               round once and store.
+//
+// The accumulator is double-buffered in TMEM (2 x BN fp32 columns) so the
+// epilogue of tile i overlaps the main loop of tile i+1.  No TMA multicast.
+// Every mbarrier wait is bounded: on timeout the CTA records an error bit in
+// *status, stops issuing work, drains what it issued and frees its TMEM.
+#pragma once
+
+#include <cuda.h>
+#include "molten/common.cuh"
+
+namespace molten {
+
+// Kernel parameter block; mirrored by `molten_gemm_args` in include/molten_rt.h.
+struct alignas(64) GemmArgs {
+  CUtensorMap tmap_a;              // A [M, K], box {BK, BM}, 128B swizzle
+  CUtensorMap tmap_b;              // B [K, N], box {64, BK}, 128B swizzle
+  const void* in[8];               // epilogue operands (kernel order)
+  void* out[8];                    // outputs
+  long long m, n, k;
+  long long row_offset;            // global row of local row 0
+  int* status;                     // error bits (may be null)
+  int pad_;
+};
+
+enum GemmStatus { kGemmTimeoutFull = 1, kGemmTimeoutEmpty = 2, kGemmTimeoutAcc = 4,
+                  kGemmTimeoutDrain = 8 };
+
+#ifndef MOLTEN_WAIT_NS
+#define MOLTEN_WAIT_NS 1000000000ull   // 1 s per wait
+#endif
+
+// ------------------------------------------------------------ primitives
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile("{\n\t.reg .pred p;\n\t"
+               "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+               "selp.u32 %0, 1, 0, p;\n\t}"
+               : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+  return ok != 0;
+}
+// Wait for the phase with the given parity to complete; false on timeout.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > MOLTEN_WAIT_NS) return false;
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+               " [%0], [%1, {%3, %4}], [%2];"
+               :: "r"(dst), "l"(map), "r"(bar), "r"(x), "r"(y) : "memory");
+}
+
+// tcgen05 shared-memory matrix descriptor (sm_100 version 1).
+//   start address, LBO, SBO in 16-byte units; layout 2 = 128-byte swizzle.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;           // version
+  d |= (uint64_t)2 << 61;           // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor, kind::f16: D f32, A/B bf16 (or f16), A K-major,
+// B MN-major, shape M x N.
+template <int M, int N, bool F16IN>
+__device__ __forceinline__ constexpr uint32_t umma_idesc() {
+  return (1u << 4)                                  // D format f32
+       | ((F16IN ? 0u : 1u) << 7)                    // A format
+       | ((F16IN ? 0u : 1u) << 10)                   // B format
+       | (0u << 15)                                  // A K-major
+       | (1u << 16)                                  // B MN-major
+       | ((uint32_t)(N >> 3) << 17)
+       | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile("{\n\t.reg .pred p;\n\t"
+               "setp.ne.b32 p, %4, 0;\n\t"
+               "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+               :: "r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(accumulate) : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+               :: "r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// 32 lanes x 32 consecutive fp32 columns -> 32 registers per thread.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&r)[32]) {
+  uint32_t u[32];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+               "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+               "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+               : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]),
+                 "=r"(u[6]), "=r"(u[7]), "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]),
+                 "=r"(u[12]), "=r"(u[13]), "=r"(u[14]), "=r"(u[15]), "=r"(u[16]), "=r"(u[17]),
+                 "=r"(u[18]), "=r"(u[19]), "=r"(u[20]), "=r"(u[21]), "=r"(u[22]), "=r"(u[23]),
+                 "=r"(u[24]), "=r"(u[25]), "=r"(u[26]), "=r"(u[27]), "=r"(u[28]), "=r"(u[29]),
+                 "=r"(u[30]), "=r"(u[31])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) r[i] = __uint_as_float(u[i]);
+}
+
+// ------------------------------------------------------------ the engine
+template <int BM_, int BN_, int BK_, int STAGES_>
+struct GemmLayout {
+  static constexpr int BM = BM_, BN = BN_, BK = BK_, STAGES = STAGES_;
+  static_assert(BM == 128, "one CTA owns the 128 TMEM lanes");
+  static_assert(BK == 64, "BK is one 128-byte swizzle row of 16-bit elements");
+  static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be 64..256, a multiple of 64");
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_CHUNK_BYTES = BK * 64 * 2;          // one {64, BK} box
+  static constexpr int B_BYTES = (BN / 64) * B_CHUNK_BYTES;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int ACC_BUFS = 2;
+  static constexpr int TMEM_COLS = (2 * BN <= 128) ? 128 : ((2 * BN <= 256) ? 256 : 512);
+  // barriers: full[S], empty[S], acc_full[2], acc_empty[2], done
+  static constexpr int BAR_OFFSET = STAGES * STAGE_BYTES;
+  static constexpr int NUM_BARS = 2 * STAGES + 5;
+  static constexpr int SMEM_BYTES = BAR_OFFSET + NUM_BARS * 8 + 16 + 1024;  // + alignment slack
+  static constexpr int THREADS = 256;                        // 8 warps
+  static constexpr int EPI_WARP0 = 4;                        // warps 4..7: TMEM lane quarters 0..3
+  static constexpr int EPI_WARPS = 4;
+};
+
+struct GemmShared {
+  uint8_t* tiles;          // 1024-aligned ring of stages
+  uint64_t* bars;
+  uint32_t* tmem_slot;
+  volatile int* abort_flag;
+};
+
+template <class L>
+__device__ __forceinline__ GemmShared gemm_carve(uint8_t* raw) {
+  GemmShared s;
+  const uintptr_t base = (reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023);
+  s.tiles = reinterpret_cast<uint8_t*>(base);
+  s.bars = reinterpret_cast<uint64_t*>(s.tiles + L::BAR_OFFSET);
+  s.tmem_slot = reinterpret_cast<uint32_t*>(s.bars + L::NUM_BARS);
+  s.abort_flag = reinterpret_cast<volatile int*>(s.tmem_slot + 1);
+  return s;
+}
+
+__device__ __forceinline__ int gemm_tid() { return threadIdx.y * blockDim.x + threadIdx.x; }
+
+// barrier addresses
+template <class L> struct Bars {
+  uint32_t base;
+  __device__ __forceinline__ explicit Bars(const GemmShared& s) : base(smem_u32(s.bars)) {}
+  __device__ __forceinline__ uint32_t full(int i) const { return base + 8u * i; }
+  __device__ __forceinline__ uint32_t empty(int i) const { return base + 8u * (L::STAGES + i); }
+  __device__ __forceinline__ uint32_t acc_full(int b) const { return base + 8u * (2 * L::STAGES + b); }
+  __device__ __forceinline__ uint32_t acc_empty(int b) const { return base + 8u * (2 * L::STAGES + 2 + b); }
+  __device__ __forceinline__ uint32_t done() const { return base + 8u * (2 * L::STAGES + 4); }
+};
+
+__device__ __forceinline__ void gemm_fail(const GemmShared& s, const GemmArgs& args, int code) {
+  *s.abort_flag = 1;
+  if (args.status) atomicOr(args.status, code);
+}
+
+// Barrier init + TMEM allocation.  Every thread calls it; the caller then
+// runs __syncthreads() before gemm_roles.
+template <class L>
+__device__ __forceinline__ void gemm_init(const GemmShared& s, const GemmArgs& args) {
+  const int tid = gemm_tid(), warp = tid / 32;
+  if (tid == 0) {
+    const Bars<L> b(s);
+    for (int i = 0; i < L::STAGES; ++i) { mbar_init(b.full(i), 1); mbar_init(b.empty(i), 1); }
+    for (int i = 0; i < 2; ++i) { mbar_init(b.acc_full(i), 1); mbar_init(b.acc_empty(i), L::EPI_WARPS); }
+    mbar_init(b.done(), 1);
+    *s.abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" :: "l"(&args.tmap_a) : "memory");
+    asm volatile("prefetch.tensormap [%0];" :: "l"(&args.tmap_b) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 :: "r"(smem_u32(s.tmem_slot)), "r"((uint32_t)L::TMEM_COLS) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+}
+
+// The three roles.  Epi::apply(args, row, col0, acc[32]) writes C[row, col0..col0+31].
+template <class L, bool F16IN, class Epi>
+__device__ __forceinline__ void gemm_roles(const GemmShared& s, const GemmArgs& args) {
+  tc_fence_after();
+  const int tid = gemm_tid(), warp = tid / 32, lane = tid % 32;
+  const uint32_t tmem = *s.tmem_slot;
+  const Bars<L> bar(s);
+  const long long MB = (args.m + L::BM - 1) / L::BM;
+  const long long NB = (args.n + L::BN - 1) / L::BN;
+  const long long T = MB * NB;
+  const int KB = (int)((args.k + L::BK - 1) / L::BK);
+
+  if (warp == 0) {
+    // ------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      uint32_t st = 0, ph = 0;
+      long long issued = 0;
+      for (long long tile = blockIdx.x; tile < T && !*s.abort_flag; tile += gridDim.x) {
+        const int m0 = (int)((tile % MB) * L::BM), n0 = (int)((tile / MB) * L::BN);
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(bar.empty(st), ph ^ 1u)) { gemm_fail(s, args, kGemmTimeoutEmpty); break; }
+          if (*s.abort_flag) break;
+          const uint32_t a_dst = smem_u32(s.tiles + st * L::STAGE_BYTES);
+          const uint32_t b_dst = a_dst + L::A_BYTES;
+          mbar_expect_tx(bar.full(st), (uint32_t)L::STAGE_BYTES);
+          tma_load_2d(a_dst, &args.tmap_a, bar.full(st), kb * L::BK, m0);
+#pragma unroll
+          for (int c = 0; c < L::BN / 64; ++c)
+            tma_load_2d(b_dst + c * L::B_CHUNK_BYTES, &args.tmap_b, bar.full(st), n0 + 64 * c, kb * L::BK);
+          ++issued;
+          if (++st == (uint32_t)L::STAGES) { st = 0; ph ^= 1u; }
+        }
+      }
+      if (*s.abort_flag) {
+        // let the copies this thread issued land before the CTA can exit
+        uint32_t ds = st, dp = ph;
+        for (long long i = 0; i < issued && i < L::STAGES; ++i) {
+          if (ds == 0) { ds = L::STAGES - 1; dp ^= 1u; } else { --ds; }
+          if (!mbar_wait(bar.full(ds), dp)) { if (args.status) atomicOr(args.status, kGemmTimeoutDrain); }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t IDESC = umma_idesc<L::BM, L::BN, F16IN>();
+      uint32_t st = 0, ph = 0;
+      long long i = 0;
+      bool ok = true;
+      for (long long tile = blockIdx.x; tile < T && ok && !*s.abort_flag; tile += gridDim.x, ++i) {
+        const int b = (int)(i & 1);
+        const uint32_t acc_ph = (uint32_t)((i >> 1) & 1);
+        if (!mbar_wait(bar.acc_empty(b), acc_ph ^ 1u)) { gemm_fail(s, args, kGemmTimeoutAcc); break; }
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(b * L::BN);
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(bar.full(st), ph)) { gemm_fail(s, args, kGemmTimeoutFull); ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(s.tiles + st * L::STAGE_BYTES);
+          const uint32_t b_base = a_base + L::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < L::BK / 16; ++kk) {
+            const uint64_t ad = umma_desc(a_base + 32u * kk, 16u, 1024u);
+            const uint64_t bd = umma_desc(b_base + 2048u * kk, (uint32_t)L::B_CHUNK_BYTES, 1024u);
+            umma_f16(d, ad, bd, IDESC, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(bar.empty(st));
+          if (++st == (uint32_t)L::STAGES) { st = 0; ph ^= 1u; }
+        }
+        if (ok) umma_commit(bar.acc_full(b));
+      }
+      // all MMAs this thread issued must finish before TMEM is released
+      umma_commit(bar.done());
+      if (!mbar_wait(bar.done(), 0u)) { if (args.status) atomicOr(args.status, kGemmTimeoutDrain); }
+    }
+  } else if (warp >= L::EPI_WARP0) {
+    // ------------------------------------------------------------- epilogue
+    const int quarter = warp % 4;                  // TMEM lanes 32*quarter .. +31
+    long long i = 0;
+    for (long long tile = blockIdx.x; tile < T; tile += gridDim.x, ++i) {
+      const int b = (int)(i & 1);
+      const uint32_t acc_ph = (uint32_t)((i >> 1) & 1);
+      const bool got = mbar_wait(bar.acc_full(b), acc_ph);
+      if (!__all_sync(0xffffffffu, got ? 1 : 0)) {
+        if (lane == 0) gemm_fail(s, args, kGemmTimeoutAcc);
+        break;
+      }
+      tc_fence_after();
+      const long long row = (tile % MB) * L::BM + quarter * 32 + lane;
+      const long long nbase = (tile / MB) * L::BN;
+#pragma unroll 1
+      for (int c = 0; c < L::BN / 32; ++c) {
+        float acc[32];
+        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * L::BN + c * 32), acc);
+        const long long col0 = nbase + 32 * c;
+        if (col0 < args.n) Epi::apply(args, row, col0, acc);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar.acc_empty(b));
+      if (__any_sync(0xffffffffu, *s.abort_flag ? 1 : 0)) break;
+    }
+  }
+}
+
+// Release TMEM.  Every thread calls it after the caller's final __syncthreads().
+template <class L>
+__device__ __forceinline__ void gemm_teardown(const GemmShared& s) {
+  const int warp = gemm_tid() / 32;
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;"
+                 :: "r"(*s.tmem_slot), "r"((uint32_t)L::TMEM_COLS) : "memory");
+  }
+}
+
+}  // namespace molten

@@ -1,0 +1,146 @@
+// Row engine: the scaffolding that every generated row / elementwise kernel
+// is built on.  A row of `cols` elements is split into slots of VEC elements;
+// a team of TPC threads in each of CL CTAs of a cluster owns one row, thread
+// t of CTA rank r holding slots  j = (r * TPC + t) + k * (TPC * CL),
+// k = 0 .. NV-1, so that a warp touches 32 consecutive slots per k.
+// A CTA runs RPC such teams side by side (RPC rows at a time).
+//
+// The generated code keeps its slots in registers, so a row is read from
+// HBM once; reductions go warp shuffle -> shared memory -> (cluster) DSMEM.
+#pragma once
+
+#include "molten/common.cuh"
+
+namespace molten {
+
+#define MOLTEN_MAX_IO 8
+
+// Kernel parameter block of every row / elementwise kernel.  Mirrored by
+// `molten_row_args` in include/molten_rt.h and by the ctypes structure in
+// molten_b200/_capi.py.
+struct RowArgs {
+  const void* in[MOLTEN_MAX_IO];   // external inputs, kernel order
+  void* out[MOLTEN_MAX_IO];        // outputs, kernel order
+  long long rows;                  // rows handled by this launch
+  long long row_offset;            // global index of this launch's row 0
+  long long cols;                  // elements per row (must equal COLS)
+  int* status;                     // unused by row kernels; may be null
+};
+
+// ------------------------------------------------------------ reductions
+struct OpSum { __device__ __forceinline__ float operator()(float a, float b) const { return a + b; } };
+struct OpMax { __device__ __forceinline__ float operator()(float a, float b) const { return fmaxf(a, b); } };
+struct OpMin { __device__ __forceinline__ float operator()(float a, float b) const { return fminf(a, b); } };
+
+__device__ __forceinline__ unsigned cluster_ctarank() {
+  unsigned r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float ld_dsmem(const float* local, unsigned rank) {
+  unsigned a = static_cast<unsigned>(__cvta_generic_to_shared(local)), ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
+  return v;
+}
+
+template <int TPC, int RPC, int CL>
+struct RowTeam {
+  static constexpr int BLOCK = TPC * RPC;
+  static constexpr int WPR = TPC >= 32 ? TPC / 32 : 1;   // warps per row team
+  static_assert(TPC >= 32 ? TPC % 32 == 0 : (32 % TPC == 0), "team size must tile a warp");
+  static_assert(BLOCK % 32 == 0 && BLOCK <= 1024, "bad block size");
+
+  // shared-memory floats needed by `reduce` for NR values in `passes` passes
+  __host__ __device__ static constexpr int smem_floats(int nr, int calls) {
+    return RPC * WPR * nr + (CL > 1 ? calls * RPC * nr : 0);
+  }
+
+  int t;            // thread index inside the team
+  int team;         // team index inside the CTA
+  int rank;         // CTA rank inside the cluster
+  long long row;    // local row index (may be >= rows for idle teams)
+  bool row_ok;
+
+  __device__ __forceinline__ RowTeam(long long rows, long long row_base) {
+    t = threadIdx.x % TPC;
+    team = threadIdx.x / TPC;
+    rank = CL > 1 ? static_cast<int>(cluster_ctarank()) : 0;
+    const long long cta_row0 = row_base + (long long)(blockIdx.x / CL) * RPC;
+    row = cta_row0 + team;
+    row_ok = row < rows;
+  }
+
+  // slot index of this thread's k-th slot
+  __device__ __forceinline__ long long slot(int k) const {
+    return (long long)(rank * TPC + t) + (long long)k * (TPC * CL);
+  }
+
+  // All-reduce NR values across the row team (all CTAs of the cluster).
+  // Every thread of the CTA must call this (idle teams pass neutral values).
+  // `smem` must hold smem_floats(NR, passes) floats; `pass` selects the
+  // cluster exchange area so consecutive passes never overwrite a value a
+  // peer CTA may still be reading.
+  template <int NR, class Op>
+  __device__ __forceinline__ void reduce(float (&v)[NR], Op op, float* smem, int pass) const {
+    // 1) inside the warp (or the sub-warp team)
+    constexpr int W = TPC < 32 ? TPC : 32;
+#pragma unroll
+    for (int off = W / 2; off > 0; off >>= 1)
+#pragma unroll
+      for (int i = 0; i < NR; ++i) v[i] = op(v[i], __shfl_xor_sync(0xffffffffu, v[i], off));
+    // 2) across the warps of the team
+    if constexpr (WPR > 1) {
+      const int warp = t / 32, lane = t % 32;
+      float* red = smem + team * WPR * NR;
+      if (lane == 0) {
+#pragma unroll
+        for (int i = 0; i < NR; ++i) red[warp * NR + i] = v[i];
+      }
+      __syncthreads();
+#pragma unroll
+      for (int i = 0; i < NR; ++i) {
+        float a = red[i];
+#pragma unroll
+        for (int w = 1; w < WPR; ++w) a = op(a, red[w * NR + i]);
+        v[i] = a;
+      }
+      __syncthreads();   // the area is reused by the next pass
+    }
+    // 3) across the CTAs of the cluster
+    if constexpr (CL > 1) {
+      float* part = smem + RPC * WPR * NR + pass * RPC * NR + team * NR;
+      if (t == 0) {
+#pragma unroll
+        for (int i = 0; i < NR; ++i) part[i] = v[i];
+      }
+      cluster_arrive();
+      cluster_wait();
+#pragma unroll
+      for (int i = 0; i < NR; ++i) {
+        float a = ld_dsmem(part + i, 0);
+#pragma unroll
+        for (int r = 1; r < CL; ++r) a = op(a, ld_dsmem(part + i, r));
+        v[i] = a;
+      }
+    }
+  }
+
+  // A CTA of a cluster must not exit while a peer may still read its shared
+  // memory: call once after the last `reduce`, before leaving the kernel.
+  __device__ __forceinline__ void cluster_done_arrive() const {
+    if constexpr (CL > 1) cluster_arrive();
+  }
+  __device__ __forceinline__ void cluster_done_wait() const {
+    if constexpr (CL > 1) cluster_wait();
+  }
+};
+
+}  // namespace molten

@@ -1,0 +1,489 @@
+"""CUDA C++ emission for the row and elementwise families.
+
+Each sub-kernel becomes one ``extern "C" __global__`` function built on
+``molten/row_engine.cuh``.  Shapes (cols), dtypes, the op DAG, constants and
+the launch geometry are baked in as constexpr; rows and pointers are runtime
+kernel arguments (``molten::RowArgs``).
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+from .lowering import DTYPE_CTYPE, LoweringError, SubKernel, Value
+from .plan import pass_closures
+
+
+def c_float(x: float) -> str:
+    """Exact fp32 literal for x (rounded to fp32 first)."""
+    f = float(np.float32(x))
+    if math.isnan(f):
+        return "NAN"
+    if math.isinf(f):
+        return "INFINITY" if f > 0 else "(-INFINITY)"
+    if f == 0.0:
+        return "-0.0f" if math.copysign(1.0, f) < 0 else "0.0f"
+    if f == int(f) and abs(f) < 1e7:
+        return f"{int(f)}.0f"
+    return f"{f.hex()}f /* {f!r} */"
+
+
+def value_expr(v: Value, a, precise: bool) -> str:
+    """C expression for value v given the spelled arguments a."""
+    P = "true" if precise else "false"
+    op = v.op
+    if op == "add":
+        return f"({a[0]} + {a[1]})"
+    if op == "sub":
+        return f"({a[0]} - {a[1]})"
+    if op == "mul":
+        return f"({a[0]} * {a[1]})"
+    if op == "div":
+        return f"({a[0]} / {a[1]})" if precise else f"__fdividef({a[0]}, {a[1]})"
+    if op == "rcp":
+        return f"(1.0f / {a[0]})"
+    if op == "neg":
+        return f"(-{a[0]})"
+    if op == "sqrt":
+        return f"sqrtf({a[0]})"
+    if op == "rsqrt":
+        return f"rsqrtf({a[0]})"
+    if op == "exp":
+        return f"expf({a[0]})" if precise else f"__expf({a[0]})"
+    if op == "log":
+        return f"logf({a[0]})" if precise else f"__logf({a[0]})"
+    if op == "tanh":
+        return f"tanhf({a[0]})" if precise else f"m_tanh<false>({a[0]})"
+    if op == "sigmoid":
+        return f"m_sigmoid<{P}>({a[0]})"
+    if op == "silu":
+        return f"m_silu<{P}>({a[0]})"
+    if op == "gelu":
+        return f"m_gelu_tanh<{P}>({a[0]})"
+    if op == "relu":
+        return f"fmaxf({a[0]}, 0.0f)"
+    if op == "abs":
+        return f"fabsf({a[0]})"
+    if op == "clamp":
+        e = a[0]
+        lo, hi = v.attrs.get("min"), v.attrs.get("max")
+        if lo is not None:
+            e = f"fmaxf({e}, {c_float(lo)})"
+        if hi is not None:
+            e = f"fminf({e}, {c_float(hi)})"
+        return e
+    raise LoweringError(f"no expression for {op}")
+
+
+_RED_INIT = {"rsum": "0.0f", "rmax": "(-INFINITY)", "rmin": "INFINITY"}
+_RED_OP = {"rsum": "OpSum", "rmax": "OpMax", "rmin": "OpMin"}
+_RED_COMBINE = {"rsum": "{a} += {x};", "rmax": "{a} = fmaxf({a}, {x});",
+                "rmin": "{a} = fminf({a}, {x});"}
+_LOAD_HINT = {True: "kLoadStream", False: "kLoadDefault"}
+
+
+def _ctype(dtype: str) -> str:
+    return DTYPE_CTYPE[dtype]
+
+
+def _row_index_expr(opd, local: str, glob: str) -> str:
+    if opd.row_map == "full":
+        return local
+    if opd.row_map == "zero":
+        return "0LL"
+    terms = []
+    for div, mod, stride in opd.row_terms:
+        t = glob if div == 1 else f"({glob} / {div}LL)"
+        t = f"({t} % {mod}LL)"
+        if stride != 1:
+            t = f"{t} * {stride}LL"
+        terms.append(t)
+    return "(" + " + ".join(terms) + ")" if terms else "0LL"
+
+
+def _mask_period(v: Value, cols: int) -> int:
+    p = v.attrs.get("period")
+    return int(p) if p else int(cols)
+
+
+class _Emitter:
+    def __init__(self, sk: SubKernel, name: str):
+        self.sk = sk
+        self.name = name
+        self.values = sk.values
+        self.cfg = sk.config
+        self.needed = set(self.cfg["needed"])
+        self.lines = []
+
+    def w(self, s=""):
+        self.lines.append(s)
+
+    # --------------------------------------------------------- leaf spelling
+    def leaf(self, vid: int, in_loop: bool, prefetched: set, mat_ready: set,
+             loaded_now: set) -> str:
+        v = self.values[vid]
+        if v.kind == "const" and v.op == "const":
+            return c_float(v.attrs["value"])
+        if v.kind in ("row", "const"):
+            return f"v{vid}"
+        if vid in mat_ready:
+            return f"m{vid}[k][e]"
+        if v.op == "load":
+            i = v.attrs["operand"]
+            if i in prefetched:
+                return f"to_f32(s{i}[k].v[e])"
+            return f"to_f32(sl{i}.v[e])"
+        if v.op == "acc":
+            return "acc[e]"
+        return f"v{vid}"
+
+    def elem_statements(self, targets, prefetched, mat_ready, indent):
+        """Emit statements for the elem values in ``targets`` (closure),
+        in topological order, inside the (k, e) loop."""
+        out = []
+        for vid in sorted(targets):
+            v = self.values[vid]
+            if v.kind != "elem" or vid in mat_ready:
+                continue
+            if v.op in ("load", "acc"):
+                continue
+            if v.op == "mask":
+                period = _mask_period(v, self.sk.cols)
+                out.append(f"{indent}const float v{vid} = (col > mlim{vid}) ? (-INFINITY) : 0.0f;")
+                continue
+            args = [self.leaf(a, True, prefetched, mat_ready, set()) for a in v.args]
+            out.append(f"{indent}const float v{vid} = {value_expr(v, args, self.sk.precise)};")
+        return out
+
+    def row_statement(self, vid, prefetched) -> str:
+        # once per row: always the precise form
+        v = self.values[vid]
+        args = [self.leaf(a, False, prefetched, set(), set()) for a in v.args]
+        return f"const float v{vid} = {value_expr(v, args, True)};"
+
+    def header(self, kind: str):
+        sk = self.sk
+        ops = " -> ".join(v for v in self.cfg.get("op_names", []))
+        self.w(f"// Molten sm_100a {kind} kernel: {self.name}")
+        if ops:
+            self.w(f"// Fused ops: {ops}")
+        self.w(f"// cols = {sk.cols}; inputs: " + ", ".join(
+            f"{o.name}[{o.dtype} {o.last}/{o.row_map}]" for o in sk.operands))
+        self.w("#include \"molten/row_engine.cuh\"")
+        self.w("")
+
+    def pointers(self, lrow: str, grow: str, ok: str, vec_slots: bool = True):
+        sk = self.sk
+        for opd in sk.operands:
+            ct = _ctype(opd.dtype)
+            idx = _row_index_expr(opd, f"({ok} ? {lrow} : 0LL)", grow)
+            stride = "COLS" if opd.last == "vec" else "1LL"
+            self.w(f"  const {ct}* __restrict__ in{opd.index} = "
+                   f"static_cast<const {ct}*>(args.in[{opd.index}]) + {idx} * {stride};")
+        for out in sk.outputs:
+            ct = _ctype(out.dtype)
+            stride = "COLS" if out.kind == "full" else "1LL"
+            self.w(f"  {ct}* __restrict__ out{out.index} = "
+                   f"static_cast<{ct}*>(args.out[{out.index}]) + ({ok} ? {lrow} : 0LL) * {stride};")
+
+    def row_leaves(self, prefetched):
+        """Row-kind loads and mask limits (computed once per row)."""
+        sk = self.sk
+        for vid in sorted(self.needed):
+            v = self.values[vid]
+            if v.op == "load" and v.kind == "row":
+                i = v.attrs["operand"]
+                self.w(f"  const float v{vid} = rok ? load_scalar(in{i}) : 0.0f;")
+            if v.op == "mask":
+                period = _mask_period(v, sk.cols)
+                off = int(v.attrs.get("offset", 0))
+                self.w(f"  const long long mlim{vid} = (grow % {period}LL) + ({off}LL);")
+
+
+def emit_row(sk: SubKernel, name: str) -> str:
+    e = _Emitter(sk, name)
+    cfg = sk.config
+    VEC, NV, TPC, RPC, CL = cfg["vec"], cfg["nv"], cfg["tpc"], cfg["rpc"], cfg["cl"]
+    prefetch = set(cfg["prefetch"])
+    materialize = {int(v): int(p) for v, p in cfg["materialize"]}
+    values = sk.values
+    needed = e.needed
+    closures = pass_closures(values, sk, needed, materialize)
+    # reductions per pass, in id order
+    reds = {p: [] for p in range(sk.passes)}
+    for vid in sorted(needed):
+        v = values[vid]
+        if v.op in ("rsum", "rmax", "rmin"):
+            reds[v.avail - 1].append(vid)
+    # one exchange area per reduce call
+    n_calls = sum(len({values[r].op for r in rs}) for rs in reds.values())
+    max_nr = max([len(rs) for rs in reds.values()], default=1) or 1
+
+    e.header("row")
+    e.w("using namespace molten;")
+    e.w("")
+    e.w(f"extern \"C\" __global__ void __launch_bounds__({TPC * RPC}) "
+        f"{name}(const __grid_constant__ RowArgs args) {{")
+    e.w(f"  constexpr int VEC = {VEC}, NV = {NV}, TPC = {TPC}, RPC = {RPC}, CL = {CL};")
+    e.w(f"  constexpr long long COLS = {sk.cols}LL, NVEC = {cfg['nvec']}LL;")
+    e.w("  typedef RowTeam<TPC, RPC, CL> Team;")
+    e.w(f"  __shared__ float red_smem[Team::smem_floats({max_nr}, {max(n_calls, 1)}) > 0 ? "
+        f"Team::smem_floats({max_nr}, {max(n_calls, 1)}) : 1];")
+    e.w("  const Team tm(args.rows, 0);")
+    e.w("  const long long lrow = tm.row;")
+    e.w("  const long long grow = args.row_offset + lrow;")
+    e.w("  const bool rok = tm.row_ok;")
+    e.w("  (void)grow;")
+    e.pointers("lrow", "grow", "rok")
+    e.row_leaves(prefetch)
+    # row-level values available from the start
+    emitted_rows = set()
+
+    def emit_rows_at(p):
+        for vid in sorted(needed):
+            v = values[vid]
+            if v.kind in ("row", "const") and v.avail == p and vid not in emitted_rows \
+                    and v.op not in ("load", "const", "rsum", "rmax", "rmin"):
+                e.w("  " + e.row_statement(vid, prefetch))
+                emitted_rows.add(vid)
+
+    emit_rows_at(0)
+    # prefetch the row-streamed operands
+    for opd in sk.operands:
+        if opd.index in prefetch:
+            ct = _ctype(opd.dtype)
+            e.w(f"  Slot<{ct}, VEC> s{opd.index}[NV];")
+    if prefetch:
+        e.w("#pragma unroll")
+        e.w("  for (int k = 0; k < NV; ++k) {")
+        e.w("    const long long j = tm.slot(k);")
+        e.w("    if (rok && j < NVEC) {")
+        for opd in sk.operands:
+            if opd.index in prefetch:
+                hint = _LOAD_HINT[opd.row_map == "full"]
+                e.w(f"      s{opd.index}[k] = load_slot<{hint}, {_ctype(opd.dtype)}, VEC>"
+                    f"(in{opd.index} + j * VEC);")
+        e.w("    }")
+        e.w("  }")
+    for vid in sorted(materialize):
+        e.w(f"  float m{vid}[NV][VEC];")
+    mat_ready = set()
+    call = 0
+    for p in range(sk.passes):
+        rs = reds[p]
+        e.w(f"  // ---- pass {p}: " + ", ".join(f"{values[r].op}(v{values[r].args[0]})" for r in rs))
+        for r in rs:
+            e.w(f"  float v{r} = {_RED_INIT[values[r].op]};")
+        targets = set(closures[p])
+        to_mat = {m for m, pm in materialize.items() if pm == p}
+        e.w("#pragma unroll")
+        e.w("  for (int k = 0; k < NV; ++k) {")
+        e.w("    const long long j = tm.slot(k);")
+        e.w("    if (!(rok && j < NVEC)) continue;")
+        _emit_nonprefetched_loads(e, targets, prefetch, "    ")
+        e.w("#pragma unroll")
+        e.w("    for (int e = 0; e < VEC; ++e) {")
+        if any(values[t].op == "mask" for t in targets):
+            e.w("      const long long col = j * VEC + e;")
+        for st in e.elem_statements(targets, prefetch, mat_ready, "      "):
+            e.w(st)
+        for m in sorted(to_mat):
+            e.w(f"      m{m}[k][e] = v{m};")
+        for r in rs:
+            x = e.leaf(values[r].args[0], True, prefetch, mat_ready, set())
+            e.w("      " + _RED_COMBINE[values[r].op].format(a=f"v{r}", x=x))
+        e.w("    }")
+        e.w("  }")
+        mat_ready |= to_mat
+        by_op = {}
+        for r in rs:
+            by_op.setdefault(values[r].op, []).append(r)
+        for op, group in by_op.items():
+            nr = len(group)
+            e.w("  {")
+            e.w(f"    float red[{nr}] = {{" + ", ".join(f"v{r}" for r in group) + "};")
+            e.w(f"    tm.reduce<{nr}>(red, {_RED_OP[op]}{{}}, red_smem, {call});")
+            for i, r in enumerate(group):
+                e.w(f"    v{r} = red[{i}];")
+            e.w("  }")
+            call += 1
+        emit_rows_at(p + 1)
+    e.w("  tm.cluster_done_arrive();")
+    # ---- final pass: outputs
+    fin = set(closures[sk.passes])
+    full_outs = [o for o in sk.outputs if o.kind == "full"]
+    if full_outs:
+        e.w("  // ---- final pass: outputs")
+        e.w("#pragma unroll")
+        e.w("  for (int k = 0; k < NV; ++k) {")
+        e.w("    const long long j = tm.slot(k);")
+        e.w("    if (!(rok && j < NVEC)) continue;")
+        _emit_nonprefetched_loads(e, fin, prefetch, "    ")
+        for o in full_outs:
+            e.w(f"    float f{o.index}[VEC];")
+        e.w("#pragma unroll")
+        e.w("    for (int e = 0; e < VEC; ++e) {")
+        if any(values[t].op == "mask" for t in fin):
+            e.w("      const long long col = j * VEC + e;")
+        for st in e.elem_statements(fin, prefetch, mat_ready, "      "):
+            e.w(st)
+        for o in full_outs:
+            src = e.leaf(sk.out_values[o.index], True, prefetch, mat_ready, set())
+            e.w(f"      f{o.index}[e] = {src};")
+        e.w("    }")
+        for o in full_outs:
+            ct = _ctype(o.dtype)
+            e.w(f"    Slot<{ct}, VEC> o{o.index}; pack_slot<{ct}, VEC>(o{o.index}, f{o.index});")
+            e.w(f"    store_slot<kStoreDefault, {ct}, VEC>(out{o.index} + j * VEC, o{o.index});")
+        e.w("  }")
+    for o in sk.outputs:
+        if o.kind == "row":
+            src = e.leaf(sk.out_values[o.index], False, prefetch, set(), set())
+            e.w(f"  if (rok && tm.t == 0 && tm.rank == 0) store_scalar(out{o.index}, {src});")
+    e.w("  tm.cluster_done_wait();")
+    e.w("}")
+    return "\n".join(e.lines) + "\n"
+
+
+def _emit_nonprefetched_loads(e: _Emitter, targets, prefetch, indent):
+    sk = e.sk
+    used = set()
+    for t in targets:
+        v = e.values[t]
+        if v.op == "load" and v.kind == "elem" and v.attrs["operand"] not in prefetch:
+            used.add(v.attrs["operand"])
+        for a in v.args:
+            va = e.values[a]
+            if va.op == "load" and va.kind == "elem" and va.attrs["operand"] not in prefetch:
+                used.add(va.attrs["operand"])
+    for i in sorted(used):
+        opd = sk.operands[i]
+        ct = _ctype(opd.dtype)
+        e.w(f"{indent}const Slot<{ct}, VEC> sl{i} = load_slot<kLoadDefault, {ct}, VEC>(in{i} + j * VEC);")
+
+
+def emit_ew(sk: SubKernel, name: str) -> str:
+    """Pure elementwise kernel: grid.x = column tiles, grid.y strides over
+    blocks of RPC * UPT rows; per-column operands are loaded once per thread
+    and reused for every row it visits."""
+    e = _Emitter(sk, name)
+    cfg = sk.config
+    VEC, NV, TPC, RPC, UPT = cfg["vec"], cfg["nv"], cfg["tpc"], cfg["rpc"], cfg["upt"]
+    values = sk.values
+    needed = e.needed
+    e.header("elementwise")
+    e.w("using namespace molten;")
+    e.w("")
+    e.w(f"extern \"C\" __global__ void __launch_bounds__({TPC * RPC}) "
+        f"{name}(const __grid_constant__ RowArgs args) {{")
+    e.w(f"  constexpr int VEC = {VEC}, NV = {NV}, TPC = {TPC}, RPC = {RPC}, UPT = {UPT};")
+    e.w(f"  constexpr long long COLS = {sk.cols}LL, NVEC = {cfg['nvec']}LL;")
+    e.w("  const int t = threadIdx.x % TPC, team = threadIdx.x / TPC;")
+    e.w("  const long long tile0 = (long long)blockIdx.x * (TPC * NV);")
+    # per-column operands: hoisted loads
+    col_ops = [o for o in sk.operands if o.last == "vec" and o.row_map == "zero"]
+    row_ops = [o for o in sk.operands if o.last == "vec" and o.row_map != "zero"]
+    bc_ops = [o for o in sk.operands if o.last == "bcast"]
+    for o in col_ops:
+        ct = _ctype(o.dtype)
+        e.w(f"  Slot<{ct}, VEC> c{o.index}[NV];")
+        e.w("#pragma unroll")
+        e.w("  for (int k = 0; k < NV; ++k) {")
+        e.w("    const long long j = tile0 + t + (long long)k * TPC;")
+        e.w(f"    if (j < NVEC) c{o.index}[k] = load_slot<kLoadDefault, {ct}, VEC>"
+            f"(static_cast<const {ct}*>(args.in[{o.index}]) + j * VEC);")
+        e.w("  }")
+    e.w("  for (long long rb = blockIdx.y; rb * (RPC * UPT) < args.rows; rb += gridDim.y) {")
+    # row loads for all UPT rows first
+    for o in row_ops:
+        ct = _ctype(o.dtype)
+        e.w(f"    Slot<{ct}, VEC> s{o.index}[UPT][NV];")
+    e.w("#pragma unroll")
+    e.w("    for (int u = 0; u < UPT; ++u) {")
+    e.w("      const long long lrow = rb * (RPC * UPT) + (long long)u * RPC + team;")
+    e.w("      const long long grow = args.row_offset + lrow;")
+    e.w("      (void)grow;")
+    e.w("      if (lrow >= args.rows) continue;")
+    e.w("#pragma unroll")
+    e.w("      for (int k = 0; k < NV; ++k) {")
+    e.w("        const long long j = tile0 + t + (long long)k * TPC;")
+    e.w("        if (j >= NVEC) continue;")
+    for o in row_ops:
+        ct = _ctype(o.dtype)
+        idx = _row_index_expr(o, "lrow", "grow")
+        hint = _LOAD_HINT[o.row_map == "full"]
+        e.w(f"        s{o.index}[u][k] = load_slot<{hint}, {ct}, VEC>(static_cast<const {ct}*>"
+            f"(args.in[{o.index}]) + {idx} * COLS + j * VEC);")
+    e.w("      }")
+    e.w("    }")
+    e.w("#pragma unroll")
+    e.w("    for (int u = 0; u < UPT; ++u) {")
+    e.w("      const long long lrow = rb * (RPC * UPT) + (long long)u * RPC + team;")
+    e.w("      const long long grow = args.row_offset + lrow;")
+    e.w("      (void)grow;")
+    e.w("      if (lrow >= args.rows) continue;")
+    for o in bc_ops:
+        ct = _ctype(o.dtype)
+        idx = _row_index_expr(o, "lrow", "grow")
+        for vid in sorted(needed):
+            v = values[vid]
+            if v.op == "load" and v.attrs["operand"] == o.index:
+                e.w(f"      const float v{vid} = load_scalar(static_cast<const {ct}*>"
+                    f"(args.in[{o.index}]) + {idx});")
+    for vid in sorted(needed):
+        v = values[vid]
+        if v.op == "mask":
+            period = _mask_period(v, sk.cols)
+            off = int(v.attrs.get("offset", 0))
+            e.w(f"      const long long mlim{vid} = (grow % {period}LL) + ({off}LL);")
+    for vid in sorted(needed):
+        v = values[vid]
+        if v.kind in ("row", "const") and v.op not in ("load", "const"):
+            args = [_ew_leaf(e, a) for a in v.args]
+            e.w(f"      const float v{vid} = {value_expr(v, args, True)};")
+    e.w("#pragma unroll")
+    e.w("      for (int k = 0; k < NV; ++k) {")
+    e.w("        const long long j = tile0 + t + (long long)k * TPC;")
+    e.w("        if (j >= NVEC) continue;")
+    for o in sk.outputs:
+        e.w(f"        float f{o.index}[VEC];")
+    e.w("#pragma unroll")
+    e.w("        for (int e = 0; e < VEC; ++e) {")
+    if any(values[t].op == "mask" for t in needed):
+        e.w("          const long long col = j * VEC + e;")
+    for vid in sorted(needed):
+        v = values[vid]
+        if v.kind != "elem" or v.op in ("load",):
+            continue
+        if v.op == "mask":
+            e.w(f"          const float v{vid} = (col > mlim{vid}) ? (-INFINITY) : 0.0f;")
+            continue
+        args = [_ew_leaf(e, a) for a in v.args]
+        e.w(f"          const float v{vid} = {value_expr(v, args, sk.precise)};")
+    for o in sk.outputs:
+        e.w(f"          f{o.index}[e] = {_ew_leaf(e, sk.out_values[o.index])};")
+    e.w("        }")
+    for o in sk.outputs:
+        ct = _ctype(o.dtype)
+        e.w(f"        Slot<{ct}, VEC> o{o.index}; pack_slot<{ct}, VEC>(o{o.index}, f{o.index});")
+        e.w(f"        store_slot<kStoreDefault, {ct}, VEC>(static_cast<{ct}*>(args.out[{o.index}]) "
+            f"+ lrow * COLS + j * VEC, o{o.index});")
+    e.w("      }")
+    e.w("    }")
+    e.w("  }")
+    e.w("}")
+    return "\n".join(e.lines) + "\n"
+
+
+def _ew_leaf(e: _Emitter, vid: int) -> str:
+    v = e.values[vid]
+    if v.kind == "const" and v.op == "const":
+        return c_float(v.attrs["value"])
+    if v.op == "load" and v.kind == "elem":
+        o = e.sk.operands[v.attrs["operand"]]
+        if o.row_map == "zero":
+            return f"to_f32(c{o.index}[k].v[e])"
+        return f"to_f32(s{o.index}[u][k].v[e])"
+    return f"v{vid}"

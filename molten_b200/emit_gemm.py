@@ -1,0 +1,121 @@
+"""CUDA emission for the MATMUL + elementwise-epilogue family.
+
+The emitted module instantiates the tcgen05 engine of
+``molten/gemm_sm100.cuh`` with a generated epilogue functor: the epilogue
+warps read 32 fp32 accumulator columns of one output row from TMEM, and the
+functor applies the fused ops (bias add, GELU, ...) in fp32, rounds once and
+stores 16 bytes at a time.
+"""
+
+from __future__ import annotations
+
+from .emit import _mask_period, _row_index_expr, c_float, value_expr
+from .lowering import DTYPE_CTYPE, LoweringError, SubKernel
+
+
+def emit_gemm(sk: SubKernel, name: str) -> str:
+    cfg = sk.config
+    BM, BN, BK, ST = cfg["bm"], cfg["bn"], cfg["bk"], cfg["stages"]
+    a = sk.operands[sk.a_operand]
+    f16in = "true" if a.dtype == "float16" else "false"
+    values = sk.values
+    needed = set(cfg["needed"])
+    L = []
+    w = L.append
+    w(f"// Molten sm_100a tcgen05 GEMM + epilogue: {name}")
+    w(f"// C[{sk.m}, {sk.n}] = epilogue(A[{sk.m}, {sk.k}] @ B[{sk.k}, {sk.n}]); "
+      f"tile {BM}x{BN}x{BK}, {ST} stages")
+    w("#include \"molten/gemm_sm100.cuh\"")
+    w("")
+    w("using namespace molten;")
+    w("")
+    w("namespace {")
+    w(f"constexpr int TILE_M = {BM}, TILE_N = {BN}, TILE_K = {BK}, STAGES = {ST};")
+    w(f"typedef GemmLayout<TILE_M, TILE_N, TILE_K, STAGES> Layout_{name};")
+    w(f"struct Epilogue_{name} {{")
+    w("  // C[row, col0 .. col0 + 31] from the fp32 accumulators of one TMEM row")
+    w("  __device__ __forceinline__ static void apply(const GemmArgs& args, long long row,")
+    w("                                               long long col0, const float (&acc)[32]) {")
+    w(f"    constexpr long long N = {sk.n}LL;")
+    w("    if (row >= args.m) return;")
+    w("    const long long grow = args.row_offset + row;")
+    w("    (void)grow;")
+    # row-level leaves
+    for vid in sorted(needed):
+        v = values[vid]
+        if v.op == "load" and v.kind == "row":
+            o = sk.operands[v.attrs["operand"]]
+            ct = DTYPE_CTYPE[o.dtype]
+            idx = _row_index_expr(o, "row", "grow")
+            w(f"    const float v{vid} = load_scalar(static_cast<const {ct}*>(args.in[{o.index}]) + {idx});")
+        if v.op == "mask":
+            period = _mask_period(v, sk.n)
+            off = int(v.attrs.get("offset", 0))
+            w(f"    const long long mlim{vid} = (grow % {period}LL) + ({off}LL);")
+    for vid in sorted(needed):
+        v = values[vid]
+        if v.kind in ("row", "const") and v.op not in ("load", "const"):
+            args = [_leaf(sk, x) for x in v.args]
+            w(f"    const float v{vid} = {value_expr(v, args, True)};")
+    w("#pragma unroll")
+    w("    for (int q = 0; q < 4; ++q) {")
+    w("      const long long c = col0 + 8 * q;")
+    w("      if (c >= N) break;")
+    vec_ops = sorted({values[v].attrs["operand"] for v in needed
+                      if values[v].op == "load" and values[v].kind == "elem"})
+    for i in vec_ops:
+        o = sk.operands[i]
+        ct = DTYPE_CTYPE[o.dtype]
+        idx = _row_index_expr(o, "row", "grow")
+        w(f"      const Slot<{ct}, 8> sl{i} = load_slot<kLoadDefault, {ct}, 8>("
+          f"static_cast<const {ct}*>(args.in[{i}]) + {idx} * N + c);")
+    for o in sk.outputs:
+        w(f"      float f{o.index}[8];")
+    w("#pragma unroll")
+    w("      for (int e = 0; e < 8; ++e) {")
+    if any(values[v].op == "mask" for v in needed):
+        w("        const long long col = c + e;")
+    for vid in sorted(needed):
+        v = values[vid]
+        if v.kind != "elem" or v.op in ("load", "acc"):
+            continue
+        if v.op == "mask":
+            w(f"        const float v{vid} = (col > mlim{vid}) ? (-INFINITY) : 0.0f;")
+            continue
+        args = [_leaf(sk, x) for x in v.args]
+        w(f"        const float v{vid} = {value_expr(v, args, sk.precise)};")
+    for o in sk.outputs:
+        w(f"        f{o.index}[e] = {_leaf(sk, sk.out_values[o.index])};")
+    w("      }")
+    for o in sk.outputs:
+        ct = DTYPE_CTYPE[o.dtype]
+        w(f"      Slot<{ct}, 8> o{o.index}; pack_slot<{ct}, 8>(o{o.index}, f{o.index});")
+        w(f"      store_slot<kStoreDefault, {ct}, 8>(static_cast<{ct}*>(args.out[{o.index}]) "
+          f"+ row * N + c, o{o.index});")
+    w("    }")
+    w("  }")
+    w("};")
+    w("}  // namespace")
+    w("")
+    w(f"extern \"C\" __global__ void __launch_bounds__(256, 1) "
+      f"{name}(const __grid_constant__ GemmArgs args) {{")
+    w("  extern __shared__ __align__(1024) uint8_t smem_raw[];")
+    w(f"  const GemmShared sh = gemm_carve<Layout_{name}>(smem_raw);")
+    w(f"  gemm_init<Layout_{name}>(sh, args);     // mbarriers + TMEM allocation")
+    w("  __syncthreads();")
+    w(f"  gemm_roles<Layout_{name}, {f16in}, Epilogue_{name}>(sh, args);")
+    w("  __syncthreads();")
+    w(f"  gemm_teardown<Layout_{name}>(sh);       // TMEM release")
+    w("}")
+    return "\n".join(L) + "\n"
+
+
+def _leaf(sk: SubKernel, vid: int) -> str:
+    v = sk.values[vid]
+    if v.op == "const" and v.kind == "const":
+        return c_float(v.attrs["value"])
+    if v.op == "acc":
+        return "acc[8 * q + e]"
+    if v.op == "load" and v.kind == "elem":
+        return f"to_f32(sl{v.attrs['operand']}.v[e])"
+    return f"v{vid}"

@@ -1,0 +1,39 @@
+"""Tile / pipeline configuration of the tcgen05 GEMM + epilogue kernel."""
+
+from __future__ import annotations
+
+NUM_SMS_B200 = 148
+
+
+def choose_gemm_config(sk, override: dict) -> dict:
+    """Pick the CTA tile for C[M, N] = A[M, K] @ B[K, N] (+ epilogue).
+
+    One CTA owns a BM x BN output tile with its fp32 accumulator in TMEM;
+    BK = 64 bf16 = one 128-byte swizzle row.  BN is chosen to balance the
+    persistent tile loop over the SMs.
+    """
+    o = dict(override or {})
+    M, N, K = sk.m, sk.n, sk.k
+    bm = o.get("bm", 128)
+    bk = o.get("bk", 64)
+    if "bn" in o:
+        bn = o["bn"]
+    else:
+        best = None
+        for cand in (256, 192, 128, 64):
+            if N % cand and cand != 64:
+                continue
+            tiles = -(-M // bm) * -(-N // cand)
+            waves = -(-tiles // NUM_SMS_B200)
+            eff = tiles / (waves * NUM_SMS_B200)
+            key = (-(eff * cand / 256 ** 0.25), -cand)
+            if best is None or key < best[0]:
+                best = (key, cand)
+        bn = best[1]
+    stage_bytes = (bm * bk + bk * bn) * 2
+    stages = o.get("stages") or max(2, min(8, (200 * 1024) // stage_bytes))
+    smem = stages * stage_bytes + (2 * stages + 5) * 8 + 16 + 1024
+    if smem > 232448:
+        raise ValueError(f"GEMM tile needs {smem} bytes of shared memory")
+    return {"bm": bm, "bn": bn, "bk": bk, "stages": stages,
+            "epi_warps": 4, "threads": 256, "smem_bytes": smem}

@@ -1,0 +1,517 @@
+"""Lowering of one fusion group to kernel plans.
+
+A fusion group (``fusion.py``) is lowered for one concrete specialisation
+(shapes and dtypes of its external inputs) into one or more *sub-kernels*:
+
+* ``row``  -- row patterns with last-dim reductions (RMSNorm, RMSNorm*SiLU,
+  softmax, any reduction + elementwise DAG).  A row is register-resident.
+* ``ew``   -- pure elementwise DAGs with numpy broadcasting of per-column,
+  per-row and scalar operands (the N-op chains).
+* ``gemm`` -- MATMUL followed by an elementwise epilogue (bias, GELU ...).
+
+A group that cannot run as one kernel (a MATMUL whose result feeds a row
+reduction, or elementwise ops feeding a MATMUL) is split into consecutive
+sub-kernels whose intermediates the runtime allocates.
+
+Semantics follow the reference's CPU definitions (``benchmarks/ops.py``):
+RMS(x) = sqrt(mean(x^2, -1) + eps) (``ops.py:15``), softmax over the last
+dim (``ops.py:45-47``), tanh-form GELU (``ops.py:52``, ``codegen.py:63``),
+SiLU(g) = g * sigmoid(g) (``ops.py:19-21``).  All arithmetic is fp32; inputs
+are widened exactly and outputs are rounded once (round to nearest even).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Optional
+
+from .ir import DataflowGraph, OpType, ELEMENTWISE_OPS, REDUCTION_OPS
+
+
+class LoweringError(NotImplementedError):
+    """The group (or this specialisation of it) has no sm_100a lowering."""
+
+
+# ------------------------------------------------------------------- dtypes
+_DTYPE_ALIASES = {
+    "float32": "float32", "float": "float32", "fp32": "float32", "f32": "float32",
+    "bfloat16": "bfloat16", "bf16": "bfloat16",
+    "float16": "float16", "half": "float16", "fp16": "float16", "f16": "float16",
+}
+DTYPE_SIZE = {"float32": 4, "bfloat16": 2, "float16": 2}
+DTYPE_CTYPE = {"float32": "float", "bfloat16": "bf16", "float16": "f16"}
+
+
+def canon_dtype(d) -> str:
+    s = str(d).replace("torch.", "")
+    if s not in _DTYPE_ALIASES:
+        raise LoweringError(f"unsupported dtype {d!r} (float32, bfloat16, float16)")
+    return _DTYPE_ALIASES[s]
+
+
+def promote(dtypes) -> str:
+    """torch-style promotion among the three float types."""
+    ds = set(dtypes)
+    if not ds:
+        return "float32"
+    if len(ds) == 1:
+        return ds.pop()
+    return "float32"
+
+
+# ------------------------------------------------------------------- shapes
+def broadcast_shapes(a: tuple, b: tuple) -> tuple:
+    n = max(len(a), len(b))
+    a = (1,) * (n - len(a)) + tuple(a)
+    b = (1,) * (n - len(b)) + tuple(b)
+    out = []
+    for x, y in zip(a, b):
+        if x == y or y == 1:
+            out.append(x)
+        elif x == 1:
+            out.append(y)
+        else:
+            raise LoweringError(f"shapes {a} and {b} do not broadcast")
+    return tuple(out)
+
+
+def prod(xs) -> int:
+    p = 1
+    for x in xs:
+        p *= int(x)
+    return p
+
+
+def is_mask_const(op) -> bool:
+    return op.op_type == OpType.CONSTANT and op.attrs.get("kind") == "causal_mask"
+
+
+def _reduces_last_dim(op, ndim: int) -> bool:
+    d = op.reduction_dim
+    return d is None or d == -1 or (ndim > 0 and d == ndim - 1)
+
+
+def infer_shapes(graph: DataflowGraph, op_ids, known: dict) -> dict:
+    """Concrete shape of every op in ``op_ids`` (topological order) given
+    the shapes in ``known`` (external inputs).  Reductions keep the reduced
+    dim as size 1, like ``mean(-1, keepdim=True)`` in ``ops.py:15``."""
+    shapes = dict(known)
+    for oid in op_ids:
+        op = graph.ops[oid]
+        ins = [shapes[i] for i in op.inputs]
+        t = op.op_type
+        if t in ELEMENTWISE_OPS:
+            s = ()
+            for x in ins:
+                s = broadcast_shapes(s, x)
+        elif t == OpType.SOFTMAX:
+            s = ins[0]
+            if not _reduces_last_dim(op, len(s)):
+                raise LoweringError("softmax only over the last dim")
+        elif t in REDUCTION_OPS:
+            s = ins[0]
+            if not _reduces_last_dim(op, len(s)):
+                raise LoweringError(f"{t.name} only over the last dim")
+            s = tuple(s[:-1]) + (1,) if len(s) else (1,)
+        elif t == OpType.MATMUL:
+            a, b = ins
+            if len(b) != 2 or len(a) < 2:
+                raise LoweringError("MATMUL needs A [..., M, K] and a 2-D B [K, N]")
+            if a[-1] != b[0]:
+                raise LoweringError(f"MATMUL inner dims differ: {a} @ {b}")
+            s = tuple(a[:-1]) + (b[1],)
+        else:
+            raise LoweringError(f"{t.name} has no sm_100a lowering")
+        shapes[oid] = tuple(int(d) for d in s)
+    return shapes
+
+
+# ----------------------------------------------------------- plan objects
+@dataclass
+class Operand:
+    """An external input of a sub-kernel."""
+    index: int            # position in the kernel's input pointer array
+    op_id: int            # graph op (or sub-kernel value) providing it
+    name: str
+    dtype: str
+    shape: tuple
+    last: str             # "vec": varies along columns; "bcast": size 1 there
+    row_map: str          # "full", "zero" or "general"
+    row_terms: tuple = () # general: ((div, mod, stride), ...) over global row
+
+
+@dataclass
+class OutputSpec:
+    index: int
+    op_id: int
+    dtype: str
+    shape: tuple
+    kind: str             # "full" (rows x cols) or "row" (one value per row)
+
+
+@dataclass
+class Value:
+    """Node of a per-row expression DAG."""
+    id: int
+    kind: str             # "const" | "row" | "elem"
+    op: str
+    args: tuple = ()
+    attrs: dict = field(default_factory=dict)
+    avail: int = 0        # first pass in which the value can be computed
+
+
+@dataclass
+class SubKernel:
+    family: str           # "row" | "ew" | "gemm"
+    op_ids: list          # graph ops computed here (topological order)
+    operands: list        # [Operand]
+    outputs: list         # [OutputSpec]
+    rows: int = 1
+    cols: int = 1
+    values: list = field(default_factory=list)      # [Value] (topological)
+    out_values: list = field(default_factory=list)  # value id per output
+    passes: int = 0
+    precise: bool = True
+    config: dict = field(default_factory=dict)
+    # gemm only
+    m: int = 0
+    n: int = 0
+    k: int = 0
+    a_operand: Optional[int] = None
+    b_operand: Optional[int] = None
+
+
+@dataclass
+class GroupPlan:
+    name: str
+    inputs: list          # graph op ids the caller passes, in order
+    input_dtypes: list
+    input_shapes: list
+    outputs: list         # graph op ids returned, in order
+    output_dtypes: list
+    output_shapes: list
+    kernels: list         # [SubKernel]
+    temps: dict           # op id -> (shape, dtype) of intermediates
+
+
+# ------------------------------------------------------------ group split
+def group_topo(graph: DataflowGraph, op_ids) -> list:
+    members = set(op_ids)
+    return [i for i in graph.topological_order() if i in members]
+
+
+def _deps_within(graph, root, members) -> set:
+    out, stack = set(), [root]
+    while stack:
+        cur = stack.pop()
+        for i in graph.ops[cur].inputs:
+            if i in members and i not in out:
+                out.add(i)
+                stack.append(i)
+    return out
+
+
+def group_boundary(graph: DataflowGraph, op_ids):
+    """(external inputs, outputs, live ops) of a group.
+
+    Outputs are members consumed by an OUTPUT op or by an op outside the
+    group; with none of those, the group's sinks (ops nobody consumes) are the
+    outputs, which matches the reference emitting the last op's value.  Ops no
+    output depends on (e.g. left behind by identity elimination) are dropped.
+    """
+    members = set(op_ids)
+    consumers = {i: [] for i in members}
+    for oid, op in graph.ops.items():
+        for i in op.inputs:
+            if i in consumers:
+                consumers[i].append(oid)
+    outs = [i for i in group_topo(graph, op_ids)
+            if any(c not in members or graph.ops[c].op_type == OpType.OUTPUT
+                   for c in consumers[i])]
+    if not outs:
+        outs = [i for i in group_topo(graph, op_ids) if not consumers[i]]
+    live = set(outs)
+    for o in outs:
+        live |= _deps_within(graph, o, members)
+    ordered = [i for i in group_topo(graph, op_ids) if i in live]
+    ext = []
+    for i in ordered:
+        for j in graph.ops[i].inputs:
+            if j not in members and j not in ext:
+                ext.append(j)
+    ext.sort()
+    return ext, outs, ordered
+
+
+def split_group(graph: DataflowGraph, ordered: list) -> list:
+    """Split a group's live ops into (family, ops) sub-kernels."""
+    mm = [i for i in ordered if graph.ops[i].op_type == OpType.MATMUL]
+    if not mm:
+        fam = "row" if any(graph.is_reduction(i) for i in ordered) else "ew"
+        return [(fam, list(ordered))]
+    m = mm[0]
+    members = set(ordered)
+    pre_set = _deps_within(graph, m, members)
+    pre = [i for i in ordered if i in pre_set]
+    post = [i for i in ordered if i not in pre_set and i != m]
+    post_set = set(post)
+    epi, rest = [m], []
+    epi_set = {m}
+    for i in post:
+        op = graph.ops[i]
+        depends = any(j in epi_set for j in op.inputs)
+        ok_inputs = all(j in epi_set or j not in post_set for j in op.inputs)
+        if graph.is_elementwise(i) and depends and ok_inputs:
+            epi.append(i)
+            epi_set.add(i)
+        else:
+            rest.append(i)
+    out = []
+    if pre:
+        out.append(("row" if any(graph.is_reduction(i) for i in pre) else "ew", pre))
+    out.append(("gemm", epi))
+    if rest:
+        out.append(("row" if any(graph.is_reduction(i) for i in rest) else "ew", rest))
+    return out
+
+
+# ------------------------------------------------------- operand analysis
+def classify_operand(shape: tuple, it_shape: tuple):
+    """(last, row_map, row_terms) of an operand broadcast to ``it_shape``."""
+    n = len(it_shape)
+    if len(shape) > n:
+        raise LoweringError(f"operand {shape} has more dims than {it_shape}")
+    s = (1,) * (n - len(shape)) + tuple(shape)
+    cols = it_shape[-1] if n else 1
+    last_dim = s[-1] if n else 1
+    if last_dim == cols:
+        last = "vec"
+    elif last_dim == 1:
+        last = "bcast"
+    else:
+        raise LoweringError(f"operand {shape} does not broadcast to {it_shape}")
+    lead_it, lead_op = it_shape[:-1], s[:-1]
+    if tuple(lead_op) == tuple(lead_it):
+        return last, "full", ()
+    if all(d == 1 for d in lead_op):
+        return last, "zero", ()
+    terms = []
+    for d in range(len(lead_it)):
+        if lead_op[d] == 1:
+            continue
+        if lead_op[d] != lead_it[d]:
+            raise LoweringError(f"operand {shape} does not broadcast to {it_shape}")
+        div = prod(lead_it[d + 1:])
+        stride = prod(lead_op[d + 1:])
+        terms.append((div, int(lead_it[d]), stride))
+    return last, "general", tuple(terms)
+
+
+_UNARY = {
+    OpType.NEG: "neg", OpType.SQRT: "sqrt", OpType.RSQRT: "rsqrt",
+    OpType.EXP: "exp", OpType.LOG: "log", OpType.TANH: "tanh",
+    OpType.SIGMOID: "sigmoid", OpType.GELU: "gelu", OpType.SILU: "silu",
+    OpType.RELU: "relu", OpType.ABS: "abs", OpType.CLAMP: "clamp",
+}
+_BINARY = {OpType.ADD: "add", OpType.SUB: "sub", OpType.MUL: "mul", OpType.DIV: "div"}
+_KIND_RANK = {"const": 0, "row": 1, "elem": 2}
+EXPENSIVE = {"exp", "log", "tanh", "sigmoid", "gelu", "silu", "sqrt", "rsqrt", "div"}
+
+
+class _DagBuilder:
+    def __init__(self, cols: int):
+        self.values: list = []
+        self.cols = cols
+        self._memo: dict = {}
+
+    def add(self, kind, op, args=(), attrs=None, avail=None) -> int:
+        attrs = attrs or {}
+        key = (op, tuple(args), tuple(sorted((k, repr(v)) for k, v in attrs.items())))
+        if op not in ("load",) and key in self._memo:
+            return self._memo[key]
+        if avail is None:
+            avail = max([self.values[a].avail for a in args], default=0)
+        vid = len(self.values)
+        self.values.append(Value(vid, kind, op, tuple(args), attrs, avail))
+        self._memo[key] = vid
+        return vid
+
+    def kind_of(self, args) -> str:
+        return max((self.values[a].kind for a in args), key=_KIND_RANK.get, default="const")
+
+    def const(self, x: float) -> int:
+        return self.add("const", "const", (), {"value": float(x)})
+
+    def unary(self, op, a, attrs=None):
+        return self.add(self.kind_of([a]), op, (a,), attrs)
+
+    def binary(self, op, a, b):
+        return self.add(self.kind_of([a, b]), op, (a, b))
+
+    def reduce(self, op, a) -> int:
+        v = self.values[a]
+        if v.kind != "elem":
+            # reduction of a value constant along the row
+            if op == "rsum":
+                return self.binary("mul", a, self.const(self.cols))
+            return a
+        return self.add("row", op, (a,), avail=v.avail + 1)
+
+
+def build_dag(graph: DataflowGraph, op_ids: list, operands: list, cols: int,
+              acc_op: Optional[int] = None):
+    """Translate graph ops into a Value DAG.  Returns (values, env)."""
+    b = _DagBuilder(cols)
+    env: dict = {}
+    if acc_op is not None:
+        env[acc_op] = b.add("elem", "acc", ())
+    for opd in operands:
+        src = graph.ops.get(opd.op_id)
+        kind = "elem" if opd.last == "vec" else "row"
+        env[opd.op_id] = b.add(kind, "load", (), {"operand": opd.index})
+    for oid in op_ids:
+        op = graph.ops[oid]
+        for i in op.inputs:
+            if i in env:
+                continue
+            src = graph.ops[i]
+            if is_mask_const(src):
+                env[i] = b.add("elem", "mask", (), {"period": src.attrs.get("period"),
+                                                   "offset": int(src.attrs.get("offset", 0))})
+            elif src.op_type == OpType.CONSTANT:
+                env[i] = b.const(src.attrs.get("value", 0.0) or 0.0)
+            else:
+                raise LoweringError(f"operand op {i} of op {oid} is not available")
+        args = [env[i] for i in op.inputs]
+        t = op.op_type
+        if t in _BINARY:
+            if len(args) != 2:
+                raise LoweringError(f"{t.name} needs two inputs")
+            if t == OpType.DIV and b.values[args[1]].kind in ("row", "const") \
+                    and b.values[args[0]].kind == "elem":
+                # divide by a per-row scalar: one reciprocal per row
+                r = b.unary("rcp", args[1])
+                env[oid] = b.binary("mul", args[0], r)
+            else:
+                env[oid] = b.binary(_BINARY[t], *args)
+        elif t in _UNARY:
+            attrs = {}
+            if t == OpType.CLAMP:
+                attrs = {"min": op.attrs.get("min"), "max": op.attrs.get("max")}
+            env[oid] = b.unary(_UNARY[t], args[0], attrs)
+        elif t == OpType.SOFTMAX:
+            x = args[0]
+            mx = b.reduce("rmax", x)
+            e = b.unary("exp", b.binary("sub", x, mx))
+            s = b.reduce("rsum", e)
+            env[oid] = b.binary("mul", e, b.unary("rcp", s))
+        elif t == OpType.SUM:
+            env[oid] = b.reduce("rsum", args[0])
+        elif t == OpType.MEAN:
+            env[oid] = b.binary("div", b.reduce("rsum", args[0]), b.const(cols))
+        elif t == OpType.MAX:
+            env[oid] = b.reduce("rmax", args[0])
+        elif t == OpType.MIN:
+            env[oid] = b.reduce("rmin", args[0])
+        elif t == OpType.NORM:
+            x = args[0]
+            env[oid] = b.unary("sqrt", b.reduce("rsum", b.binary("mul", x, x)))
+        elif t == OpType.RMS:
+            x = args[0]
+            eps = float(op.attrs.get("eps", 1e-6))
+            ms = b.binary("div", b.reduce("rsum", b.binary("mul", x, x)), b.const(cols))
+            env[oid] = b.unary("sqrt", b.binary("add", ms, b.const(eps)))
+        else:
+            raise LoweringError(f"{t.name} has no sm_100a lowering")
+    return b.values, env
+
+
+# ------------------------------------------------------------ heuristics
+def _pick_vec(cols: int, sizes) -> int:
+    smallest = min(sizes) if sizes else 4
+    v = max(1, 16 // smallest)
+    while v > 1 and cols % v:
+        v //= 2
+    return v
+
+
+def _regs_per_slot(sk: SubKernel, vec: int, prefetch: set, materialize) -> int:
+    """Registers one slot costs while a row is resident: the compiler keeps
+    the widened fp32 copy of a prefetched 16-bit slot once it has been read,
+    so every resident element is counted as one fp32 register."""
+    r = vec * len([o for o in sk.operands if o.index in prefetch])
+    r += vec * len(materialize)
+    return max(r, 1)
+
+
+def choose_row_config(sk: SubKernel, prefetch: set, materialize: set,
+                      override: Optional[dict] = None) -> dict:
+    sizes = [DTYPE_SIZE[o.dtype] for o in sk.operands if o.last == "vec"]
+    sizes += [DTYPE_SIZE[o.dtype] for o in sk.outputs if o.kind == "full"]
+    o = dict(override or {})
+    vec = o.get("vec") or _pick_vec(sk.cols, sizes)
+    nvec = -(-sk.cols // vec)
+    per_slot = _regs_per_slot(sk, vec, prefetch, materialize)
+    budget = o.get("reg_budget", 64)
+    nv_max = max(1, budget // per_slot)
+    if "tpc" in o:
+        tpc, cl = o["tpc"], o.get("cl", 1)
+        team = tpc * cl
+    else:
+        need = -(-nvec // nv_max)
+        if need < 32:
+            team = 1
+            while team < need:
+                team *= 2
+        else:
+            lo = 32 * (-(-need // 32))
+            best = None
+            for cand in range(lo, 2 * lo + 1, 32):
+                nv = -(-nvec // cand)
+                waste = cand * nv - nvec
+                key = (waste, cand)
+                if best is None or key < best[0]:
+                    best = (key, cand)
+            team = best[1]
+        max_cta = o.get("max_tpc", 512)
+        cl = 1
+        while team // cl > max_cta or (team % cl):
+            cl *= 2
+        if cl > 8:
+            raise LoweringError(f"row of {sk.cols} elements is too long for one cluster")
+        tpc = team // cl
+        if cl > 1 and tpc % 32:
+            tpc = 32 * (-(-tpc // 32))
+            team = tpc * cl
+    nv = o.get("nv") or -(-nvec // team)
+    if o.get("rpc"):
+        rpc = o["rpc"]
+    elif tpc >= 32:
+        rpc = max(1, min(8, 256 // tpc))
+    else:
+        rpc = max(1, 256 // tpc)
+    if tpc < 32 and (tpc * rpc) % 32:
+        rpc = 32 // tpc
+    return {"vec": vec, "nvec": nvec, "tpc": tpc, "nv": nv, "rpc": rpc, "cl": cl,
+            "block": tpc * rpc}
+
+
+def choose_ew_config(sk: SubKernel, override: Optional[dict] = None) -> dict:
+    sizes = [DTYPE_SIZE[o.dtype] for o in sk.operands if o.last == "vec"]
+    sizes += [DTYPE_SIZE[o.dtype] for o in sk.outputs]
+    o = dict(override or {})
+    vec = o.get("vec") or _pick_vec(sk.cols, sizes)
+    nvec = -(-sk.cols // vec)
+    if "tpc" in o:
+        tpc = o["tpc"]
+    else:
+        tpc = 128 if nvec >= 128 else max(1, 1 << (max(nvec, 1) - 1).bit_length())
+        tpc = min(tpc, 128)
+    nv = o.get("nv") or max(1, min(2, -(-nvec // tpc)))
+    rpc = o.get("rpc") or max(1, 256 // tpc)
+    if (tpc * rpc) % 32:
+        rpc = max(rpc, 32 // tpc)
+    upt = o.get("upt") or 4
+    return {"vec": vec, "nvec": nvec, "tpc": tpc, "nv": nv, "rpc": rpc, "upt": upt,
+            "block": tpc * rpc, "tiles": -(-nvec // (tpc * nv))}

@@ -1,0 +1,277 @@
+"""Specialise a fusion group for concrete input shapes/dtypes -> GroupPlan."""
+
+from __future__ import annotations
+
+from typing import Optional
+
+from .ir import DataflowGraph, OpType, TensorShape
+from .lowering import (
+    DTYPE_SIZE, GroupPlan, LoweringError, Operand, OutputSpec, SubKernel,
+    broadcast_shapes, build_dag, canon_dtype, choose_ew_config,
+    choose_row_config, classify_operand, group_boundary, infer_shapes,
+    is_mask_const, prod, promote, split_group, EXPENSIVE,
+)
+
+DEFAULT_SYMBOLIC_DIM = 1024
+
+
+def declared_shape(op, symbols: dict) -> tuple:
+    """Concrete stand-in for a declared (possibly symbolic) TensorShape."""
+    shp = op.shape
+    if shp is None or not isinstance(shp, TensorShape) or not shp.dims:
+        return (DEFAULT_SYMBOLIC_DIM,)
+    out = []
+    for d in shp.dims:
+        if isinstance(d, int):
+            out.append(d)
+        else:
+            out.append(symbols.setdefault(str(d), DEFAULT_SYMBOLIC_DIM))
+    return tuple(out)
+
+
+def _op_dtypes(graph, ordered, dtypes: dict) -> dict:
+    """torch-style result dtype per op (Python-scalar constants don't promote)."""
+    out = dict(dtypes)
+    for oid in ordered:
+        op = graph.ops[oid]
+        ds = []
+        for i in op.inputs:
+            src = graph.ops[i]
+            if src.op_type == OpType.CONSTANT:
+                continue
+            ds.append(out[i])
+        out[oid] = promote(ds) if ds else "float32"
+    return out
+
+
+def plan_group(graph: DataflowGraph, group_op_ids, input_shapes: dict,
+               input_dtypes: dict, name: str,
+               tune: Optional[dict] = None) -> GroupPlan:
+    """Lower one fusion group for the given shapes/dtypes of its inputs.
+
+    ``input_shapes``/``input_dtypes`` map each non-constant external op id
+    (graph INPUT ops, or ops computed by another group) to its concrete
+    shape / dtype.
+    """
+    tune = tune or {}
+    ext, outs, ordered = group_boundary(graph, group_op_ids)
+    inputs = [i for i in ext if graph.ops[i].op_type != OpType.CONSTANT]
+    for i in inputs:
+        if i not in input_shapes or i not in input_dtypes:
+            raise LoweringError(f"no shape/dtype for input op {i}")
+    known = {i: tuple(int(d) for d in input_shapes[i]) for i in inputs}
+    for i in ext:
+        if graph.ops[i].op_type == OpType.CONSTANT:
+            known[i] = ()
+    shapes = infer_shapes(graph, ordered, known)
+    dts = {i: canon_dtype(input_dtypes[i]) for i in inputs}
+    dts = _op_dtypes(graph, ordered, dts)
+
+    parts = split_group(graph, ordered)
+    produced_by = {}
+    for k, (_, ops) in enumerate(parts):
+        for o in ops:
+            produced_by[o] = k
+    out_set = set(outs)
+    kernels = []
+    temps = {}
+    for k, (family, ops) in enumerate(parts):
+        ops_set = set(ops)
+        sk_ext = []
+        for o in ops:
+            for j in graph.ops[o].inputs:
+                if j not in ops_set and j not in sk_ext:
+                    sk_ext.append(j)
+        sk_ext.sort()
+        later = set()
+        for _, ops2 in parts[k + 1:]:
+            for o in ops2:
+                later.update(graph.ops[o].inputs)
+        sk_outs = [o for o in ops if o in out_set or o in later]
+        for o in sk_outs:
+            if o not in out_set:
+                temps[o] = (shapes[o], dts[o])
+        kernels.append(_plan_sub(graph, family, ops, sk_ext, sk_outs, shapes, dts, tune))
+
+    return GroupPlan(
+        name=name, inputs=inputs,
+        input_dtypes=[dts[i] for i in inputs],
+        input_shapes=[known[i] for i in inputs],
+        outputs=list(outs), output_dtypes=[dts[o] for o in outs],
+        output_shapes=[shapes[o] for o in outs],
+        kernels=kernels, temps=temps)
+
+
+def _plan_sub(graph, family, ops, ext, outs, shapes, dts, tune) -> SubKernel:
+    if family == "gemm":
+        return _plan_gemm(graph, ops, ext, outs, shapes, dts, tune)
+    it = ()
+    for o in ops:
+        it = broadcast_shapes(it, shapes[o])
+    for j in ext:
+        src = graph.ops[j]
+        if src.op_type == OpType.CONSTANT:
+            continue
+        it = broadcast_shapes(it, shapes[j])
+    if not it:
+        it = (1,)
+    rows, cols = prod(it[:-1]), int(it[-1])
+    operands = []
+    for j in ext:
+        src = graph.ops[j]
+        if src.op_type == OpType.CONSTANT:
+            continue
+        last, row_map, terms = classify_operand(shapes[j], it)
+        operands.append(Operand(index=len(operands), op_id=j, name=src.name or f"op{j}",
+                                dtype=dts[j], shape=shapes[j], last=last,
+                                row_map=row_map, row_terms=terms))
+    outputs = []
+    row_shape = tuple(it[:-1]) + (1,)
+    for o in outs:
+        s = shapes[o]
+        s_pad = (1,) * (len(it) - len(s)) + tuple(s)
+        if s_pad == tuple(it):
+            kind = "full"
+        elif s_pad == row_shape:
+            kind = "row"
+        else:
+            raise LoweringError(f"output of op {o} with shape {s} is neither the "
+                                f"row shape {it} nor one value per row")
+        outputs.append(OutputSpec(index=len(outputs), op_id=o, dtype=dts[o], shape=s, kind=kind))
+    values, env = build_dag(graph, ops, operands, cols)
+    sk = SubKernel(family=family, op_ids=list(ops), operands=operands, outputs=outputs,
+                   rows=rows, cols=cols, values=values,
+                   out_values=[env[o] for o in outs])
+    sk.precise = any(o.dtype == "float32" for o in outputs)
+    needed = _needed(values, sk.out_values)
+    sk.passes = max([values[v].avail for v in needed], default=0)
+    if family == "ew" and sk.passes:
+        family = sk.family = "row"
+    key = f"{sk.family}"
+    override = tune.get(key) or {}
+    if sk.family == "row":
+        prefetch, materialize = _row_storage(sk, needed)
+        sk.config = choose_row_config(sk, prefetch, materialize, override)
+        sk.config["prefetch"] = sorted(prefetch)
+        sk.config["materialize"] = sorted(materialize.items())
+    else:
+        sk.config = choose_ew_config(sk, override)
+    sk.config["needed"] = sorted(needed)
+    return sk
+
+
+def _needed(values, roots) -> set:
+    seen, stack = set(), list(roots)
+    while stack:
+        v = stack.pop()
+        if v in seen:
+            continue
+        seen.add(v)
+        stack.extend(values[v].args)
+    return seen
+
+
+def pass_closures(values, sk: SubKernel, needed: set, materialized: dict):
+    """Elem values each pass must compute, stopping at materialized ones.
+
+    ``materialized`` maps a value id to the pass that computes and stores it;
+    later passes read the stored copy instead of recomputing it.
+
+    Pass p (< passes) computes the arguments of the reductions whose result
+    becomes available at p + 1; the final pass computes the outputs.
+    """
+    roots = {p: [] for p in range(sk.passes + 1)}
+    for v in needed:
+        val = values[v]
+        if val.op in ("rsum", "rmax", "rmin"):
+            roots[val.avail - 1].append(val.args[0])
+    roots[sk.passes] += [v for v in sk.out_values if values[v].kind == "elem"]
+    closures = {}
+    for p, rs in roots.items():
+        seen, stack = set(), list(rs)
+        while stack:
+            v = stack.pop()
+            if v in seen or values[v].kind != "elem":
+                continue
+            seen.add(v)
+            if v in materialized and p > materialized[v]:
+                continue
+            stack.extend(values[v].args)
+        closures[p] = seen
+    return closures
+
+
+def _row_storage(sk: SubKernel, needed: set):
+    values = sk.values
+    naive = pass_closures(values, sk, needed, {})
+    first = {}
+    uses = {}
+    for p in sorted(naive):
+        for v in naive[p]:
+            first.setdefault(v, p)
+            uses.setdefault(v, set()).add(p)
+    materialize = {}
+    for v, ps in uses.items():
+        val = values[v]
+        if val.op in EXPENSIVE and max(ps) > first[v]:
+            materialize[v] = first[v]
+    prefetch = set()
+    for opd in sk.operands:
+        if opd.last == "vec" and opd.row_map != "zero":
+            prefetch.add(opd.index)
+    return prefetch, materialize
+
+
+def _plan_gemm(graph, ops, ext, outs, shapes, dts, tune) -> SubKernel:
+    mm = ops[0]
+    a_id, b_id = graph.ops[mm].inputs
+    a_shape, b_shape = shapes[a_id], shapes[b_id]
+    K, N = int(b_shape[0]), int(b_shape[1])
+    M = prod(a_shape[:-1])
+    it = shapes[mm]
+    for o in ops:
+        it = broadcast_shapes(it, shapes[o])
+    if prod(it[:-1]) != M or it[-1] != N:
+        raise LoweringError("the GEMM epilogue broadcasts beyond the product shape")
+    operands = []
+    a_idx = b_idx = None
+    for j in ext:
+        src = graph.ops[j]
+        if src.op_type == OpType.CONSTANT:
+            continue
+        if j in (a_id, b_id) and not any(j in graph.ops[o].inputs for o in ops[1:]):
+            last, row_map, terms = "vec", "full", ()
+        else:
+            last, row_map, terms = classify_operand(shapes[j], it)
+        operands.append(Operand(index=len(operands), op_id=j, name=src.name or f"op{j}",
+                                dtype=dts[j], shape=shapes[j], last=last,
+                                row_map=row_map, row_terms=terms))
+        if j == a_id:
+            a_idx = operands[-1].index
+        if j == b_id:
+            b_idx = operands[-1].index
+    if a_id == b_id:
+        b_idx = a_idx
+    if dts[a_id] != dts[b_id] or dts[a_id] == "float32":
+        raise LoweringError("the tensor-core GEMM takes bf16 x bf16 or fp16 x fp16 operands")
+    outputs = []
+    for o in outs:
+        s = shapes[o]
+        s_pad = (1,) * (len(it) - len(s)) + tuple(s)
+        if s_pad != tuple(it):
+            raise LoweringError("GEMM outputs must have the product shape")
+        outputs.append(OutputSpec(index=len(outputs), op_id=o, dtype=dts[o], shape=s, kind="full"))
+    epi_operands = [o for o in operands if o.index not in (a_idx, b_idx)
+                    or any(o.op_id in graph.ops[x].inputs for x in ops[1:])]
+    values, env = build_dag(graph, ops[1:], epi_operands, N, acc_op=mm)
+    sk = SubKernel(family="gemm", op_ids=list(ops), operands=operands, outputs=outputs,
+                   rows=M, cols=N, values=values, out_values=[env[o] for o in outs],
+                   m=M, n=N, k=K, a_operand=a_idx, b_operand=b_idx)
+    sk.precise = any(o.dtype == "float32" for o in outputs)
+    needed = _needed(values, sk.out_values)
+    if any(values[v].avail for v in needed):
+        raise LoweringError("GEMM epilogues are elementwise only")
+    from .gemm_config import choose_gemm_config
+    sk.config = choose_gemm_config(sk, tune.get("gemm") or {})
+    sk.config["needed"] = sorted(needed)
+    return sk

@@ -1,0 +1,314 @@
+"""Runtime: generated source -> nvcc cubin -> launches through libmolten_rt.so.
+
+Drop-in for the reference's ``molten/runtime.py``: ``MoltenRuntime(cache_dir,
+verbose).compile(kernel) -> CompiledKernel`` (``runtime.py:47-94``) and
+``CompiledKernel(*tensors)`` returning a new output tensor
+(``runtime.py:31-36``), with ``clear_cache`` (``runtime.py:201-207``).
+
+Differences that follow from the design:
+
+* the kernel is built with nvcc into an sm_100a cubin (cached on disk by
+  content hash) and launched through the C ABI of ``libmolten_rt.so``
+  (``include/molten_rt.h``) on the caller's current torch stream; there is no
+  pybind module and no torch.utils.cpp_extension build;
+* a call takes every graph input in graph-input order (x, w[, g] ...), not
+  only ``x``; outputs are allocated with ``torch.empty`` (no zero fill), or
+  passed in with ``out=``;
+* the first call with a new (shape, dtype) signature re-specialises the
+  group for it (shapes and dtypes are baked into the kernel);
+* there is no CPU or eager fallback: a missing library, a failed build or a
+  failed launch raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import hashlib
+import os
+import shutil
+import threading
+from collections import OrderedDict
+from dataclasses import dataclass, field
+from pathlib import Path
+from typing import Optional
+
+from . import _capi
+from .build import build_cubin, default_cache_dir
+from .codegen import CodeGenerator, GeneratedKernel, KernelConfig, kernel_entry
+from .lowering import DTYPE_SIZE, LoweringError, canon_dtype
+
+_TORCH_DTYPES = None
+
+
+def _torch():
+    import torch
+    return torch
+
+
+def _dtype_name(t) -> str:
+    return canon_dtype(str(t.dtype))
+
+
+def _torch_dtype(name: str):
+    torch = _torch()
+    return {"float32": torch.float32, "bfloat16": torch.bfloat16, "float16": torch.float16}[name]
+
+
+_TMA_CODE = {"bfloat16": _capi.DT_BF16, "float16": _capi.DT_F16, "float32": _capi.DT_F32}
+
+
+class _Spec:
+    """One shape/dtype specialisation of a group, ready to launch."""
+
+    def __init__(self, gk: GeneratedKernel, cubin: Path):
+        self.gk = gk
+        self.plan = gk.plan
+        self.cubin = cubin
+        self.modules: dict = {}
+        self.lock = threading.Lock()
+        self.entries = [kernel_entry(gk.name, i, len(self.plan.kernels)).encode()
+                        for i in range(len(self.plan.kernels))]
+        self.out_dtypes = [_torch_dtype(d) for d in self.plan.output_dtypes]
+        self.temp_specs = {k: (tuple(s), _torch_dtype(d)) for k, (s, d) in self.plan.temps.items()}
+        self._cfgs: dict = {}
+        self._tmaps: OrderedDict = OrderedDict()
+
+    def module(self, device: int) -> _capi.Module:
+        m = self.modules.get(device)
+        if m is None:
+            with self.lock:
+                m = self.modules.get(device)
+                if m is None:
+                    m = _capi.Module(str(self.cubin), device)
+                    self.modules[device] = m
+        return m
+
+    def launch_cfg(self, i: int, device: int) -> _capi.LaunchCfg:
+        key = (i, device)
+        cfg = self._cfgs.get(key)
+        if cfg is not None:
+            return cfg
+        sk = self.plan.kernels[i]
+        c = sk.config
+        cfg = _capi.LaunchCfg()
+        if sk.family == "row":
+            grid = (-(-sk.rows // c["rpc"])) * c["cl"]
+            cfg.grid[:] = [max(1, grid), 1, 1]
+            cfg.block[:] = [c["block"], 1, 1]
+            cfg.cluster[:] = [c["cl"], 1, 1] if c["cl"] > 1 else [1, 1, 1]
+            cfg.smem_bytes = 0
+        elif sk.family == "ew":
+            rb = -(-sk.rows // (c["rpc"] * c["upt"]))
+            cfg.grid[:] = [c["tiles"], max(1, min(rb, 65535)), 1]
+            cfg.block[:] = [c["block"], 1, 1]
+            cfg.cluster[:] = [1, 1, 1]
+            cfg.smem_bytes = 0
+        else:
+            torch = _torch()
+            sms = torch.cuda.get_device_properties(device).multi_processor_count
+            tiles = (-(-sk.m // c["bm"])) * (-(-sk.n // c["bn"]))
+            cfg.grid[:] = [max(1, min(tiles, sms)), 1, 1]
+            cfg.block[:] = [128, c["threads"] // 128, 1]
+            cfg.cluster[:] = [1, 1, 1]
+            cfg.smem_bytes = c["smem_bytes"]
+        self._cfgs[key] = cfg
+        return cfg
+
+    def tmap(self, t, dtype: str, rows: int, cols: int, box_inner: int, box_outer: int) -> bytes:
+        key = (t.data_ptr(), rows, cols, t.stride(0), box_inner, box_outer)
+        v = self._tmaps.get(key)
+        if v is None:
+            esz = DTYPE_SIZE[dtype]
+            v = _capi.encode_tma_2d(_TMA_CODE[dtype], t.data_ptr(), cols, rows,
+                                    t.stride(0) * esz, box_inner, box_outer, True)
+            self._tmaps[key] = v
+            if len(self._tmaps) > 64:
+                self._tmaps.popitem(last=False)
+        else:
+            self._tmaps.move_to_end(key)
+        return v
+
+    def run(self, tensors, outs, stream: Optional[int], row_offset: int):
+        torch = _torch()
+        plan = self.plan
+        dev = tensors[0].device
+        di = dev.index if dev.index is not None else torch.cuda.current_device()
+        if stream is None:
+            stream = torch.cuda.current_stream(dev).cuda_stream
+        env = dict(zip(plan.inputs, tensors))
+        if outs is None:
+            outs = [torch.empty(s, dtype=d, device=dev)
+                    for s, d in zip(plan.output_shapes, self.out_dtypes)]
+        env.update(zip(plan.outputs, outs))
+        for op_id, (s, d) in self.temp_specs.items():
+            env[op_id] = torch.empty(s, dtype=d, device=dev)
+        mod = self.module(di)
+        for i, sk in enumerate(plan.kernels):
+            cfg = self.launch_cfg(i, di)
+            if sk.family == "gemm":
+                a = _capi.GemmArgs()
+                A = env[sk.operands[sk.a_operand].op_id]
+                B = env[sk.operands[sk.b_operand].op_id]
+                dt = sk.operands[sk.a_operand].dtype
+                A2 = A.reshape(-1, A.shape[-1])
+                ctypes.memmove(a.tmap_a, self.tmap(A2, dt, sk.m, sk.k, 64, 128), 128)
+                ctypes.memmove(a.tmap_b, self.tmap(B, dt, sk.k, sk.n, 64, 64), 128)
+                a.m, a.n, a.k = sk.m, sk.n, sk.k
+                a.status = _capi.status_word(di)
+            else:
+                a = _capi.RowArgs()
+                a.rows, a.cols = sk.rows, sk.cols
+            a.row_offset = row_offset
+            for opd in sk.operands:
+                a.inp[opd.index] = env[opd.op_id].data_ptr()
+            for o in sk.outputs:
+                a.out[o.index] = env[o.op_id].data_ptr()
+            mod.launch(self.entries[i], cfg, a, stream)
+        return outs
+
+
+@dataclass
+class CompiledKernel:
+    """A generated kernel bound to its cubin; call it with CUDA tensors."""
+    name: str
+    source: str
+    config: KernelConfig
+    _module: object = None
+    kernel: Optional[GeneratedKernel] = None
+    runtime: Optional["MoltenRuntime"] = None
+    _specs: dict = field(default_factory=dict)
+
+    def __call__(self, *tensors, out=None, stream=None, row_offset: int = 0):
+        if self.kernel is None or self.runtime is None:
+            raise RuntimeError(f"Kernel '{self.name}' not compiled. Call compile() first.")
+        plan = self.kernel.plan
+        if len(tensors) != len(plan.inputs):
+            g = self.kernel.graph
+            names = [g.ops[i].name or f"op{i}" for i in plan.inputs] if g else plan.inputs
+            raise RuntimeError(f"{self.name} takes {len(plan.inputs)} tensors {names}, "
+                               f"got {len(tensors)}")
+        prepared = []
+        for t in tensors:
+            if not getattr(t, "is_cuda", False):
+                raise RuntimeError(f"{self.name}: inputs must be CUDA tensors (got {type(t).__name__} "
+                                   f"on {getattr(t, 'device', '?')})")
+            prepared.append(t)
+        dev = prepared[0].device
+        for t in prepared[1:]:
+            if t.device != dev:
+                raise RuntimeError(f"{self.name}: all inputs must be on {dev}, got {t.device}")
+        spec = self._spec_for(prepared)
+        prepared = self._conform(spec, prepared)
+        if out is not None:
+            outs = list(out) if isinstance(out, (list, tuple)) else [out]
+            self._check_outs(spec, outs, dev)
+        else:
+            outs = None
+        res = spec.run(prepared, outs, stream, row_offset)
+        return res[0] if len(res) == 1 else tuple(res)
+
+    # -- specialisation -------------------------------------------------
+    def _signature(self, tensors):
+        aligned = all(t.data_ptr() % 16 == 0 for t in tensors)
+        return tuple((str(t.dtype), tuple(t.shape)) for t in tensors) + (aligned,)
+
+    def _spec_for(self, tensors) -> _Spec:
+        sig = self._signature(tensors)
+        spec = self._specs.get(sig)
+        if spec is not None:
+            return spec
+        plan = self.kernel.plan
+        shapes = {i: tuple(t.shape) for i, t in zip(plan.inputs, tensors)}
+        dtypes = {i: _dtype_name(t) for i, t in zip(plan.inputs, tensors)}
+        same = (all(tuple(plan.input_shapes[k]) == shapes[i] for k, i in enumerate(plan.inputs))
+                and all(plan.input_dtypes[k] == dtypes[i] for k, i in enumerate(plan.inputs))
+                and sig[-1])
+        if same:
+            gk = self.kernel
+        else:
+            if self.kernel.graph is None or self.kernel.group is None:
+                raise RuntimeError(f"{self.name} was generated for {plan.input_shapes} "
+                                   f"{plan.input_dtypes} and cannot be re-specialised")
+            tune = dict(self.runtime.tune)
+            if not sig[-1]:
+                for fam in ("row", "ew"):
+                    tune[fam] = dict(tune.get(fam) or {}, vec=1)
+            gen = CodeGenerator(dtype=None, tune=tune)
+            gk = gen.generate(self.kernel.graph, self.kernel.group, shapes, dtypes)
+        cubin = build_cubin(gk.source, gk.name, self.runtime.cache_dir, self.runtime.verbose)
+        spec = _Spec(gk, cubin)
+        self._specs[sig] = spec
+        return spec
+
+    @staticmethod
+    def _conform(spec: _Spec, tensors):
+        plan = spec.plan
+        gemm_b = set()
+        for sk in plan.kernels:
+            if sk.family == "gemm":
+                gemm_b.add(sk.operands[sk.b_operand].op_id)
+        out = []
+        for op_id, t in zip(plan.inputs, tensors):
+            if op_id in gemm_b and t.dim() == 2 and t.stride(1) == 1 \
+                    and (t.stride(0) * t.element_size()) % 16 == 0:
+                out.append(t)              # a column slice of B is fine for TMA
+            else:
+                out.append(t.contiguous())
+        return out
+
+    @staticmethod
+    def _check_outs(spec: _Spec, outs, dev):
+        plan = spec.plan
+        if len(outs) != len(plan.outputs):
+            raise RuntimeError(f"expected {len(plan.outputs)} output tensors, got {len(outs)}")
+        for t, s, d in zip(outs, plan.output_shapes, spec.out_dtypes):
+            if tuple(t.shape) != tuple(s) or t.dtype != d or t.device != dev or not t.is_contiguous():
+                raise RuntimeError(f"output must be a contiguous {d} tensor of shape {tuple(s)} "
+                                   f"on {dev}")
+
+    def specialization(self, *tensors) -> GeneratedKernel:
+        """The GeneratedKernel that a call with these tensors runs."""
+        return self._spec_for(list(tensors)).gk
+
+
+class MoltenRuntime:
+    """Builds generated kernels into cubins and hands out callables."""
+
+    def __init__(self, cache_dir: Optional[str] = None, verbose: bool = False,
+                 tune: Optional[dict] = None):
+        self.verbose = verbose
+        self.cache_dir = Path(cache_dir) if cache_dir else default_cache_dir()
+        self.cache_dir.mkdir(parents=True, exist_ok=True)
+        self.tune = tune or {}
+        self._compiled: dict = {}
+        _capi.load_library()           # fail loudly when the runtime is missing
+
+    def compile(self, kernel: GeneratedKernel) -> CompiledKernel:
+        key = hashlib.sha256(kernel.source.encode()).hexdigest()[:16]
+        ck = self._compiled.get(key)
+        if ck is not None:
+            return ck
+        cubin = build_cubin(kernel.source, kernel.name, self.cache_dir, self.verbose)
+        ck = CompiledKernel(name=kernel.name, source=kernel.source, config=kernel.config,
+                            _module=str(cubin), kernel=kernel, runtime=self)
+        sig = None
+        if kernel.plan is not None:
+            sig = tuple((str(_torch_dtype(d)), tuple(s))
+                        for d, s in zip(kernel.plan.input_dtypes, kernel.plan.input_shapes)) + (True,)
+            ck._specs[sig] = _Spec(kernel, cubin)
+        self._compiled[key] = ck
+        if self.verbose:
+            print(f"molten: built {cubin.name}")
+        return ck
+
+    def clear_cache(self) -> None:
+        if self.cache_dir.exists():
+            for f in self.cache_dir.iterdir():
+                if f.suffix in (".cubin", ".cu"):
+                    f.unlink()
+        self._compiled.clear()
+
+    @staticmethod
+    def read_status(device: int = 0, reset: bool = True) -> int:
+        """Error bits set by kernels with bounded waits on ``device``."""
+        return _capi.read_status(device, reset)

@@ -1,0 +1,153 @@
+"""Named workloads of the benchmark set: graph + seeded synthetic inputs.
+
+Shapes and value distributions are the benchmark set's (no dataset is
+involved):
+
+=========================  ==============================================
+rmsnorm                    x fp32 [2048, 5120] ~ N(0,1); w = 1 + 0.1 N(0,1)
+rmsnorm_silu_gate          x, g bf16 [rows, 3584] ~ N(0,1); w = 1 + 0.1 N(0,1);
+                           rows 1 (decode), 2048 (prefill), 8192 (long)
+softmax                    logits ~ N(0, 3^2), [32*2048, 2048] (as
+                           [32, 2048, 2048]) or [4096, 32768]; fp32 / bf16;
+                           optional causal mask
+chain                      x, r bf16 [16384, 8192] ~ N(0,1); a, b, s ~ U(-1,1)
+gemm_bias_gelu             A bf16 [8192, 4096] ~ N(0,1); B [4096, 14336] ~
+                           N(0, 1/4096); bias [14336] ~ N(0, 0.02^2)
+=========================  ==============================================
+
+Values are drawn in fp32 from ``torch.Generator().manual_seed(seed)`` and
+then cast, so a given (workload, seed, device type) always yields the same
+tensors.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+from . import graphs
+
+
+@dataclass
+class Workload:
+    name: str
+    kind: str
+    params: dict
+    dtype: str
+    # algorithmic work per call
+    bytes_per_call: int = 0
+    flops_per_call: int = 0
+    input_names: list = field(default_factory=list)
+
+    def graph(self, **over):
+        p = dict(self.params)
+        p.update(over)
+        return graphs.BUILDERS[self.kind](dtype=self.dtype, **p)
+
+
+def _esz(dtype):
+    return 4 if dtype == "float32" else 2
+
+
+def _rms(name, rows, cols, dtype, silu):
+    kind = "rmsnorm_silu_gate" if silu else "rmsnorm"
+    e = _esz(dtype)
+    nbytes = rows * cols * e * (3 if silu else 2) + cols * e
+    names = ["x", "w", "gate"] if silu else ["x", "w"]
+    return Workload(name, kind, {"rows": rows, "cols": cols}, dtype, nbytes, 0, names)
+
+
+def _softmax(name, shape, dtype, causal):
+    n = 1
+    for d in shape:
+        n *= d
+    return Workload(name, "softmax", {"shape": tuple(shape), "causal": causal}, dtype,
+                    2 * n * _esz(dtype), 0, ["logits"])
+
+
+WORKLOADS = {w.name: w for w in [
+    _rms("rmsnorm_f32_2048x5120", 2048, 5120, "float32", False),
+    _rms("rmsnorm_silu_bf16_1x3584", 1, 3584, "bfloat16", True),
+    _rms("rmsnorm_silu_bf16_2048x3584", 2048, 3584, "bfloat16", True),
+    _rms("rmsnorm_silu_bf16_8192x3584", 8192, 3584, "bfloat16", True),
+    _softmax("softmax_f32_65536x2048", (32, 2048, 2048), "float32", False),
+    _softmax("softmax_f32_65536x2048_causal", (32, 2048, 2048), "float32", True),
+    _softmax("softmax_bf16_65536x2048", (32, 2048, 2048), "bfloat16", False),
+    _softmax("softmax_bf16_65536x2048_causal", (32, 2048, 2048), "bfloat16", True),
+    _softmax("softmax_f32_4096x32768", (4096, 32768), "float32", False),
+    _softmax("softmax_f32_4096x32768_causal", (4096, 32768), "float32", True),
+    _softmax("softmax_bf16_4096x32768", (4096, 32768), "bfloat16", False),
+    _softmax("softmax_bf16_4096x32768_causal", (4096, 32768), "bfloat16", True),
+    Workload("chain_bf16_16384x8192", "chain", {"rows": 16384, "cols": 8192}, "bfloat16",
+             3 * 16384 * 8192 * 2 + 3 * 8192 * 2, 0, ["x", "r", "a", "b", "s"]),
+    Workload("gemm_bias_gelu_bf16_8192x4096x14336", "gemm_bias_gelu",
+             {"m": 8192, "k": 4096, "n": 14336}, "bfloat16",
+             (8192 * 4096 + 4096 * 14336 + 14336 + 8192 * 14336) * 2,
+             2 * 8192 * 4096 * 14336, ["A", "B", "bias"]),
+]}
+
+HEADLINE = "rmsnorm_silu_bf16_8192x3584"
+
+
+def scaled(w: Workload, **params) -> Workload:
+    """The same workload kind at other sizes (for small parity cases)."""
+    p = dict(w.params)
+    p.update(params)
+    if w.kind in ("rmsnorm", "rmsnorm_silu_gate"):
+        return _rms(w.name + "_scaled", p["rows"], p["cols"], w.dtype, w.kind != "rmsnorm")
+    if w.kind == "softmax":
+        return _softmax(w.name + "_scaled", p["shape"], w.dtype, p["causal"])
+    if w.kind == "chain":
+        r, c = p["rows"], p["cols"]
+        return Workload(w.name + "_scaled", "chain", {"rows": r, "cols": c}, w.dtype,
+                        3 * r * c * 2 + 3 * c * 2, 0, list(w.input_names))
+    m, k, n = p["m"], p["k"], p["n"]
+    return Workload(w.name + "_scaled", "gemm_bias_gelu", {"m": m, "k": k, "n": n}, w.dtype,
+                    (m * k + k * n + n + m * n) * 2, 2 * m * k * n, list(w.input_names))
+
+
+def make_inputs(w: Workload, seed: int = 0, device="cpu") -> list:
+    """Seeded inputs of a workload, in graph-input order, as torch tensors."""
+    import torch
+    dev = torch.device(device)
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    dt = {"float32": torch.float32, "bfloat16": torch.bfloat16, "float16": torch.float16}[w.dtype]
+    p = w.params
+
+    def normal(shape, mean=0.0, std=1.0):
+        t = torch.randn(*shape, generator=g, device=dev, dtype=torch.float32)
+        if std != 1.0:
+            t.mul_(std)
+        if mean != 0.0:
+            t.add_(mean)
+        return t.to(dt)
+
+    def uniform(shape, lo, hi):
+        t = torch.rand(*shape, generator=g, device=dev, dtype=torch.float32)
+        return t.mul_(hi - lo).add_(lo).to(dt)
+
+    if w.kind in ("rmsnorm", "rmsnorm_silu_gate"):
+        rows, cols = p["rows"], p["cols"]
+        x = normal((rows, cols))
+        wt = normal((cols,), 1.0, 0.1)
+        if w.kind == "rmsnorm":
+            return [x, wt]
+        gate = normal((rows, cols))
+        return [x, wt, gate]
+    if w.kind == "softmax":
+        return [normal(p["shape"], 0.0, 3.0)]
+    if w.kind == "chain":
+        rows, cols = p["rows"], p["cols"]
+        x = normal((rows, cols))
+        r = normal((rows, cols))
+        a = uniform((cols,), -1.0, 1.0)
+        b = uniform((cols,), -1.0, 1.0)
+        s = uniform((cols,), -1.0, 1.0)
+        return [x, r, a, b, s]
+    if w.kind == "gemm_bias_gelu":
+        m, k, n = p["m"], p["k"], p["n"]
+        A = normal((m, k))
+        B = normal((k, n), 0.0, (1.0 / k) ** 0.5)
+        bias = normal((n,), 0.0, 0.02)
+        return [A, B, bias]
+    raise KeyError(w.kind)

@@ -1,0 +1,286 @@
+"""Parity of the sm_100a kernels with the oracle, on a B200.
+
+Every call goes through MoltenRuntime -> libmolten_rt.so (molten_launch).
+Bars (tests/_golden.assert_close): fp32 within 1e-5 relative, bf16 within
+1e-2 relative of the fp32-accumulated reference.
+
+* golden cases: the exact inputs of tests/golden, checked against the
+  reference's own results;
+* full-size benchmark workloads: rows are independent, so a seeded sample of
+  rows is checked against the oracle, plus size-independent properties
+  (softmax rows sum to 1 and masked entries are exactly 0, repeated runs are
+  bit-identical, the GEMM's bounded waits never time out);
+* edge cases: one row, ragged widths, misaligned pointers, GEMM shapes that
+  are not tile multiples, row-sharded launches with a global row offset.
+"""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from molten_b200 import graphs, workloads
+from molten_b200.codegen import compile_graph
+from molten_b200.runtime import MoltenRuntime
+from oracle import graph_oracle as orc
+from tests._golden import CASES, assert_close, graph_for, load
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+TORCH_DT = {"float32": torch.float32, "bfloat16": torch.bfloat16, "float16": torch.float16}
+
+
+@pytest.fixture(scope="module")
+def rt():
+    return MoltenRuntime()
+
+
+def to_torch(arr, dev=DEV):
+    if arr.dtype == np.uint16:
+        return torch.from_numpy(arr.view(np.int16).copy()).view(torch.bfloat16).to(dev)
+    return torch.from_numpy(arr.copy()).to(dev)
+
+
+def to_numpy(t):
+    t = t.detach().cpu()
+    if t.dtype == torch.bfloat16:
+        return t.view(torch.int16).numpy().view(np.uint16)
+    return t.numpy()
+
+
+def as_f32(t):
+    return t.detach().float().cpu().numpy()
+
+
+def run_graph(rt, g, tensors, dtype, **kw):
+    ks = compile_graph(g, dtype=dtype)
+    assert len(ks) == 1
+    ck = rt.compile(ks[0])
+    return ck(*tensors, **kw), ck
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_golden_case(rt, case):
+    meta, inputs, ref_f32, ref_out = load(case)
+    g = graph_for(meta, inputs)
+    tensors = [to_torch(inputs[k]) for k in meta["inputs"]]
+    dt = meta["out_dtype"]
+    out, _ = run_graph(rt, g, tensors, tensors[0].dtype.__str__().replace("torch.", ""))
+    torch.cuda.synchronize()
+    assert_close(as_f32(out), ref_f32, dt, case)
+    # and against the oracle's once-rounded output
+    res = orc.evaluate(g, inputs)
+    oid = g.ops[g._outputs[0]].inputs[0]
+    assert_close(as_f32(out), res[("f32", oid)], dt, case + " vs oracle")
+
+
+def _sample_rows(rows, n, seed=0):
+    rng = np.random.default_rng(seed)
+    pick = set(rng.choice(rows, size=min(n, rows), replace=False).tolist())
+    pick |= {0, rows - 1}
+    return np.array(sorted(pick))
+
+
+def _rows_2d(t):
+    return t.reshape(-1, t.shape[-1])
+
+
+FULL = [
+    "rmsnorm_f32_2048x5120",
+    "rmsnorm_silu_bf16_1x3584",
+    "rmsnorm_silu_bf16_2048x3584",
+    "rmsnorm_silu_bf16_8192x3584",
+    "softmax_f32_65536x2048",
+    "softmax_f32_65536x2048_causal",
+    "softmax_bf16_65536x2048_causal",
+    "softmax_f32_4096x32768",
+    "softmax_bf16_4096x32768_causal",
+    "chain_bf16_16384x8192",
+]
+
+
+@pytest.mark.parametrize("name", FULL)
+def test_full_size_row_workloads(rt, name):
+    w = workloads.WORKLOADS[name]
+    g = w.graph()
+    xs = workloads.make_inputs(w, seed=0, device=DEV)
+    out, ck = run_graph(rt, g, xs, w.dtype)
+    out2 = ck(*xs)
+    torch.cuda.synchronize()
+    assert torch.equal(out.view(torch.int16) if out.dtype != torch.float32 else out.view(torch.int32),
+                       out2.view(torch.int16) if out2.dtype != torch.float32 else out2.view(torch.int32)), \
+        "repeated runs differ"
+    rows = _rows_2d(xs[0]).shape[0]
+    pick = _sample_rows(rows, 48)
+    # evaluate the oracle on the sampled rows only (rows are independent)
+    sub_inputs = {}
+    names = [g.ops[i].name for i in sorted(i for i, o in g.ops.items() if o.op_type.name == "INPUT")]
+    for nm, t in zip(names, xs):
+        if t.dim() >= 2 and _rows_2d(t).shape[0] == rows:
+            sub_inputs[nm] = to_numpy(_rows_2d(t)[torch.as_tensor(pick, device=t.device)])
+        else:
+            sub_inputs[nm] = to_numpy(t)
+    got = as_f32(_rows_2d(out)[torch.as_tensor(pick, device=out.device)])
+    if w.kind == "softmax":
+        # the mask depends on the global row: evaluate row by row
+        g1 = graphs.softmax((1, got.shape[1]), causal=w.params["causal"])
+        oid = g1.ops[g1._outputs[0]].inputs[0]
+        ref = np.concatenate([
+            orc.evaluate(g1, {"logits": sub_inputs["logits"][i:i + 1]},
+                         row_offset=int(r))[("f32", oid)]
+            for i, r in enumerate(pick)])
+        full = as_f32(_rows_2d(out))
+        sums = full.astype(np.float64).sum(axis=1)
+        tol = 1e-5 if w.dtype == "float32" else 2e-2
+        assert np.all(np.abs(sums - 1.0) < tol * max(1, np.sqrt(full.shape[1]) / 8)), "row sums"
+        assert np.all(full >= 0)
+        if w.params["causal"]:
+            cols = full.shape[1]
+            r = np.arange(full.shape[0]) % cols
+            masked = np.arange(cols)[None, :] > r[:, None]
+            assert np.all(full[masked] == 0.0), "masked entries must be exactly 0"
+    else:
+        sg = w.graph(rows=len(pick))
+        res = orc.evaluate(sg, sub_inputs)
+        ref = res[("f32", sg.ops[sg._outputs[0]].inputs[0])]
+    assert_close(got, ref, w.dtype, name)
+
+
+def test_full_size_gemm(rt):
+    w = workloads.WORKLOADS["gemm_bias_gelu_bf16_8192x4096x14336"]
+    A, B, bias = workloads.make_inputs(w, seed=0, device=DEV)
+    out, ck = run_graph(rt, w.graph(), [A, B, bias], "bfloat16")
+    torch.cuda.synchronize()
+    assert MoltenRuntime.read_status(0) == 0, "a bounded wait timed out"
+    pick = _sample_rows(A.shape[0], 6)
+    Ar = to_numpy(A[torch.as_tensor(pick, device=DEV)])
+    cols = _sample_rows(B.shape[1], 512, seed=1)
+    Bc = to_numpy(B[:, torch.as_tensor(cols, device=DEV)].contiguous())
+    bc = to_numpy(bias[torch.as_tensor(cols, device=DEV)])
+    sg = graphs.gemm_bias_gelu(len(pick), A.shape[1], len(cols))
+    res = orc.evaluate(sg, {"A": Ar, "B": Bc, "bias": bc})
+    ref = res[("f32", sg.ops[sg._outputs[0]].inputs[0])]
+    got = as_f32(out[torch.as_tensor(pick, device=DEV)][:, torch.as_tensor(cols, device=DEV)])
+    assert_close(got, ref, "bfloat16", "gemm full size")
+    out2 = ck(A, B, bias)
+    torch.cuda.synchronize()
+    assert torch.equal(out.view(torch.int16), out2.view(torch.int16)), "repeated runs differ"
+
+
+@pytest.mark.parametrize("m,k,n", [(128, 64, 64), (200, 72, 136), (1, 4096, 256), (257, 512, 320),
+                                   (1024, 1024, 1024)])
+def test_gemm_shapes(rt, m, k, n):
+    g = graphs.gemm_bias_gelu(m, k, n)
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(m * 7 + n)
+    A = torch.randn(m, k, generator=gen, device=DEV).to(torch.bfloat16)
+    B = (torch.randn(k, n, generator=gen, device=DEV) / k ** 0.5).to(torch.bfloat16)
+    bias = (torch.randn(n, generator=gen, device=DEV) * 0.02).to(torch.bfloat16)
+    out, _ = run_graph(rt, g, [A, B, bias], "bfloat16")
+    torch.cuda.synchronize()
+    assert MoltenRuntime.read_status(0) == 0
+    res = orc.evaluate(g, {"A": to_numpy(A), "B": to_numpy(B), "bias": to_numpy(bias)})
+    assert_close(as_f32(out), res[("f32", g.ops[g._outputs[0]].inputs[0])], "bfloat16",
+                 f"gemm {m}x{k}x{n}")
+
+
+def test_gemm_plain_matmul_fp16(rt):
+    g = graphs.gemm_bias_gelu(256, 256, 256, dtype="float16")
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(5)
+    A = torch.randn(256, 256, generator=gen, device=DEV).half()
+    B = (torch.randn(256, 256, generator=gen, device=DEV) / 16).half()
+    bias = (torch.randn(256, generator=gen, device=DEV) * 0.02).half()
+    out, _ = run_graph(rt, g, [A, B, bias], "float16")
+    torch.cuda.synchronize()
+    res = orc.evaluate(g, {"A": to_numpy(A), "B": to_numpy(B), "bias": to_numpy(bias)})
+    assert_close(as_f32(out), res[("f32", g.ops[g._outputs[0]].inputs[0])], "float16", "fp16 gemm")
+
+
+@pytest.mark.parametrize("rows,cols,dtype", [(1, 5120, "float32"), (5, 1000, "float32"),
+                                             (3, 3583, "bfloat16"), (7, 24, "bfloat16"),
+                                             (33, 128, "float16"), (2, 32768, "bfloat16")])
+def test_rmsnorm_edge_shapes(rt, rows, cols, dtype):
+    g = graphs.rmsnorm_silu_gate(rows, cols, dtype=dtype)
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(rows * 131 + cols)
+    x = torch.randn(rows, cols, generator=gen, device=DEV).to(TORCH_DT[dtype])
+    wt = (1 + 0.1 * torch.randn(cols, generator=gen, device=DEV)).to(TORCH_DT[dtype])
+    gt = torch.randn(rows, cols, generator=gen, device=DEV).to(TORCH_DT[dtype])
+    out, _ = run_graph(rt, g, [x, wt, gt], dtype)
+    torch.cuda.synchronize()
+    res = orc.evaluate(g, {"x": to_numpy(x), "w": to_numpy(wt), "gate": to_numpy(gt)})
+    assert_close(as_f32(out), res[("f32", g.ops[g._outputs[0]].inputs[0])], dtype,
+                 f"rmsnorm_silu {rows}x{cols} {dtype}")
+
+
+def test_misaligned_pointers_take_the_scalar_path(rt):
+    g = graphs.rmsnorm(4, 512)
+    base = torch.randn(4 * 512 + 1, device=DEV)
+    x = base[1:].view(4, 512)                         # 4-byte offset: not 16-byte aligned
+    wt = torch.randn(512, device=DEV)
+    ck = rt.compile(compile_graph(g)[0])
+    out = ck(x, wt)
+    torch.cuda.synchronize()
+    assert ck.specialization(x, wt).plan.kernels[0].config["vec"] == 1
+    res = orc.evaluate(g, {"x": to_numpy(x), "w": to_numpy(wt)})
+    assert_close(as_f32(out), res[("f32", g.ops[g._outputs[0]].inputs[0])], "float32", "misaligned")
+
+
+def test_row_sharded_launches_match_whole(rt):
+    """Rank-style row blocks with their global row offset reproduce the
+    single launch bit for bit (causal mask included)."""
+    from molten_b200.shard import row_shards
+    g = graphs.softmax((96, 256), causal=True)
+    x = 3 * torch.randn(96, 256, device=DEV)
+    ck = rt.compile(compile_graph(g)[0])
+    whole = ck(x)
+    parts = []
+    for start, stop in row_shards(96, 3):
+        gs = graphs.softmax((stop - start, 256), causal=True)
+        cks = rt.compile(compile_graph(gs)[0])
+        parts.append(cks(x[start:stop], row_offset=start))
+    torch.cuda.synchronize()
+    assert torch.equal(torch.cat(parts), whole)
+
+
+def test_out_argument_and_stream(rt):
+    g = graphs.chain(64, 1024)
+    w = workloads.scaled(workloads.WORKLOADS["chain_bf16_16384x8192"], rows=64, cols=1024)
+    xs = workloads.make_inputs(w, seed=3, device=DEV)
+    ck = rt.compile(compile_graph(g, dtype="bfloat16")[0])
+    out = torch.empty(64, 1024, dtype=torch.bfloat16, device=DEV)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        r = ck(*xs, out=out)
+    s.synchronize()
+    assert r is out
+    res = orc.evaluate(g, {n: to_numpy(t) for n, t in zip(["x", "r", "a", "b", "s"], xs)})
+    assert_close(as_f32(out), res[("f32", g.ops[g._outputs[0]].inputs[0])], "bfloat16", "out=")
+
+
+def test_multi_kernel_group_gemm_then_softmax(rt):
+    """MATMUL -> SOFTMAX (one fusion group) runs as GEMM + row kernel."""
+    from molten_b200.ir import DataflowGraph, TensorShape
+    g = DataflowGraph("scores")
+    q = g.add_input("q", TensorShape([128, 64]), dtype="bfloat16")
+    k = g.add_input("k", TensorShape([64, 256]), dtype="bfloat16")
+    g.add_output(g.softmax(g.matmul(q, k)))
+    Q = torch.randn(128, 64, device=DEV).to(torch.bfloat16)
+    K = (torch.randn(64, 256, device=DEV) / 8).to(torch.bfloat16)
+    ks = compile_graph(g, dtype="bfloat16")
+    ck = rt.compile(ks[0])
+    out = ck(Q, K)
+    torch.cuda.synchronize()
+    res = orc.evaluate(g, {"q": to_numpy(Q), "k": to_numpy(K)})
+    assert_close(as_f32(out), res[("f32", g.ops[g._outputs[0]].inputs[0])], "bfloat16", "scores")
+
+
+def test_wrong_inputs_raise(rt):
+    g = graphs.rmsnorm(4, 64)
+    ck = rt.compile(compile_graph(g)[0])
+    x = torch.randn(4, 64, device=DEV)
+    with pytest.raises(RuntimeError, match="takes 2 tensors"):
+        ck(x)
+    with pytest.raises(RuntimeError, match="CUDA tensors"):
+        ck(x.cpu(), torch.randn(64))
