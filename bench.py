@@ -45,6 +45,8 @@ def parse_args():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0)
+    p.add_argument("--soak", type=float, default=1.0, help="untimed seconds under load before timing")
+    p.add_argument("--no-graph", action="store_true", help="time eager launches, not a CUDA graph")
     return p.parse_args()
 
 
@@ -66,7 +68,7 @@ class ClockSampler:
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, bus_id: str):
-        self.bus_id = bus_id.lower()
+        self.bus_id = str(bus_id).lower()
         self.proc = None
         self.lines = []
         self.t = None
@@ -103,7 +105,7 @@ class ClockSampler:
             if len(parts) < 9:
                 continue
             bus = parts[0].lower()
-            if self.bus_id and not (bus.endswith(self.bus_id[-12:]) or self.bus_id.endswith(bus[-12:])):
+            if self.bus_id and bus[-7:] != self.bus_id[-7:]:      # "bb:dd.f"
                 continue
             try:
                 sms.append(float(parts[1]))
@@ -274,15 +276,36 @@ def run_molten(args, w):
         step(i)
     torch.cuda.synchronize(dev)
 
+    # The K timed steps are one CUDA graph holding exactly K launches, so the
+    # host's per-call Python cost is not inside the device timing.
+    graph = None
+    if flush is None and not args.no_graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(args.steps):
+                step(i)
+        torch.cuda.synchronize(dev)
+
     # ---- timed region (device time, max over ranks)
     bus = ""
     try:
-        bus = torch.cuda.get_device_properties(dev).pci_bus_id
+        pr = torch.cuda.get_device_properties(dev)
+        bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
     except Exception:
         pass
     clocks = ClockSampler(bus)
     clocks.start()
-    time.sleep(0.3)
+    # untimed soak (extra warm-up) so the clocks are sampled under load
+    soak_end = time.perf_counter() + args.soak
+    while time.perf_counter() < soak_end:
+        if graph is not None:
+            graph.replay()
+        else:
+            for i in range(min(args.steps, 20)):
+                if flush is not None:
+                    flush.zero_()
+                step(i)
+        torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
@@ -290,8 +313,11 @@ def run_molten(args, w):
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for i in range(args.steps):
-            step(i)
+        if graph is not None:
+            graph.replay()
+        else:
+            for i in range(args.steps):
+                step(i)
         e1.record(stream)
         torch.cuda.synchronize(dev)
         total_ms = e0.elapsed_time(e1)
@@ -388,6 +414,8 @@ def run_molten(args, w):
                   f"{sets} rotating input sets ({in_bytes * sets / 2**20:.0f} MiB > 2x L2)")
            if flush is None else "L2 flushed (256 MiB write) before every timed launch",
            "parallelism": f"dp{world}" if not is_gemm else f"n-shard{world}",
+           "timing": ("one CUDA graph replay of exactly K launches" if graph is not None
+                      else "eager launches") + f", CUDA events; {args.soak:.1f} s untimed soak",
            "kernel": gk.name, "tiles": {k: v for k, v in gk.plan.kernels[0].config.items()
                                         if k not in ("needed", "prefetch", "materialize")}}
     res = {"metric": metric, "value": world * work / (ms * 1e-3) / scale, "unit": unit,

@@ -91,8 +91,10 @@ def launch_records(plan: GroupPlan, name: str) -> list:
     for i, sk in enumerate(plan.kernels):
         c = sk.config
         rec = {"entry": kernel_entry(name, i, len(plan.kernels)), "family": sk.family}
-        if sk.family == "row":
-            rec.update(block=c["block"], rpc=c["rpc"], cl=c["cl"], smem=0)
+        if sk.family == "row" and c.get("engine") == "tma":
+            rec.update(engine="tma", block=32 * (c["nc"] + 1), stages=c["stages"], smem=c["smem"])
+        elif sk.family == "row":
+            rec.update(engine="regs", block=c["block"], rpc=c["rpc"], cl=c["cl"], smem=0)
         elif sk.family == "ew":
             rec.update(block=c["block"], rpc=c["rpc"], upt=c["upt"], tiles=c["tiles"], smem=0)
         else:
@@ -154,7 +156,7 @@ class CodeGenerator:
         return self.generate_from_plan(plan, name, graph, group)
 
     def generate_from_plan(self, plan: GroupPlan, name: str, graph=None, group=None):
-        from .emit import emit_ew, emit_row
+        from .emit import emit_ew, emit_row, emit_row_tma
         from .emit_gemm import emit_gemm
         chunks = []
         ops_txt = " -> ".join(graph.ops[i].op_type.name for i in group.op_ids) if graph else ""
@@ -166,7 +168,11 @@ class CodeGenerator:
         block_x, block_y, fam = 256, 1, "ew"
         for i, sk in enumerate(plan.kernels):
             entry = kernel_entry(name, i, len(plan.kernels))
-            if sk.family == "row":
+            if sk.family == "row" and sk.config.get("engine") == "tma":
+                chunks.append(emit_row_tma(sk, entry))
+                smem = max(smem, sk.config["smem"])
+                block_x = 32 * (sk.config["nc"] + 1)
+            elif sk.family == "row":
                 chunks.append(emit_row(sk, entry))
                 c = sk.config
                 smem = max(smem, 4)

@@ -112,6 +112,12 @@ __device__ __forceinline__ void pack_slot(Slot<T, VEC>& s, const float (&f)[VEC]
   }
 }
 
+// Clamp a 64-bit column limit into int range (limits outside [-1, 2^31-1]
+// mask every / no column of any row the kernels can address).
+__device__ __forceinline__ int clamp_col_limit(long long v) {
+  return v < -1 ? -1 : (v > 2147483647LL ? 2147483647 : (int)v);
+}
+
 template <typename T>
 __device__ __forceinline__ float load_scalar(const T* p) { return to_f32(p[0]); }
 

@@ -147,9 +147,9 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&r)[32]) {
 }
 
 // ------------------------------------------------------------ the engine
-template <int BM_, int BN_, int BK_, int STAGES_>
+template <int BM_, int BN_, int BK_, int STAGES_, int GROUP_M_ = 16>
 struct GemmLayout {
-  static constexpr int BM = BM_, BN = BN_, BK = BK_, STAGES = STAGES_;
+  static constexpr int BM = BM_, BN = BN_, BK = BK_, STAGES = STAGES_, GROUP_M = GROUP_M_;
   static_assert(BM == 128, "one CTA owns the 128 TMEM lanes");
   static_assert(BK == 64, "BK is one 128-byte swizzle row of 16-bit elements");
   static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be 64..256, a multiple of 64");
@@ -187,6 +187,22 @@ __device__ __forceinline__ GemmShared gemm_carve(uint8_t* raw) {
 }
 
 __device__ __forceinline__ int gemm_tid() { return threadIdx.y * blockDim.x + threadIdx.x; }
+
+// Output tile of persistent-loop index `tile`.  Tiles are walked in groups
+// of GROUP_M row blocks, column-major inside a group, so the CTAs running at
+// the same time share a GROUP_M-block panel of A and a few panels of B, which
+// stay in L2 instead of being re-read from HBM on every wave.
+template <class L>
+__device__ __forceinline__ void gemm_tile_coords(long long tile, long long MB, long long NB,
+                                                 int& m0, int& n0) {
+  const long long G = L::GROUP_M;
+  const long long span = G * NB;                       // tiles of a full group
+  const long long g = tile / span;
+  const long long r = tile - g * span;
+  const long long rows_g = (MB - g * G) < G ? (MB - g * G) : G;   // last group may be short
+  m0 = (int)((g * G + r % rows_g) * L::BM);
+  n0 = (int)((r / rows_g) * L::BN);
+}
 
 // barrier addresses
 template <class L> struct Bars {
@@ -245,7 +261,8 @@ __device__ __forceinline__ void gemm_roles(const GemmShared& s, const GemmArgs& 
       uint32_t st = 0, ph = 0;
       long long issued = 0;
       for (long long tile = blockIdx.x; tile < T && !*s.abort_flag; tile += gridDim.x) {
-        const int m0 = (int)((tile % MB) * L::BM), n0 = (int)((tile / MB) * L::BN);
+        int m0, n0;
+        gemm_tile_coords<L>(tile, MB, NB, m0, n0);
         for (int kb = 0; kb < KB; ++kb) {
           if (!mbar_wait(bar.empty(st), ph ^ 1u)) { gemm_fail(s, args, kGemmTimeoutEmpty); break; }
           if (*s.abort_flag) break;
@@ -315,8 +332,10 @@ __device__ __forceinline__ void gemm_roles(const GemmShared& s, const GemmArgs& 
         break;
       }
       tc_fence_after();
-      const long long row = (tile % MB) * L::BM + quarter * 32 + lane;
-      const long long nbase = (tile / MB) * L::BN;
+      int m0, n0;
+      gemm_tile_coords<L>(tile, MB, NB, m0, n0);
+      const long long row = (long long)m0 + quarter * 32 + lane;
+      const long long nbase = n0;
 #pragma unroll 1
       for (int c = 0; c < L::BN / 32; ++c) {
         float acc[32];

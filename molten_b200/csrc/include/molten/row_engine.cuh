@@ -133,6 +133,58 @@ struct RowTeam {
     }
   }
 
+  // (max, sum-of-exponentials) pair of one softmax row, combined across the
+  // team: (m1, s1) + (m2, s2) = (M, s1 e^(m1-M) + s2 e^(m2-M)), M = max.
+  // A side whose max is -inf (all its elements masked) contributes 0.
+  __device__ __forceinline__ static void softmax_combine(float& m, float& s, float m2, float s2) {
+    const float M = fmaxf(m, m2);
+    const float a = (m == -INFINITY) ? 0.0f : s * expf(m - M);
+    const float b = (m2 == -INFINITY) ? 0.0f : s2 * expf(m2 - M);
+    m = M;
+    s = a + b;
+  }
+
+  // All-reduce of one softmax (max, sum) pair per row, in the same three
+  // levels as `reduce` (uses 2 floats per warp / per CTA of `smem`).
+  __device__ __forceinline__ void reduce_softmax(float& m, float& s, float* smem, int pass) const {
+    constexpr int W = TPC < 32 ? TPC : 32;
+#pragma unroll
+    for (int off = W / 2; off > 0; off >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, off);
+      const float s2 = __shfl_xor_sync(0xffffffffu, s, off);
+      softmax_combine(m, s, m2, s2);
+    }
+    if constexpr (WPR > 1) {
+      const int warp = t / 32, lane = t % 32;
+      float* red = smem + team * WPR * 2;
+      if (lane == 0) {
+        red[warp * 2] = m;
+        red[warp * 2 + 1] = s;
+      }
+      __syncthreads();
+      float M = red[0], S = red[1];
+#pragma unroll
+      for (int w = 1; w < WPR; ++w) softmax_combine(M, S, red[w * 2], red[w * 2 + 1]);
+      m = M;
+      s = S;
+      __syncthreads();
+    }
+    if constexpr (CL > 1) {
+      float* part = smem + RPC * WPR * 2 + pass * RPC * 2 + team * 2;
+      if (t == 0) {
+        part[0] = m;
+        part[1] = s;
+      }
+      cluster_arrive();
+      cluster_wait();
+      float M = ld_dsmem(part, 0), S = ld_dsmem(part + 1, 0);
+#pragma unroll
+      for (int r = 1; r < CL; ++r) softmax_combine(M, S, ld_dsmem(part, r), ld_dsmem(part + 1, r));
+      m = M;
+      s = S;
+    }
+  }
+
   // A CTA of a cluster must not exit while a peer may still read its shared
   // memory: call once after the last `reduce`, before leaving the kernel.
   __device__ __forceinline__ void cluster_done_arrive() const {

@@ -107,9 +107,10 @@ int need_driver() {
   return MOLTEN_OK;
 }
 
-// Make `device` current on this thread and make sure its primary context
-// exists (the runtime creates it lazily).
-int use_device(int device) {
+// Make `device` current on this thread.  With init != 0 also make sure its
+// primary context exists (the runtime creates it lazily); launches pass 0 so
+// that nothing but the launch itself happens while a stream is captured.
+int use_device(int device, int init = 1) {
   int cur = -1;
   cudaError_t e = cudaGetDevice(&cur);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
@@ -117,8 +118,10 @@ int use_device(int device) {
     e = cudaSetDevice(device);
     if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
   }
-  e = cudaFree(nullptr);
-  if (e != cudaSuccess) return cuda_fail(e, "initialising the device context");
+  if (init) {
+    e = cudaFree(nullptr);
+    if (e != cudaSuccess) return cuda_fail(e, "initialising the device context");
+  }
   return MOLTEN_OK;
 }
 
@@ -270,7 +273,7 @@ int molten_launch(void* mod, const char* kernel, const molten_launch_cfg* cfg,
     return fail(MOLTEN_ERR_INVALID, std::string("kernel '") + kernel + "' takes a " +
                                         std::to_string(k->param_bytes) + "-byte parameter block, got " +
                                         std::to_string(params_bytes));
-  rc = use_device(m->device);
+  rc = use_device(m->device, 0);
   if (rc) return rc;
   if (cfg->smem_bytes > 48 * 1024 && (int)cfg->smem_bytes > k->smem_set) {
     std::lock_guard<std::mutex> lock(m->mu);

@@ -129,6 +129,8 @@ class _Emitter:
         if v.kind in ("row", "const"):
             return f"v{vid}"
         if vid in mat_ready:
+            if v.op == "softmax":
+                return f"(m{vid}[k][e] * sc{vid})"
             return f"m{vid}[k][e]"
         if v.op == "load":
             i = v.attrs["operand"]
@@ -147,7 +149,7 @@ class _Emitter:
             v = self.values[vid]
             if v.kind != "elem" or vid in mat_ready:
                 continue
-            if v.op in ("load", "acc"):
+            if v.op in ("load", "acc", "softmax"):
                 continue
             if v.op == "mask":
                 period = _mask_period(v, self.sk.cols)
@@ -199,7 +201,7 @@ class _Emitter:
             if v.op == "mask":
                 period = _mask_period(v, sk.cols)
                 off = int(v.attrs.get("offset", 0))
-                self.w(f"  const long long mlim{vid} = (grow % {period}LL) + ({off}LL);")
+                self.w(f"  const int mlim{vid} = clamp_col_limit((grow % {period}LL) + ({off}LL));")
 
 
 def emit_row(sk: SubKernel, name: str) -> str:
@@ -217,9 +219,14 @@ def emit_row(sk: SubKernel, name: str) -> str:
         v = values[vid]
         if v.op in ("rsum", "rmax", "rmin"):
             reds[v.avail - 1].append(vid)
+    smx = {p: [] for p in range(sk.passes)}
+    for vid in sorted(needed):
+        if values[vid].op == "softmax":
+            smx[values[vid].avail - 1].append(vid)
     # one exchange area per reduce call
     n_calls = sum(len({values[r].op for r in rs}) for rs in reds.values())
-    max_nr = max([len(rs) for rs in reds.values()], default=1) or 1
+    n_calls += sum(len(v) for v in smx.values())
+    max_nr = max([len(rs) for rs in reds.values()] + [2 if any(smx.values()) else 1]) or 1
 
     e.header("row")
     e.w("using namespace molten;")
@@ -271,13 +278,40 @@ def emit_row(sk: SubKernel, name: str) -> str:
         e.w(f"  float m{vid}[NV][VEC];")
     mat_ready = set()
     call = 0
+    EXP = "expf" if sk.precise else "__expf"
     for p in range(sk.passes):
         rs = reds[p]
-        e.w(f"  // ---- pass {p}: " + ", ".join(f"{values[r].op}(v{values[r].args[0]})" for r in rs))
+        e.w(f"  // ---- pass {p}: " + ", ".join(f"{values[r].op}(v{values[r].args[0]})"
+                                             for r in rs + smx[p]))
         for r in rs:
             e.w(f"  float v{r} = {_RED_INIT[values[r].op]};")
         targets = set(closures[p])
-        to_mat = {m for m, pm in materialize.items() if pm == p}
+        to_mat = {m for m, pm in materialize.items() if pm == p and values[m].op != "softmax"}
+        if smx[p]:
+            # online softmax, step 1: this thread's max of each softmax input
+            xs_targets = set()
+            for v in smx[p]:
+                xs_targets |= _closure_within(values, values[v].args[0], targets)
+            for v in smx[p]:
+                e.w(f"  float lm{v} = (-INFINITY), ls{v} = 0.0f;")
+            e.w("#pragma unroll")
+            e.w("  for (int k = 0; k < NV; ++k) {")
+            e.w("    const long long j = tm.slot(k);")
+            e.w("    if (!(rok && j < NVEC)) continue;")
+            _emit_nonprefetched_loads(e, xs_targets, prefetch, "    ")
+            e.w("#pragma unroll")
+            e.w("    for (int e = 0; e < VEC; ++e) {")
+            if any(values[t].op == "mask" for t in xs_targets):
+                e.w("      const int col = (int)(j * VEC) + e;")
+            for st in e.elem_statements(xs_targets, prefetch, mat_ready, "      "):
+                e.w(st)
+            for v in smx[p]:
+                x = e.leaf(values[v].args[0], True, prefetch, mat_ready, set())
+                e.w(f"      lm{v} = fmaxf(lm{v}, {x});")
+            e.w("    }")
+            e.w("  }")
+            for v in smx[p]:
+                e.w(f"  const float lz{v} = (lm{v} == (-INFINITY)) ? 0.0f : lm{v};")
         e.w("#pragma unroll")
         e.w("  for (int k = 0; k < NV; ++k) {")
         e.w("    const long long j = tm.slot(k);")
@@ -286,17 +320,29 @@ def emit_row(sk: SubKernel, name: str) -> str:
         e.w("#pragma unroll")
         e.w("    for (int e = 0; e < VEC; ++e) {")
         if any(values[t].op == "mask" for t in targets):
-            e.w("      const long long col = j * VEC + e;")
+            e.w("      const int col = (int)(j * VEC) + e;")
         for st in e.elem_statements(targets, prefetch, mat_ready, "      "):
             e.w(st)
         for m in sorted(to_mat):
             e.w(f"      m{m}[k][e] = v{m};")
+        for v in smx[p]:
+            # step 2: exponentials relative to the thread's max, kept in registers
+            x = e.leaf(values[v].args[0], True, prefetch, mat_ready, set())
+            e.w(f"      {{ const float ev = {EXP}({x} - lz{v}); m{v}[k][e] = ev; ls{v} += ev; }}")
         for r in rs:
             x = e.leaf(values[r].args[0], True, prefetch, mat_ready, set())
             e.w("      " + _RED_COMBINE[values[r].op].format(a=f"v{r}", x=x))
         e.w("    }")
         e.w("  }")
         mat_ready |= to_mat
+        for v in smx[p]:
+            # step 3: one pair reduction per row; scale = e^(m_thread - M) / S
+            e.w(f"  float gm{v} = lm{v}, gs{v} = ls{v};")
+            e.w(f"  tm.reduce_softmax(gm{v}, gs{v}, red_smem, {call});")
+            e.w(f"  const float sc{v} = (gs{v} > 0.0f) ? ((lm{v} == (-INFINITY)) ? 0.0f : "
+                f"expf(lm{v} - gm{v}) / gs{v}) : NAN;")
+            call += 1
+            mat_ready.add(v)
         by_op = {}
         for r in rs:
             by_op.setdefault(values[r].op, []).append(r)
@@ -326,7 +372,7 @@ def emit_row(sk: SubKernel, name: str) -> str:
         e.w("#pragma unroll")
         e.w("    for (int e = 0; e < VEC; ++e) {")
         if any(values[t].op == "mask" for t in fin):
-            e.w("      const long long col = j * VEC + e;")
+            e.w("      const int col = (int)(j * VEC) + e;")
         for st in e.elem_statements(fin, prefetch, mat_ready, "      "):
             e.w(st)
         for o in full_outs:
@@ -437,7 +483,7 @@ def emit_ew(sk: SubKernel, name: str) -> str:
         if v.op == "mask":
             period = _mask_period(v, sk.cols)
             off = int(v.attrs.get("offset", 0))
-            e.w(f"      const long long mlim{vid} = (grow % {period}LL) + ({off}LL);")
+            e.w(f"      const int mlim{vid} = clamp_col_limit((grow % {period}LL) + ({off}LL));")
     for vid in sorted(needed):
         v = values[vid]
         if v.kind in ("row", "const") and v.op not in ("load", "const"):
@@ -452,7 +498,7 @@ def emit_ew(sk: SubKernel, name: str) -> str:
     e.w("#pragma unroll")
     e.w("        for (int e = 0; e < VEC; ++e) {")
     if any(values[t].op == "mask" for t in needed):
-        e.w("          const long long col = j * VEC + e;")
+        e.w("          const int col = (int)(j * VEC) + e;")
     for vid in sorted(needed):
         v = values[vid]
         if v.kind != "elem" or v.op in ("load",):
@@ -487,3 +533,253 @@ def _ew_leaf(e: _Emitter, vid: int) -> str:
             return f"to_f32(c{o.index}[k].v[e])"
         return f"to_f32(s{o.index}[u][k].v[e])"
     return f"v{vid}"
+
+
+def emit_row_tma(sk: SubKernel, name: str) -> str:
+    """Row kernel on the TMA-staged engine (molten/row_tma.cuh): rows of the
+    row-indexed operands stream through a shared-memory ring; one consumer
+    warp per row; reductions are warp shuffles."""
+    cfg = sk.config
+    VEC, NV, NC, ST = cfg["vec"], cfg["nv"], cfg["nc"], cfg["stages"]
+    staged = list(cfg["staged"])                   # operand indices, stage order
+    offs = dict(zip(staged, cfg["stage_offsets"]))
+    values = sk.values
+    needed = set(cfg["needed"])
+    materialize = {int(v): int(p) for v, p in cfg["materialize"]}
+    closures = pass_closures(values, sk, needed, materialize)
+    reds = {p: [] for p in range(sk.passes)}
+    for vid in sorted(needed):
+        v = values[vid]
+        if v.op in ("rsum", "rmax", "rmin"):
+            reds[v.avail - 1].append(vid)
+    L = []
+    w = L.append
+    w(f"// Molten sm_100a TMA-staged row kernel: {name}")
+    w(f"// cols = {sk.cols}; inputs: " + ", ".join(
+        f"{o.name}[{o.dtype} {o.last}/{o.row_map}]" for o in sk.operands))
+    w("#include \"molten/row_tma.cuh\"")
+    w("")
+    w("using namespace molten;")
+    w("")
+    w(f"extern \"C\" __global__ void __launch_bounds__({32 * (NC + 1)}, 1) "
+      f"{name}(const __grid_constant__ RowArgs args) {{")
+    w(f"  constexpr int VEC = {VEC}, NV = {NV}, NC = {NC}, STAGES = {ST}, "
+      f"STAGE_BYTES = {cfg['stage_bytes']};")
+    w(f"  constexpr long long COLS = {sk.cols}LL, NVEC = {cfg['nvec']}LL;")
+    w(f"  constexpr uint32_t ROW_BYTES = {cfg['row_bytes']}u;")
+    w("  extern __shared__ __align__(128) uint8_t smem_raw[];")
+    w("  const auto ring = row_ring_carve<STAGES, STAGE_BYTES>(smem_raw);")
+    w("  row_ring_init(ring);")
+    w("  __syncthreads();")
+    w("  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;")
+    w("  const long long G = gridDim.x;")
+    w("  const long long nloc = args.rows > (long long)blockIdx.x ? "
+      "(args.rows - 1 - blockIdx.x) / G + 1 : 0;")
+    w("  if (warp == 0) {")
+    w("    if (lane == 0) {")
+    w("      long long issued = 0;")
+    w("      for (long long j = 0; j < nloc && !*ring.abort_flag; ++j) {")
+    w("        const int s = (int)(j % STAGES);")
+    w("        const uint32_t ph = (uint32_t)((j / STAGES) & 1);")
+    w("        if (!mbar_wait(ring.empty(s), ph ^ 1u)) {")
+    w("          row_ring_fail(ring.abort_flag, args.status, kRowTimeoutEmpty);")
+    w("          break;")
+    w("        }")
+    w("        const long long lrow = (long long)blockIdx.x + j * G;")
+    w("        const long long grow = args.row_offset + lrow;")
+    w("        (void)grow;")
+    w("        mbar_expect_tx(ring.full(s), ROW_BYTES);")
+    for i in staged:
+        o = sk.operands[i]
+        ct = _ctype(o.dtype)
+        idx = _row_index_expr(o, "lrow", "grow")
+        w(f"        bulk_g2s(ring.stage(s) + {offs[i]}u, "
+          f"static_cast<const {ct}*>(args.in[{i}]) + {idx} * COLS, "
+          f"{sk.cols * DTYPE_SIZE_OF[o.dtype]}u, ring.full(s));")
+    w("        ++issued;")
+    w("      }")
+    w("      if (*ring.abort_flag) {")
+    w("        for (long long i = issued - 1; i >= 0 && i >= issued - STAGES; --i) {")
+    w("          if (!mbar_wait(ring.full((int)(i % STAGES)), (uint32_t)((i / STAGES) & 1)) && args.status)")
+    w("            atomicOr(args.status, kRowTimeoutDrain);")
+    w("        }")
+    w("      }")
+    w("    }")
+    w("  } else {")
+    w("    for (long long j = warp - 1; j < nloc; j += NC) {")
+    w("      const int s = (int)(j % STAGES);")
+    w("      const bool got = mbar_wait(ring.full(s), (uint32_t)((j / STAGES) & 1));")
+    w("      if (!__all_sync(0xffffffffu, got ? 1 : 0)) {")
+    w("        if (lane == 0) row_ring_fail(ring.abort_flag, args.status, kRowTimeoutFull);")
+    w("        break;")
+    w("      }")
+    w("      const uint32_t sb = ring.stage(s);")
+    w("      (void)sb;")
+    w("      const long long lrow = (long long)blockIdx.x + j * G;")
+    w("      const long long grow = args.row_offset + lrow;")
+    w("      (void)grow;")
+    # non-staged operand pointers and outputs
+    for o in sk.operands:
+        if o.index in staged:
+            continue
+        ct = _ctype(o.dtype)
+        idx = _row_index_expr(o, "lrow", "grow")
+        stride = "COLS" if o.last == "vec" else "1LL"
+        w(f"      const {ct}* __restrict__ in{o.index} = static_cast<const {ct}*>(args.in[{o.index}]) "
+          f"+ {idx} * {stride};")
+    for out in sk.outputs:
+        ct = _ctype(out.dtype)
+        stride = "COLS" if out.kind == "full" else "1LL"
+        w(f"      {ct}* __restrict__ out{out.index} = static_cast<{ct}*>(args.out[{out.index}]) "
+          f"+ lrow * {stride};")
+    for vid in sorted(needed):
+        v = values[vid]
+        if v.op == "load" and v.kind == "row":
+            w(f"      const float v{vid} = load_scalar(in{v.attrs['operand']});")
+        if v.op == "mask":
+            period = _mask_period(v, sk.cols)
+            off = int(v.attrs.get("offset", 0))
+            w(f"      const int mlim{vid} = clamp_col_limit((grow % {period}LL) + ({off}LL));")
+    emitted = set()
+
+    def rows_at(p):
+        for vid in sorted(needed):
+            v = values[vid]
+            if v.kind in ("row", "const") and v.avail == p and vid not in emitted \
+                    and v.op not in ("load", "const", "rsum", "rmax", "rmin"):
+                args = [_tma_leaf(sk, a, staged, set()) for a in v.args]
+                w(f"      const float v{vid} = {value_expr(v, args, True)};")
+                emitted.add(vid)
+
+    rows_at(0)
+    for vid in sorted(materialize):
+        w(f"      float m{vid}[NV][VEC];")
+    mat_ready = set()
+
+    def slot_loop(targets, body_extra, tail=None, outs=()):
+        w("#pragma unroll")
+        w("      for (int k = 0; k < NV; ++k) {")
+        w("        const long long j = lane + 32LL * k;")
+        w("        if (j >= NVEC) break;")
+        used_staged, used_glob = set(), set()
+        for t in targets:
+            vt = values[t]
+            for x in [t] + list(vt.args):
+                vx = values[x]
+                if vx.op == "load" and vx.kind == "elem" and x not in mat_ready:
+                    (used_staged if vx.attrs["operand"] in staged else used_glob).add(vx.attrs["operand"])
+        for i in sorted(used_staged):
+            o = sk.operands[i]
+            ct = _ctype(o.dtype)
+            off = offs[i]
+            w(f"        const Slot<{ct}, VEC> st{i} = lds_slot<{ct}, VEC>(sb + {off}u + "
+              f"(uint32_t)(j * (VEC * {DTYPE_SIZE_OF[o.dtype]})));")
+        for i in sorted(used_glob):
+            o = sk.operands[i]
+            ct = _ctype(o.dtype)
+            w(f"        const Slot<{ct}, VEC> sl{i} = load_slot<kLoadDefault, {ct}, VEC>(in{i} + j * VEC);")
+        for o in outs:
+            w(f"        float f{o.index}[VEC];")
+        w("#pragma unroll")
+        w("        for (int e = 0; e < VEC; ++e) {")
+        if any(values[t].op == "mask" for t in targets):
+            w("          const int col = (int)(j * VEC) + e;")
+        for vid in sorted(targets):
+            v = values[vid]
+            if v.kind != "elem" or vid in mat_ready or v.op == "load":
+                continue
+            if v.op == "mask":
+                w(f"          const float v{vid} = (col > mlim{vid}) ? (-INFINITY) : 0.0f;")
+                continue
+            args = [_tma_leaf(sk, a, staged, mat_ready) for a in v.args]
+            w(f"          const float v{vid} = {value_expr(v, args, sk.precise)};")
+        body_extra()
+        w("        }")
+        if tail:
+            tail()
+        w("      }")
+
+    for p in range(sk.passes):
+        rs = reds[p]
+        for r in rs:
+            w(f"      float v{r} = {_RED_INIT[values[r].op]};")
+        targets = set(closures[p])
+        to_mat = {m for m, pm in materialize.items() if pm == p}
+
+        def extra(rs=rs, to_mat=to_mat):
+            for m in sorted(to_mat):
+                w(f"          m{m}[k][e] = v{m};")
+            for r in rs:
+                x = _tma_leaf(sk, values[r].args[0], staged, mat_ready)
+                w("          " + _RED_COMBINE[values[r].op].format(a=f"v{r}", x=x))
+
+        slot_loop(targets, extra)
+        mat_ready |= to_mat
+        by_op = {}
+        for r in rs:
+            by_op.setdefault(values[r].op, []).append(r)
+        for op, grp in by_op.items():
+            fn = {"rsum": "warp_allreduce_sum", "rmax": "warp_allreduce_max",
+                  "rmin": "warp_allreduce_min"}[op]
+            w("      {")
+            w(f"        float red[{len(grp)}] = {{" + ", ".join(f"v{r}" for r in grp) + "};")
+            w(f"        {fn}<{len(grp)}>(red);")
+            for i, r in enumerate(grp):
+                w(f"        v{r} = red[{i}];")
+            w("      }")
+        rows_at(p + 1)
+    fin = set(closures[sk.passes])
+    full_outs = [o for o in sk.outputs if o.kind == "full"]
+
+    def fin_extra():
+        for o in full_outs:
+            w(f"          f{o.index}[e] = {_tma_leaf(sk, sk.out_values[o.index], staged, mat_ready)};")
+
+    def fin_tail():
+        for o in full_outs:
+            ct = _ctype(o.dtype)
+            w(f"        Slot<{ct}, VEC> o{o.index}; pack_slot<{ct}, VEC>(o{o.index}, f{o.index});")
+            w(f"        store_slot<kStoreDefault, {ct}, VEC>(out{o.index} + j * VEC, o{o.index});")
+
+    if full_outs:
+        slot_loop(fin, fin_extra, fin_tail, full_outs)
+    for o in sk.outputs:
+        if o.kind == "row":
+            w(f"      if (lane == 0) store_scalar(out{o.index}, "
+              f"{_tma_leaf(sk, sk.out_values[o.index], staged, mat_ready)});")
+    w("      __syncwarp();")
+    w("      if (lane == 0) mbar_arrive(ring.empty(s));")
+    w("      if (__any_sync(0xffffffffu, *ring.abort_flag ? 1 : 0)) break;")
+    w("    }")
+    w("  }")
+    w("}")
+    return "\n".join(L) + "\n"
+
+
+DTYPE_SIZE_OF = {"float32": 4, "bfloat16": 2, "float16": 2}
+
+
+def _tma_leaf(sk: SubKernel, vid: int, staged, mat_ready) -> str:
+    v = sk.values[vid]
+    if v.kind == "const" and v.op == "const":
+        return c_float(v.attrs["value"])
+    if v.kind in ("row", "const"):
+        return f"v{vid}"
+    if vid in mat_ready:
+        return f"m{vid}[k][e]"
+    if v.op == "load":
+        i = v.attrs["operand"]
+        return f"to_f32(st{i}.v[e])" if i in staged else f"to_f32(sl{i}.v[e])"
+    return f"v{vid}"
+
+
+def _closure_within(values, root, allowed) -> set:
+    """Elem values among ``allowed`` that ``root`` depends on (inclusive)."""
+    out, stack = set(), [root]
+    while stack:
+        v = stack.pop()
+        if v in out or v not in allowed:
+            continue
+        out.add(v)
+        stack.extend(values[v].args)
+    return out

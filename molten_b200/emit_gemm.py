@@ -31,7 +31,7 @@ def emit_gemm(sk: SubKernel, name: str) -> str:
     w("")
     w("namespace {")
     w(f"constexpr int TILE_M = {BM}, TILE_N = {BN}, TILE_K = {BK}, STAGES = {ST};")
-    w(f"typedef GemmLayout<TILE_M, TILE_N, TILE_K, STAGES> Layout_{name};")
+    w(f"typedef GemmLayout<TILE_M, TILE_N, TILE_K, STAGES, {cfg.get('group_m', 16)}> Layout_{name};")
     w(f"struct Epilogue_{name} {{")
     w("  // C[row, col0 .. col0 + 31] from the fp32 accumulators of one TMEM row")
     w("  __device__ __forceinline__ static void apply(const GemmArgs& args, long long row,")
@@ -51,7 +51,7 @@ def emit_gemm(sk: SubKernel, name: str) -> str:
         if v.op == "mask":
             period = _mask_period(v, sk.n)
             off = int(v.attrs.get("offset", 0))
-            w(f"    const long long mlim{vid} = (grow % {period}LL) + ({off}LL);")
+            w(f"    const int mlim{vid} = clamp_col_limit((grow % {period}LL) + ({off}LL));")
     for vid in sorted(needed):
         v = values[vid]
         if v.kind in ("row", "const") and v.op not in ("load", "const"):
@@ -74,7 +74,7 @@ def emit_gemm(sk: SubKernel, name: str) -> str:
     w("#pragma unroll")
     w("      for (int e = 0; e < 8; ++e) {")
     if any(values[v].op == "mask" for v in needed):
-        w("        const long long col = c + e;")
+        w("        const int col = (int)c + e;")
     for vid in sorted(needed):
         v = values[vid]
         if v.kind != "elem" or v.op in ("load", "acc"):

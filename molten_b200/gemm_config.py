@@ -35,5 +35,6 @@ def choose_gemm_config(sk, override: dict) -> dict:
     smem = stages * stage_bytes + (2 * stages + 5) * 8 + 16 + 1024
     if smem > 232448:
         raise ValueError(f"GEMM tile needs {smem} bytes of shared memory")
-    return {"bm": bm, "bn": bn, "bk": bk, "stages": stages,
+    group_m = o.get("group_m", 16)
+    return {"bm": bm, "bn": bn, "bk": bk, "stages": stages, "group_m": group_m,
             "epi_warps": 4, "threads": 256, "smem_bytes": smem}

@@ -359,6 +359,10 @@ class _DagBuilder:
         return self.add("row", op, (a,), avail=v.avail + 1)
 
 
+def acc_op_present(b) -> bool:
+    return any(v.op == "acc" for v in b.values)
+
+
 def build_dag(graph: DataflowGraph, op_ids: list, operands: list, cols: int,
               acc_op: Optional[int] = None):
     """Translate graph ops into a Value DAG.  Returns (values, env)."""
@@ -402,10 +406,15 @@ def build_dag(graph: DataflowGraph, op_ids: list, operands: list, cols: int,
             env[oid] = b.unary(_UNARY[t], args[0], attrs)
         elif t == OpType.SOFTMAX:
             x = args[0]
-            mx = b.reduce("rmax", x)
-            e = b.unary("exp", b.binary("sub", x, mx))
-            s = b.reduce("rsum", e)
-            env[oid] = b.binary("mul", e, b.unary("rcp", s))
+            if b.values[x].kind == "elem" and not acc_op_present(b):
+                # one-round online softmax: computed in the pass of x, usable
+                # from the next one (the row engine keeps e = exp(x - m_thread))
+                env[oid] = b.add("elem", "softmax", (x,), avail=b.values[x].avail + 1)
+            else:
+                mx = b.reduce("rmax", x)
+                e = b.unary("exp", b.binary("sub", x, mx))
+                s = b.reduce("rsum", e)
+                env[oid] = b.binary("mul", e, b.unary("rcp", s))
         elif t == OpType.SUM:
             env[oid] = b.reduce("rsum", args[0])
         elif t == OpType.MEAN:
@@ -508,10 +517,74 @@ def choose_ew_config(sk: SubKernel, override: Optional[dict] = None) -> dict:
     else:
         tpc = 128 if nvec >= 128 else max(1, 1 << (max(nvec, 1) - 1).bit_length())
         tpc = min(tpc, 128)
-    nv = o.get("nv") or max(1, min(2, -(-nvec // tpc)))
+    nv = o.get("nv") or 1
     rpc = o.get("rpc") or max(1, 256 // tpc)
     if (tpc * rpc) % 32:
         rpc = max(rpc, 32 // tpc)
     upt = o.get("upt") or 4
     return {"vec": vec, "nvec": nvec, "tpc": tpc, "nv": nv, "rpc": rpc, "upt": upt,
             "block": tpc * rpc, "tiles": -(-nvec // (tpc * nv))}
+
+
+SMEM_RING_BUDGET = 200 * 1024
+
+
+def choose_row_tma_config(sk: SubKernel, prefetch: set, materialize: dict,
+                          override: Optional[dict] = None):
+    """Config of the TMA-staged row engine, or None when it does not apply.
+
+    Staged operands are the row-indexed ones (``prefetch``); a stage holds one
+    row of each, every part 128-byte aligned.  The engine needs whole 16-byte
+    slots and at least 8 stages in the shared-memory budget.
+    """
+    o = dict(override or {})
+    # opt-in only (the register engine measured faster on every benchmark
+    # row); never under a vec override, which the runtime uses for inputs
+    # that are not 16-byte aligned -- bulk copies need 16-byte alignment
+    if o.get("engine") != "tma" or "vec" in o or not prefetch:
+        return None
+    if any(v.op == "softmax" for v in sk.values):
+        return None
+    staged = sorted(prefetch)
+    sizes = [DTYPE_SIZE[sk.operands[i].dtype] for i in staged]
+    sizes += [DTYPE_SIZE[x.dtype] for x in sk.operands if x.last == "vec"]
+    sizes += [DTYPE_SIZE[x.dtype] for x in sk.outputs if x.kind == "full"]
+    vec = 16 // min(sizes)
+    if sk.cols % vec:
+        return None
+    offsets, off = [], 0
+    for i in staged:
+        offsets.append(off)
+        off += -(-(sk.cols * DTYPE_SIZE[sk.operands[i].dtype]) // 128) * 128
+    stage_bytes = off
+    s_max = o.get("stages") or min(32, SMEM_RING_BUDGET // stage_bytes)
+    if s_max < o.get("min_stages", 8) and o.get("engine") != "tma":
+        return None
+    # Stage s is always consumed by warp s % NC, which needs STAGES % NC == 0:
+    # a warp then meets the stages it owns in order and can never wait on a
+    # phase two ahead of the one in flight (mbarrier parity would alias).
+    best = None
+    for min_nc in ((o["nc"],) if "nc" in o else (6, 2)):
+        for st in range(max(2, s_max), 1, -1):
+            for nc in ([o["nc"]] if "nc" in o else range(10, min_nc - 1, -1)):
+                if st % nc == 0:
+                    best = (st, nc)
+                    break
+            if best:
+                break
+        if best:
+            break
+    if best is None:
+        return None
+    stages, nc = best
+    nvec = sk.cols // vec
+    nv = -(-nvec // 32)
+    mat = dict(materialize)
+    if nv * vec * len(mat) > 64:
+        mat = {}                     # recompute instead of holding in registers
+    return {"engine": "tma", "vec": vec, "nvec": nvec, "nv": nv, "nc": nc,
+            "stages": stages, "stage_bytes": stage_bytes, "staged": staged,
+            "stage_offsets": offsets,
+            "row_bytes": sum(sk.cols * DTYPE_SIZE[sk.operands[i].dtype] for i in staged),
+            "smem": stages * stage_bytes + 2 * stages * 8 + 16 + 128,
+            "materialize": sorted(mat.items()), "prefetch": staged, "cl": 1}

@@ -8,7 +8,7 @@ from .ir import DataflowGraph, OpType, TensorShape
 from .lowering import (
     DTYPE_SIZE, GroupPlan, LoweringError, Operand, OutputSpec, SubKernel,
     broadcast_shapes, build_dag, canon_dtype, choose_ew_config,
-    choose_row_config, classify_operand, group_boundary, infer_shapes,
+    choose_row_config, choose_row_tma_config, classify_operand, group_boundary, infer_shapes,
     is_mask_const, prod, promote, split_group, EXPENSIVE,
 )
 
@@ -68,6 +68,12 @@ def plan_group(graph: DataflowGraph, group_op_ids, input_shapes: dict,
     dts = _op_dtypes(graph, ordered, dts)
 
     parts = split_group(graph, ordered)
+    # intermediates between the sub-kernels of one group are stored in fp32,
+    # so a split group still rounds once (at its outputs); a MATMUL operand
+    # keeps its 16-bit type because the tensor cores read it
+    mm_operands = {i for o in ordered if graph.ops[o].op_type == OpType.MATMUL
+                   for i in graph.ops[o].inputs}
+    storage = dict(dts)
     produced_by = {}
     for k, (_, ops) in enumerate(parts):
         for o in ops:
@@ -90,8 +96,10 @@ def plan_group(graph: DataflowGraph, group_op_ids, input_shapes: dict,
         sk_outs = [o for o in ops if o in out_set or o in later]
         for o in sk_outs:
             if o not in out_set:
-                temps[o] = (shapes[o], dts[o])
-        kernels.append(_plan_sub(graph, family, ops, sk_ext, sk_outs, shapes, dts, tune))
+                if o not in mm_operands:
+                    storage[o] = "float32"
+                temps[o] = (shapes[o], storage[o])
+        kernels.append(_plan_sub(graph, family, ops, sk_ext, sk_outs, shapes, storage, tune))
 
     return GroupPlan(
         name=name, inputs=inputs,
@@ -151,9 +159,14 @@ def _plan_sub(graph, family, ops, ext, outs, shapes, dts, tune) -> SubKernel:
     override = tune.get(key) or {}
     if sk.family == "row":
         prefetch, materialize = _row_storage(sk, needed)
-        sk.config = choose_row_config(sk, prefetch, materialize, override)
-        sk.config["prefetch"] = sorted(prefetch)
-        sk.config["materialize"] = sorted(materialize.items())
+        tma = choose_row_tma_config(sk, prefetch, materialize, override)
+        if tma is not None:
+            sk.config = tma
+        else:
+            sk.config = choose_row_config(sk, prefetch, materialize, override)
+            sk.config["engine"] = "regs"
+            sk.config["prefetch"] = sorted(prefetch)
+            sk.config["materialize"] = sorted(materialize.items())
     else:
         sk.config = choose_ew_config(sk, override)
     sk.config["needed"] = sorted(needed)
@@ -183,7 +196,7 @@ def pass_closures(values, sk: SubKernel, needed: set, materialized: dict):
     roots = {p: [] for p in range(sk.passes + 1)}
     for v in needed:
         val = values[v]
-        if val.op in ("rsum", "rmax", "rmin"):
+        if val.op in ("rsum", "rmax", "rmin", "softmax"):
             roots[val.avail - 1].append(val.args[0])
     roots[sk.passes] += [v for v in sk.out_values if values[v].kind == "elem"]
     closures = {}
@@ -203,17 +216,19 @@ def pass_closures(values, sk: SubKernel, needed: set, materialized: dict):
 
 def _row_storage(sk: SubKernel, needed: set):
     values = sk.values
-    naive = pass_closures(values, sk, needed, {})
+    # a softmax keeps its exponentials in registers from the pass of its input
+    soft = {v: values[v].avail - 1 for v in needed if values[v].op == "softmax"}
+    naive = pass_closures(values, sk, needed, soft)
     first = {}
     uses = {}
     for p in sorted(naive):
         for v in naive[p]:
             first.setdefault(v, p)
             uses.setdefault(v, set()).add(p)
-    materialize = {}
+    materialize = dict(soft)
     for v, ps in uses.items():
         val = values[v]
-        if val.op in EXPENSIVE and max(ps) > first[v]:
+        if val.op in EXPENSIVE and max(ps) > first[v] and v not in materialize:
             materialize[v] = first[v]
     prefetch = set()
     for opd in sk.operands:

@@ -72,6 +72,7 @@ class _Spec:
         self.temp_specs = {k: (tuple(s), _torch_dtype(d)) for k, (s, d) in self.plan.temps.items()}
         self._cfgs: dict = {}
         self._tmaps: OrderedDict = OrderedDict()
+        self.align = [_alignment_rules(sk) for sk in self.plan.kernels]
 
     def module(self, device: int) -> _capi.Module:
         m = self.modules.get(device)
@@ -91,7 +92,14 @@ class _Spec:
         sk = self.plan.kernels[i]
         c = sk.config
         cfg = _capi.LaunchCfg()
-        if sk.family == "row":
+        if sk.family == "row" and c.get("engine") == "tma":
+            torch = _torch()
+            sms = torch.cuda.get_device_properties(device).multi_processor_count
+            cfg.grid[:] = [max(1, min(sk.rows, sms)), 1, 1]
+            cfg.block[:] = [32 * (c["nc"] + 1), 1, 1]
+            cfg.cluster[:] = [1, 1, 1]
+            cfg.smem_bytes = c["smem"]
+        elif sk.family == "row":
             grid = (-(-sk.rows // c["rpc"])) * c["cl"]
             cfg.grid[:] = [max(1, grid), 1, 1]
             cfg.block[:] = [c["block"], 1, 1]
@@ -158,13 +166,48 @@ class _Spec:
             else:
                 a = _capi.RowArgs()
                 a.rows, a.cols = sk.rows, sk.cols
+                if sk.config.get("engine") == "tma":
+                    a.status = _capi.status_word(di)
             a.row_offset = row_offset
-            for opd in sk.operands:
-                a.inp[opd.index] = env[opd.op_id].data_ptr()
-            for o in sk.outputs:
-                a.out[o.index] = env[o.op_id].data_ptr()
+            ins_al, outs_al = self.align[i]
+            for opd, al in zip(sk.operands, ins_al):
+                p = env[opd.op_id].data_ptr()
+                if p % al:
+                    raise _capi.MoltenError(f"input {opd.name!r} at {p:#x} is not {al}-byte aligned "
+                                            f"as kernel {self.entries[i].decode()} requires")
+                a.inp[opd.index] = p
+            for o, al in zip(sk.outputs, outs_al):
+                p = env[o.op_id].data_ptr()
+                if p % al:
+                    raise _capi.MoltenError(f"output at {p:#x} is not {al}-byte aligned "
+                                            f"as kernel {self.entries[i].decode()} requires")
+                a.out[o.index] = p
             mod.launch(self.entries[i], cfg, a, stream)
         return outs
+
+
+def _alignment_rules(sk):
+    """Byte alignment each input / output pointer of a sub-kernel needs:
+    16 for TMA sources and for 16-byte vector slots, the slot size for
+    narrower slots, the element size for per-row scalars."""
+    c = sk.config
+    if sk.family == "gemm":
+        ins = [16 if o.last == "vec" else DTYPE_SIZE[o.dtype] for o in sk.operands]
+        return ins, [16 for _ in sk.outputs]
+    vec = c.get("vec", 1)
+    staged = set(c.get("staged", ())) if c.get("engine") == "tma" else set()
+    ins = []
+    for o in sk.operands:
+        esz = DTYPE_SIZE[o.dtype]
+        if o.index in staged:
+            ins.append(16)
+        elif o.last == "vec":
+            ins.append(min(16, vec * esz))
+        else:
+            ins.append(esz)
+    outs = [min(16, vec * DTYPE_SIZE[o.dtype]) if o.kind == "full" else DTYPE_SIZE[o.dtype]
+            for o in sk.outputs]
+    return ins, outs
 
 
 @dataclass

@@ -151,3 +151,20 @@ def make_inputs(w: Workload, seed: int = 0, device="cpu") -> list:
         bias = normal((n,), 0.0, 0.02)
         return [A, B, bias]
     raise KeyError(w.kind)
+
+
+def input_shapes(w: Workload) -> list:
+    """Shapes of ``make_inputs(w)`` without allocating anything."""
+    p = w.params
+    if w.kind == "rmsnorm":
+        return [(p["rows"], p["cols"]), (p["cols"],)]
+    if w.kind == "rmsnorm_silu_gate":
+        return [(p["rows"], p["cols"]), (p["cols"],), (p["rows"], p["cols"])]
+    if w.kind == "softmax":
+        return [tuple(p["shape"])]
+    if w.kind == "chain":
+        r, c = p["rows"], p["cols"]
+        return [(r, c), (r, c), (c,), (c,), (c,)]
+    if w.kind == "gemm_bias_gelu":
+        return [(p["m"], p["k"]), (p["k"], p["n"]), (p["n"],)]
+    raise KeyError(w.kind)

@@ -154,3 +154,21 @@ def test_every_pattern_compiles_for_sm100a(tmp_path):
         cubins = list(ex.map(lambda it: build_cubin(it[1].source, it[1].name, tmp_path), items))
     for c in cubins:
         assert c.exists() and c.stat().st_size > 1000
+
+
+def test_alignment_rules():
+    from molten_b200.runtime import _alignment_rules
+    g = graphs.rmsnorm_silu_gate(4, 64, dtype="bfloat16")
+    grp = FusionEngine().fuse(g)[0]
+    shapes = {0: (4, 64), 1: (64,), 2: (4, 64)}
+    dts = {i: "bfloat16" for i in shapes}
+    sk = CodeGenerator().generate(g, grp, shapes, dts).plan.kernels[0]
+    assert _alignment_rules(sk) == ([16, 16, 16], [16])
+    sk = CodeGenerator(tune={"row": {"vec": 1}}).generate(g, grp, shapes, dts).plan.kernels[0]
+    assert _alignment_rules(sk) == ([2, 2, 2], [2])
+    # the TMA ring engine is opt-in and never used with a vec override
+    sk = CodeGenerator(tune={"row": {"engine": "tma", "vec": 1}}).generate(g, grp, shapes, dts)
+    assert sk.plan.kernels[0].config["engine"] == "regs"
+    sk = CodeGenerator(tune={"row": {"engine": "tma"}}).generate(g, grp, shapes, dts)
+    assert sk.plan.kernels[0].config["engine"] == "tma"
+    assert _alignment_rules(sk.plan.kernels[0])[0] == [16, 16, 16]

@@ -222,9 +222,23 @@ def test_misaligned_pointers_take_the_scalar_path(rt):
     ck = rt.compile(compile_graph(g)[0])
     out = ck(x, wt)
     torch.cuda.synchronize()
-    assert ck.specialization(x, wt).plan.kernels[0].config["vec"] == 1
+    sk = ck.specialization(x, wt).plan.kernels[0]
+    assert sk.config["vec"] == 1 and sk.config.get("engine") != "tma"
     res = orc.evaluate(g, {"x": to_numpy(x), "w": to_numpy(wt)})
     assert_close(as_f32(out), res[("f32", g.ops[g._outputs[0]].inputs[0])], "float32", "misaligned")
+
+
+def test_misaligned_output_is_refused_before_launch(rt):
+    from molten_b200._capi import MoltenError
+    g = graphs.rmsnorm(4, 512)
+    ck = rt.compile(compile_graph(g)[0])
+    x = torch.randn(4, 512, device=DEV)
+    wt = torch.randn(512, device=DEV)
+    base = torch.empty(4 * 512 + 1, device=DEV)
+    with pytest.raises(RuntimeError):          # shape/contiguity check or alignment guard
+        ck(x, wt, out=base[1:].view(4, 512))
+    torch.cuda.synchronize()                   # the context is still healthy
+    assert torch.isfinite(ck(x, wt)).all()
 
 
 def test_row_sharded_launches_match_whole(rt):
