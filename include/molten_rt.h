@@ -129,6 +129,23 @@ int molten_status_word(int device, int** dev_ptr);
 /* Read (and when reset != 0 clear) the device error word; synchronises. */
 int molten_read_status(int device, int* value, int reset);
 
+/* Allocation-free attention-score rows (no counterpart in the reference):
+ * out[m, n] = softmax over each row of (q[m, kdim] @ k[kdim, n]), bf16 in and
+ * out, fp32 accumulation.  For callers that cannot call cudaMalloc (a stream
+ * being captured into a CUDA graph, a device heap owned by another
+ * allocator, loops that must not allocate after start-up): the fp32
+ * intermediate lives in a fixed device array of
+ * MOLTEN_NOALLOC_SCORES_MAX_ELEMENTS floats (32 MiB per GPU that loads the
+ * library, held until exit), so m * n must not exceed that limit
+ * (MOLTEN_ERR_INVALID otherwise).  Calls share that array: calls that overlap
+ * on the GPU race.  n and kdim must be multiples of 8, pointers 16-byte
+ * aligned.  The first call on a device resolves the array's address, so make
+ * it before any stream capture.  Runs on the current device and `stream`. */
+#define MOLTEN_NOALLOC_SCORES_MAX_ELEMENTS (8LL * 1024 * 1024)
+int molten_scores_softmax_bf16_noalloc(const void* q, const void* k, void* out,
+                                       long long m, long long n, long long kdim,
+                                       void* stream);
+
 #ifdef __cplusplus
 }
 #endif

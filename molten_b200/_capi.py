@@ -33,6 +33,9 @@ SIGNATURES = {
                                         _c.c_int]),
     "molten_status_word": (_c.c_int, [_c.c_int, _c.POINTER(_c.c_void_p)]),
     "molten_read_status": (_c.c_int, [_c.c_int, _c.POINTER(_c.c_int), _c.c_int]),
+    "molten_scores_softmax_bf16_noalloc": (_c.c_int, [_c.c_void_p, _c.c_void_p, _c.c_void_p,
+                                                      _c.c_longlong, _c.c_longlong,
+                                                      _c.c_longlong, _c.c_void_p]),
 }
 
 

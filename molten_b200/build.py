@@ -95,7 +95,7 @@ def build_runtime(verbose: bool = False, force: bool = False) -> Path:
     """Build molten_b200/lib/libmolten_rt.so (the C-ABI runtime)."""
     LIB_DIR.mkdir(exist_ok=True)
     out = LIB_DIR / "libmolten_rt.so"
-    srcs = [CSRC_DIR / "runtime.cu"]
+    srcs = [CSRC_DIR / "runtime.cu", CSRC_DIR / "noalloc_scores.cu"]
     deps = srcs + [ABI_INCLUDE / "molten_rt.h"] + list((ENGINE_INCLUDE / "molten").glob("*.cuh"))
     if out.exists() and not force and all(out.stat().st_mtime >= d.stat().st_mtime for d in deps):
         return out

@@ -161,6 +161,10 @@ std::vector<int*> g_status;
 
 }  // namespace
 
+// Lets the library's other translation units report errors through
+// molten_last_error() (C++ linkage: not part of the C ABI).
+void molten_internal_set_error(const char* msg) { g_last_error = msg ? msg : ""; }
+
 extern "C" {
 
 int molten_version(void) { return 100; }
