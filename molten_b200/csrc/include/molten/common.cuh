@@ -124,6 +124,39 @@ __device__ __forceinline__ float load_scalar(const T* p) { return to_f32(p[0]); 
 template <typename T>
 __device__ __forceinline__ void store_scalar(T* p, float v) { p[0] = from_f32<T>(v); }
 
+// 2^x with the MUFU.EX2 instruction (ex2.approx.ftz: about 2 ulp over the
+// range softmax uses); e^(x - m) = 2^(x*log2e - m*log2e) is one FFMA + EX2.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+#define MOLTEN_LOG2E 1.4426950408889634f
+
+// 1/x with the MUFU.RCP instruction (rcp.approx.ftz: about 1 ulp); 1/inf = 0
+__device__ __forceinline__ float fast_rcp(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// max of the 16-bit elements of a slot, two at a time
+template <typename T, int VEC>
+__device__ __forceinline__ float slot_max16(const Slot<T, VEC>& s, float m) {
+  static_assert(sizeof(T) == 2 && VEC % 2 == 0, "16-bit slots");
+  if constexpr (std::is_same<T, bf16>::value) {
+    __nv_bfloat162 acc = *reinterpret_cast<const __nv_bfloat162*>(&s.v[0]);
+#pragma unroll
+    for (int e = 2; e < VEC; e += 2) acc = __hmax2(acc, *reinterpret_cast<const __nv_bfloat162*>(&s.v[e]));
+    return fmaxf(m, fmaxf(__low2float(acc), __high2float(acc)));
+  } else {
+    __half2 acc = *reinterpret_cast<const __half2*>(&s.v[0]);
+#pragma unroll
+    for (int e = 2; e < VEC; e += 2) acc = __hmax2(acc, *reinterpret_cast<const __half2*>(&s.v[e]));
+    return fmaxf(m, fmaxf(__low2float(acc), __high2float(acc)));
+  }
+}
+
 // ------------------------------------------------------- elementwise math
 // Every function computes in fp32.  PRECISE selects CUDA's full-precision
 // library functions; otherwise the fast hardware intrinsics are used (the
@@ -155,9 +188,17 @@ template <bool PRECISE> __device__ __forceinline__ float m_tanh(float x) {
 // evaluated through the identity 0.5 (1 + tanh(z)) = 1 / (1 + e^{-2z}), which
 // has no cancellation for large negative v.
 template <bool PRECISE> __device__ __forceinline__ float m_gelu_tanh(float v) {
-  const float k2 = 1.5957691216057308f;  // 2 * sqrt(2 / pi)
-  const float z2 = k2 * v * fmaf(0.044715f * v, v, 1.0f);
-  return m_div<PRECISE>(v, 1.0f + m_exp<PRECISE>(-z2));
+  if constexpr (PRECISE) {
+    const float k2 = 1.5957691216057308f;  // 2 * sqrt(2 / pi)
+    const float z2 = k2 * v * fmaf(0.044715f * v, v, 1.0f);
+    return v / (1.0f + expf(-z2));
+  } else {
+    // e^{-2z} = 2^{v (c1 + c2 v^2)}, c1 = -2 sqrt(2/pi) log2(e),
+    // c2 = 0.044715 c1: three FP32 ops, EX2, one add, RCP, one multiply
+    const float c1 = -2.3022082f, c2 = -0.10294324f;
+    const float e = fast_exp2(v * fmaf(c2, v * v, c1));
+    return v * fast_rcp(1.0f + e);
+  }
 }
 
 }  // namespace molten

@@ -28,9 +28,20 @@ struct RowArgs {
 };
 
 // ------------------------------------------------------------ reductions
-struct OpSum { __device__ __forceinline__ float operator()(float a, float b) const { return a + b; } };
-struct OpMax { __device__ __forceinline__ float operator()(float a, float b) const { return fmaxf(a, b); } };
-struct OpMin { __device__ __forceinline__ float operator()(float a, float b) const { return fminf(a, b); } };
+struct OpSum {
+  static constexpr float identity = 0.0f;
+  __device__ __forceinline__ float operator()(float a, float b) const { return a + b; }
+};
+struct OpMax {
+  static constexpr float identity = -INFINITY;
+  __device__ __forceinline__ float operator()(float a, float b) const { return fmaxf(a, b); }
+};
+struct OpMin {
+  static constexpr float identity = INFINITY;
+  __device__ __forceinline__ float operator()(float a, float b) const { return fminf(a, b); }
+};
+
+__host__ __device__ constexpr int pow2_ceil(int x) { return x <= 1 ? 1 : 2 * pow2_ceil((x + 1) / 2); }
 
 __device__ __forceinline__ unsigned cluster_ctarank() {
   unsigned r;
@@ -105,12 +116,26 @@ struct RowTeam {
         for (int i = 0; i < NR; ++i) red[warp * NR + i] = v[i];
       }
       __syncthreads();
+      if constexpr (WPR <= 4) {
 #pragma unroll
-      for (int i = 0; i < NR; ++i) {
-        float a = red[i];
+        for (int i = 0; i < NR; ++i) {
+          float a = red[i];
 #pragma unroll
-        for (int w = 1; w < WPR; ++w) a = op(a, red[w * NR + i]);
-        v[i] = a;
+          for (int w = 1; w < WPR; ++w) a = op(a, red[w * NR + i]);
+          v[i] = a;
+        }
+      } else {
+        // lane l takes warp (l mod P)'s partial, then a butterfly over each
+        // aligned group of P lanes, so that every lane ends with the total
+        constexpr int P = pow2_ceil(WPR);
+        const int src = lane % P;
+#pragma unroll
+        for (int i = 0; i < NR; ++i) {
+          float a = src < WPR ? red[src * NR + i] : Op::identity;
+#pragma unroll
+          for (int off = P / 2; off > 0; off >>= 1) a = op(a, __shfl_xor_sync(0xffffffffu, a, off));
+          v[i] = a;
+        }
       }
       __syncthreads();   // the area is reused by the next pass
     }
@@ -138,8 +163,8 @@ struct RowTeam {
   // A side whose max is -inf (all its elements masked) contributes 0.
   __device__ __forceinline__ static void softmax_combine(float& m, float& s, float m2, float s2) {
     const float M = fmaxf(m, m2);
-    const float a = (m == -INFINITY) ? 0.0f : s * expf(m - M);
-    const float b = (m2 == -INFINITY) ? 0.0f : s2 * expf(m2 - M);
+    const float a = (m == -INFINITY) ? 0.0f : s * fast_exp2((m - M) * MOLTEN_LOG2E);
+    const float b = (m2 == -INFINITY) ? 0.0f : s2 * fast_exp2((m2 - M) * MOLTEN_LOG2E);
     m = M;
     s = a + b;
   }
@@ -162,9 +187,18 @@ struct RowTeam {
         red[warp * 2 + 1] = s;
       }
       __syncthreads();
-      float M = red[0], S = red[1];
+      // lane l takes warp (l mod P)'s pair, then a butterfly over each
+      // aligned group of P lanes, so that every lane ends with the total
+      constexpr int P = pow2_ceil(WPR);
+      const int src = lane % P;
+      float M = src < WPR ? red[src * 2] : -INFINITY;
+      float S = src < WPR ? red[src * 2 + 1] : 0.0f;
 #pragma unroll
-      for (int w = 1; w < WPR; ++w) softmax_combine(M, S, red[w * 2], red[w * 2 + 1]);
+      for (int off = P / 2; off > 0; off >>= 1) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, M, off);
+        const float s2 = __shfl_xor_sync(0xffffffffu, S, off);
+        softmax_combine(M, S, m2, s2);
+      }
       m = M;
       s = S;
       __syncthreads();

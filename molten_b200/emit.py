@@ -231,7 +231,9 @@ def emit_row(sk: SubKernel, name: str) -> str:
     e.header("row")
     e.w("using namespace molten;")
     e.w("")
-    e.w(f"extern \"C\" __global__ void __launch_bounds__({TPC * RPC}) "
+    minb = cfg.get("min_blocks", 0)
+    lb = f"{TPC * RPC}, {minb}" if minb else f"{TPC * RPC}"
+    e.w(f"extern \"C\" __global__ void __launch_bounds__({lb}) "
         f"{name}(const __grid_constant__ RowArgs args) {{")
     e.w(f"  constexpr int VEC = {VEC}, NV = {NV}, TPC = {TPC}, RPC = {RPC}, CL = {CL};")
     e.w(f"  constexpr long long COLS = {sk.cols}LL, NVEC = {cfg['nvec']}LL;")
@@ -340,7 +342,7 @@ def emit_row(sk: SubKernel, name: str) -> str:
             e.w(f"  float gm{v} = lm{v}, gs{v} = ls{v};")
             e.w(f"  tm.reduce_softmax(gm{v}, gs{v}, red_smem, {call});")
             e.w(f"  const float sc{v} = (gs{v} > 0.0f) ? ((lm{v} == (-INFINITY)) ? 0.0f : "
-                f"expf(lm{v} - gm{v}) / gs{v}) : NAN;")
+                f"fast_exp2((lm{v} - gm{v}) * MOLTEN_LOG2E) / gs{v}) : NAN;")
             call += 1
             mat_ready.add(v)
         by_op = {}
@@ -422,7 +424,9 @@ def emit_ew(sk: SubKernel, name: str) -> str:
     e.header("elementwise")
     e.w("using namespace molten;")
     e.w("")
-    e.w(f"extern \"C\" __global__ void __launch_bounds__({TPC * RPC}) "
+    minb = cfg.get("min_blocks", 0)
+    lb = f"{TPC * RPC}, {minb}" if minb else f"{TPC * RPC}"
+    e.w(f"extern \"C\" __global__ void __launch_bounds__({lb}) "
         f"{name}(const __grid_constant__ RowArgs args) {{")
     e.w(f"  constexpr int VEC = {VEC}, NV = {NV}, TPC = {TPC}, RPC = {RPC}, UPT = {UPT};")
     e.w(f"  constexpr long long COLS = {sk.cols}LL, NVEC = {cfg['nvec']}LL;")

@@ -464,9 +464,41 @@ def choose_row_config(sk: SubKernel, prefetch: set, materialize: set,
     per_slot = _regs_per_slot(sk, vec, prefetch, materialize)
     budget = o.get("reg_budget", 64)
     nv_max = max(1, budget // per_slot)
+    # a warp per row when a row fits in 8 slots per lane: its reductions are
+    # shuffles only, no block barrier (measured best for short rows)
+    warp_row = (sk.passes > 0 and nvec > 32 * 2 and nvec <= 32 * 8
+                and -(-nvec // 32) * per_slot <= 128 and "reg_budget" not in o)
     if "tpc" in o:
         tpc, cl = o["tpc"], o.get("cl", 1)
         team = tpc * cl
+    elif warp_row:
+        tpc, cl, team = 32, 1, 32
+    elif "reg_budget" not in o and nvec >= 32:
+        # 4..8 streamed 16-byte slots in flight per thread, at most ~96
+        # resident fp32 values (measured: RMSNorm fp32 x 5120 and softmax
+        # fp32 x 2048 best at 5..8 slots, RMSNorm*SiLU bf16 x 3584 at 2 slots
+        # of each of its 2 streamed operands); least waste, then more slots
+        streams = max(1, len(prefetch))
+        hi = max(1, min(max(1, 8 // streams), 96 // per_slot))
+        lo = max(1, hi // 2)
+        best = None
+        for nv_c in range(hi, lo - 1, -1):
+            cand = 32 * (-(-(-(-nvec // nv_c)) // 32))
+            waste = cand * nv_c - nvec
+            key = (waste * 16 > nvec, waste, -nv_c)
+            if best is None or key < best[0]:
+                best = (key, cand)
+        team = best[1]
+        max_cta = o.get("max_tpc", 512)
+        cl = 1
+        while team // cl > max_cta or (team % cl):
+            cl *= 2
+        if cl > 8:
+            raise LoweringError(f"row of {sk.cols} elements is too long for one cluster")
+        tpc = team // cl
+        if cl > 1 and tpc % 32:
+            tpc = 32 * (-(-tpc // 32))
+            team = tpc * cl
     else:
         need = -(-nvec // nv_max)
         if need < 32:
@@ -503,6 +535,7 @@ def choose_row_config(sk: SubKernel, prefetch: set, materialize: set,
     if tpc < 32 and (tpc * rpc) % 32:
         rpc = 32 // tpc
     return {"vec": vec, "nvec": nvec, "tpc": tpc, "nv": nv, "rpc": rpc, "cl": cl,
+            "min_blocks": o.get("min_blocks", 0),
             "block": tpc * rpc}
 
 
@@ -523,7 +556,8 @@ def choose_ew_config(sk: SubKernel, override: Optional[dict] = None) -> dict:
         rpc = max(rpc, 32 // tpc)
     upt = o.get("upt") or 4
     return {"vec": vec, "nvec": nvec, "tpc": tpc, "nv": nv, "rpc": rpc, "upt": upt,
-            "block": tpc * rpc, "tiles": -(-nvec // (tpc * nv))}
+            "block": tpc * rpc, "tiles": -(-nvec // (tpc * nv)),
+            "min_blocks": o.get("min_blocks", 0)}
 
 
 SMEM_RING_BUDGET = 200 * 1024
