@@ -14,7 +14,8 @@
 //               round once and store.
 //
 // The accumulator is double-buffered in TMEM (2 x BN fp32 columns) so the
-// epilogue of tile i overlaps the main loop of tile i+1.  No TMA multicast.
+// epilogue of tile i overlaps the main loop of tile i+1.  Every TMA copy
+// lands in the issuing CTA's own shared memory.
 // Every mbarrier wait is bounded: on timeout the CTA records an error bit in
 // *status, stops issuing work, drains what it issued and frees its TMEM.
 #pragma once

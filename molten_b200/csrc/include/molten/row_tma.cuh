@@ -1,6 +1,6 @@
 // TMA-staged row engine: a persistent CTA per SM streams whole rows of the
 // row-indexed operands into a STAGES-deep shared-memory ring with
-// cp.async.bulk (the untiled TMA copy, no multicast) while NC consumer warps
+// cp.async.bulk (the untiled TMA copy, into this CTA only) while NC consumer warps
 // each take one row at a time, reduce it with warp shuffles and write the
 // outputs with 16-byte stores.
 //
