@@ -89,9 +89,9 @@ struct RowTeam {
     row_ok = row < rows;
   }
 
-  // slot index of this thread's k-th slot
-  __device__ __forceinline__ long long slot(int k) const {
-    return (long long)(rank * TPC + t) + (long long)k * (TPC * CL);
+  // slot index of this thread's k-th slot (a row has < 2^31 slots)
+  __device__ __forceinline__ int slot(int k) const {
+    return (rank * TPC + t) + k * (TPC * CL);
   }
 
   // All-reduce NR values across the row team (all CTAs of the cluster).

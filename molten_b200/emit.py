@@ -236,7 +236,8 @@ def emit_row(sk: SubKernel, name: str) -> str:
     e.w(f"extern \"C\" __global__ void __launch_bounds__({lb}) "
         f"{name}(const __grid_constant__ RowArgs args) {{")
     e.w(f"  constexpr int VEC = {VEC}, NV = {NV}, TPC = {TPC}, RPC = {RPC}, CL = {CL};")
-    e.w(f"  constexpr long long COLS = {sk.cols}LL, NVEC = {cfg['nvec']}LL;")
+    e.w(f"  constexpr long long COLS = {sk.cols}LL;")
+    e.w(f"  constexpr int NVEC = {cfg['nvec']};")
     e.w("  typedef RowTeam<TPC, RPC, CL> Team;")
     e.w(f"  __shared__ float red_smem[Team::smem_floats({max_nr}, {max(n_calls, 1)}) > 0 ? "
         f"Team::smem_floats({max_nr}, {max(n_calls, 1)}) : 1];")
@@ -264,16 +265,24 @@ def emit_row(sk: SubKernel, name: str) -> str:
         if opd.index in prefetch:
             ct = _ctype(opd.dtype)
             e.w(f"  Slot<{ct}, VEC> s{opd.index}[NV];")
+    masked_only = _causal_masked_only_operands(sk, closures, reds, smx_of(values, needed, sk.passes),
+                                               materialize)
     if prefetch:
         e.w("#pragma unroll")
         e.w("  for (int k = 0; k < NV; ++k) {")
-        e.w("    const long long j = tm.slot(k);")
+        e.w("    const int j = tm.slot(k);")
         e.w("    if (rok && j < NVEC) {")
         for opd in sk.operands:
             if opd.index in prefetch:
                 hint = _LOAD_HINT[opd.row_map == "full"]
-                e.w(f"      s{opd.index}[k] = load_slot<{hint}, {_ctype(opd.dtype)}, VEC>"
-                    f"(in{opd.index} + j * VEC);")
+                load = (f"s{opd.index}[k] = load_slot<{hint}, {_ctype(opd.dtype)}, VEC>"
+                        f"(in{opd.index} + j * VEC);")
+                if opd.index in masked_only:
+                    # only the causal softmax reads it: columns above the
+                    # row's limit are never needed, so they are not loaded
+                    e.w(f"      if (j * VEC <= mlim{masked_only[opd.index]}) {load}")
+                else:
+                    e.w(f"      {load}")
         e.w("    }")
         e.w("  }")
     for vid in sorted(materialize):
@@ -289,53 +298,36 @@ def emit_row(sk: SubKernel, name: str) -> str:
             e.w(f"  float v{r} = {_RED_INIT[values[r].op]};")
         targets = set(closures[p])
         to_mat = {m for m, pm in materialize.items() if pm == p and values[m].op != "softmax"}
-        if smx[p]:
-            # online softmax, step 1: this thread's max of each softmax input
-            xs_targets = set()
-            for v in smx[p]:
-                xs_targets |= _closure_within(values, values[v].args[0], targets)
-            for v in smx[p]:
-                e.w(f"  float lm{v} = (-INFINITY), ls{v} = 0.0f;")
+        causal = None
+        if len(smx[p]) == 1 and not rs and not to_mat:
+            causal = _causal_softmax_parts(values, smx[p][0], targets)
+        if causal is not None:
+            _emit_causal_softmax_pass(e, sk, smx[p][0], causal, targets, prefetch, mat_ready)
+        else:
+            if smx[p]:
+                _emit_softmax_local_max(e, sk, smx[p], targets, prefetch, mat_ready)
             e.w("#pragma unroll")
             e.w("  for (int k = 0; k < NV; ++k) {")
-            e.w("    const long long j = tm.slot(k);")
+            e.w("    const int j = tm.slot(k);")
             e.w("    if (!(rok && j < NVEC)) continue;")
-            _emit_nonprefetched_loads(e, xs_targets, prefetch, "    ")
+            _emit_nonprefetched_loads(e, targets, prefetch, "    ")
             e.w("#pragma unroll")
             e.w("    for (int e = 0; e < VEC; ++e) {")
-            if any(values[t].op == "mask" for t in xs_targets):
+            if any(values[t].op == "mask" for t in targets):
                 e.w("      const int col = (int)(j * VEC) + e;")
-            for st in e.elem_statements(xs_targets, prefetch, mat_ready, "      "):
+            for st in e.elem_statements(targets, prefetch, mat_ready, "      "):
                 e.w(st)
+            for m in sorted(to_mat):
+                e.w(f"      m{m}[k][e] = v{m};")
             for v in smx[p]:
+                # step 2: exponentials relative to the thread's max, kept in registers
                 x = e.leaf(values[v].args[0], True, prefetch, mat_ready, set())
-                e.w(f"      lm{v} = fmaxf(lm{v}, {x});")
+                e.w(f"      {{ const float ev = {_softmax_exp(sk, v, x)}; m{v}[k][e] = ev; ls{v} += ev; }}")
+            for r in rs:
+                x = e.leaf(values[r].args[0], True, prefetch, mat_ready, set())
+                e.w("      " + _RED_COMBINE[values[r].op].format(a=f"v{r}", x=x))
             e.w("    }")
             e.w("  }")
-            for v in smx[p]:
-                e.w(f"  const float lz{v} = (lm{v} == (-INFINITY)) ? 0.0f : lm{v};")
-        e.w("#pragma unroll")
-        e.w("  for (int k = 0; k < NV; ++k) {")
-        e.w("    const long long j = tm.slot(k);")
-        e.w("    if (!(rok && j < NVEC)) continue;")
-        _emit_nonprefetched_loads(e, targets, prefetch, "    ")
-        e.w("#pragma unroll")
-        e.w("    for (int e = 0; e < VEC; ++e) {")
-        if any(values[t].op == "mask" for t in targets):
-            e.w("      const int col = (int)(j * VEC) + e;")
-        for st in e.elem_statements(targets, prefetch, mat_ready, "      "):
-            e.w(st)
-        for m in sorted(to_mat):
-            e.w(f"      m{m}[k][e] = v{m};")
-        for v in smx[p]:
-            # step 2: exponentials relative to the thread's max, kept in registers
-            x = e.leaf(values[v].args[0], True, prefetch, mat_ready, set())
-            e.w(f"      {{ const float ev = {EXP}({x} - lz{v}); m{v}[k][e] = ev; ls{v} += ev; }}")
-        for r in rs:
-            x = e.leaf(values[r].args[0], True, prefetch, mat_ready, set())
-            e.w("      " + _RED_COMBINE[values[r].op].format(a=f"v{r}", x=x))
-        e.w("    }")
-        e.w("  }")
         mat_ready |= to_mat
         for v in smx[p]:
             # step 3: one pair reduction per row; scale = e^(m_thread - M) / S
@@ -366,7 +358,7 @@ def emit_row(sk: SubKernel, name: str) -> str:
         e.w("  // ---- final pass: outputs")
         e.w("#pragma unroll")
         e.w("  for (int k = 0; k < NV; ++k) {")
-        e.w("    const long long j = tm.slot(k);")
+        e.w("    const int j = tm.slot(k);")
         e.w("    if (!(rok && j < NVEC)) continue;")
         _emit_nonprefetched_loads(e, fin, prefetch, "    ")
         for o in full_outs:
@@ -786,4 +778,184 @@ def _closure_within(values, root, allowed) -> set:
             continue
         out.add(v)
         stack.extend(values[v].args)
+    return out
+
+
+def _softmax_exp(sk: SubKernel, v: int, x: str) -> str:
+    """e^(x - m_thread): precise expf for fp32 outputs, else one FFMA + EX2."""
+    if sk.precise:
+        return f"expf({x} - lz{v})"
+    return f"fast_exp2(fmaf({x}, MOLTEN_LOG2E, lzs{v}))"
+
+
+def _emit_softmax_thread_max_decl(e: _Emitter, sk: SubKernel, vs):
+    for v in vs:
+        e.w(f"  float lm{v} = (-INFINITY), ls{v} = 0.0f;")
+
+
+def _emit_softmax_max_tail(e: _Emitter, sk: SubKernel, vs):
+    for v in vs:
+        e.w(f"  const float lz{v} = (lm{v} == (-INFINITY)) ? 0.0f : lm{v};")
+        if not sk.precise:
+            e.w(f"  const float lzs{v} = -lz{v} * MOLTEN_LOG2E;")
+
+
+def _emit_softmax_local_max(e: _Emitter, sk: SubKernel, vs, targets, prefetch, mat_ready):
+    """Online softmax, step 1: this thread's max of each softmax input."""
+    values = sk.values
+    VEC = sk.config["vec"]
+    _emit_softmax_thread_max_decl(e, sk, vs)
+    xs_targets = set()
+    for v in vs:
+        xs_targets |= _closure_within(values, values[v].args[0], targets)
+    e.w("#pragma unroll")
+    e.w("  for (int k = 0; k < NV; ++k) {")
+    e.w("    const int j = tm.slot(k);")
+    e.w("    if (!(rok && j < NVEC)) continue;")
+    packed = [v for v in vs if _packed_max_operand(sk, values[values[v].args[0]], prefetch, VEC)]
+    for v in packed:
+        i = values[values[v].args[0]].attrs["operand"]
+        e.w(f"    lm{v} = slot_max16(s{i}[k], lm{v});      // two elements per max")
+    rest = [v for v in vs if v not in packed]
+    if rest:
+        _emit_nonprefetched_loads(e, xs_targets, prefetch, "    ")
+        e.w("#pragma unroll")
+        e.w("    for (int e = 0; e < VEC; ++e) {")
+        if any(values[t].op == "mask" for t in xs_targets):
+            e.w("      const int col = (int)(j * VEC) + e;")
+        for st in e.elem_statements(xs_targets, prefetch, mat_ready, "      "):
+            e.w(st)
+        for v in rest:
+            x = e.leaf(values[v].args[0], True, prefetch, mat_ready, set())
+            e.w(f"      lm{v} = fmaxf(lm{v}, {x});")
+        e.w("    }")
+    e.w("  }")
+    _emit_softmax_max_tail(e, sk, vs)
+
+
+def _causal_softmax_parts(values, v: int, targets):
+    """(a, mask) when the softmax input is ADD(a, causal mask) and a does not
+    depend on the mask; None otherwise."""
+    x = values[values[v].args[0]]
+    if x.op != "add":
+        return None
+    a, b = x.args
+    if values[b].op == "mask" and values[a].op != "mask":
+        pair = (a, b)
+    elif values[a].op == "mask" and values[b].op != "mask":
+        pair = (b, a)
+    else:
+        return None
+    if pair[1] in _closure_within(values, pair[0], set(range(len(values)))):
+        return None
+    return pair
+
+
+def _emit_causal_softmax_pass(e: _Emitter, sk: SubKernel, v: int, parts, targets, prefetch,
+                              mat_ready):
+    """Softmax of a + causal mask, classifying each slot once: columns
+    c0 .. c0+VEC-1 all above the row's limit (exponentials are 0, nothing is
+    computed), all at or below it (no mask arithmetic), or straddling it (the
+    one boundary slot of the row, checked per element)."""
+    values = sk.values
+    VEC = sk.config["vec"]
+    a, mk = parts
+    a_targets = _closure_within(values, a, targets)
+    lim = f"mlim{mk}"
+    _emit_softmax_thread_max_decl(e, sk, [v])
+    packed = _packed_max_operand(sk, values[a], prefetch, VEC)
+
+    def a_stmts(indent):
+        for st in e.elem_statements(a_targets, prefetch, mat_ready, indent):
+            e.w(st)
+
+    x = e.leaf(a, True, prefetch, mat_ready, set())
+    # step 1: thread max over the visible columns
+    e.w("#pragma unroll")
+    e.w("  for (int k = 0; k < NV; ++k) {")
+    e.w("    const int j = tm.slot(k);")
+    e.w("    if (!(rok && j < NVEC)) continue;")
+    e.w("    const int c0 = j * VEC;")
+    e.w(f"    if (c0 > {lim}) continue;                       // slot fully masked")
+    _emit_nonprefetched_loads(e, a_targets, prefetch, "    ")
+    if packed:
+        i = values[a].attrs["operand"]
+        e.w(f"    if (c0 + VEC - 1 <= {lim}) {{ lm{v} = slot_max16(s{i}[k], lm{v}); continue; }}")
+    else:
+        e.w(f"    if (c0 + VEC - 1 <= {lim}) {{")
+        e.w("#pragma unroll")
+        e.w("      for (int e = 0; e < VEC; ++e) {")
+        a_stmts("        ")
+        e.w(f"        lm{v} = fmaxf(lm{v}, {x});")
+        e.w("      }")
+        e.w("      continue;")
+        e.w("    }")
+    e.w("#pragma unroll")
+    e.w("    for (int e = 0; e < VEC; ++e) {")
+    a_stmts("      ")
+    e.w(f"      if (c0 + e <= {lim}) lm{v} = fmaxf(lm{v}, {x});")
+    e.w("    }")
+    e.w("  }")
+    _emit_softmax_max_tail(e, sk, [v])
+    # step 2: exponentials of the visible columns, zeros above the limit
+    ex = _softmax_exp(sk, v, x)
+    e.w("#pragma unroll")
+    e.w("  for (int k = 0; k < NV; ++k) {")
+    e.w("    const int j = tm.slot(k);")
+    e.w("    if (!(rok && j < NVEC)) continue;")
+    e.w("    const int c0 = j * VEC;")
+    e.w(f"    if (c0 > {lim}) {{")
+    e.w("#pragma unroll")
+    e.w(f"      for (int e = 0; e < VEC; ++e) m{v}[k][e] = 0.0f;")
+    e.w("      continue;")
+    e.w("    }")
+    _emit_nonprefetched_loads(e, a_targets, prefetch, "    ")
+    e.w(f"    const bool whole = c0 + VEC - 1 <= {lim};")
+    e.w("#pragma unroll")
+    e.w("    for (int e = 0; e < VEC; ++e) {")
+    a_stmts("      ")
+    e.w(f"      const float ev = (whole || c0 + e <= {lim}) ? {ex} : 0.0f;")
+    e.w(f"      m{v}[k][e] = ev;")
+    e.w(f"      ls{v} += ev;")
+    e.w("    }")
+    e.w("  }")
+
+
+def _packed_max_operand(sk: SubKernel, xv: Value, prefetch, vec: int) -> bool:
+    """The softmax input is a prefetched 16-bit operand itself: its row max
+    can be taken on packed pairs of raw elements."""
+    if xv.op != "load" or xv.kind != "elem":
+        return False
+    o = sk.operands[xv.attrs["operand"]]
+    return o.index in prefetch and o.dtype in ("bfloat16", "float16") and vec % 2 == 0
+
+
+def smx_of(values, needed, passes):
+    out = {p: [] for p in range(passes)}
+    for vid in sorted(needed):
+        if values[vid].op == "softmax":
+            out[values[vid].avail - 1].append(vid)
+    return out
+
+
+def _causal_masked_only_operands(sk: SubKernel, closures, reds, smx, materialize) -> dict:
+    """Prefetched operands read only as the `a` of a causal softmax(a + mask):
+    {operand index: mask value id}.  Their fully masked slots are skipped."""
+    values = sk.values
+    out = {}
+    for p, vs in smx.items():
+        to_mat = {m for m, pm in materialize.items() if pm == p and values[m].op != "softmax"}
+        if len(vs) != 1 or reds.get(p) or to_mat:
+            continue
+        parts = _causal_softmax_parts(values, vs[0], closures[p])
+        if parts is None:
+            continue
+        a, mk = parts
+        av = values[a]
+        if av.op != "load":
+            continue
+        i = av.attrs["operand"]
+        used_elsewhere = any(a in closures[q] for q in closures if q != p)
+        if not used_elsewhere:
+            out[i] = mk
     return out

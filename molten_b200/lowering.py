@@ -344,9 +344,17 @@ class _DagBuilder:
         return self.add("const", "const", (), {"value": float(x)})
 
     def unary(self, op, a, attrs=None):
+        va = self.values[a]
+        if op == "rcp" and va.op == "sqrt" and va.kind == "row":
+            # 1 / sqrt(x) per row -> rsqrtf(x) (2 ulp, one MUFU op)
+            return self.add("row", "rsqrt", va.args)
         return self.add(self.kind_of([a]), op, (a,), attrs)
 
     def binary(self, op, a, b):
+        va, vb = self.values[a], self.values[b]
+        if op == "div" and va.kind == "row" and vb.op == "const" and vb.attrs["value"] not in (0.0,):
+            # per-row value over a constant: one multiply by the reciprocal
+            return self.add("row", "mul", (a, self.const(1.0 / vb.attrs["value"])))
         return self.add(self.kind_of([a, b]), op, (a, b))
 
     def reduce(self, op, a) -> int:

@@ -56,12 +56,23 @@ def _rms(name, rows, cols, dtype, silu):
     return Workload(name, kind, {"rows": rows, "cols": cols}, dtype, nbytes, 0, names)
 
 
+def _visible_fraction(rows: int, cols: int) -> float:
+    """Share of a causal mask's entries that are visible (col <= row mod
+    cols), i.e. the logits a causal softmax has to read."""
+    full, rem = divmod(rows, cols)
+    per_period = cols * (cols + 1) // 2
+    tail = rem * (rem + 1) // 2
+    return (full * per_period + tail) / (rows * cols)
+
+
 def _softmax(name, shape, dtype, causal):
     n = 1
     for d in shape:
         n *= d
+    cols = shape[-1]
+    reads = n if not causal else round(n * _visible_fraction(n // cols, cols))
     return Workload(name, "softmax", {"shape": tuple(shape), "causal": causal}, dtype,
-                    2 * n * _esz(dtype), 0, ["logits"])
+                    (reads + n) * _esz(dtype), 0, ["logits"])
 
 
 WORKLOADS = {w.name: w for w in [
