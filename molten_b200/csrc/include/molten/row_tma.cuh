@@ -66,38 +66,44 @@ __device__ __forceinline__ void warp_allreduce_min(float (&v)[N]) {
     for (int i = 0; i < N; ++i) v[i] = fminf(v[i], __shfl_xor_sync(0xffffffffu, v[i], off));
 }
 
-// Shared-memory ring: STAGES stages of STAGE_BYTES, then full[S], empty[S].
-template <int STAGES, int STAGE_BYTES>
+// Shared-memory layout: STAGES stages of STAGE_BYTES, then CONST_BYTES of
+// per-column operands (copied once per CTA), then full[S], empty[S] and the
+// "constants landed" barrier.
+template <int STAGES, int STAGE_BYTES, int CONST_BYTES = 0>
 struct RowRing {
-  static constexpr int BAR_OFFSET = STAGES * STAGE_BYTES;
-  static constexpr int SMEM_BYTES = BAR_OFFSET + 2 * STAGES * 8 + 16 + 128;
+  static constexpr int CONST_OFFSET = STAGES * STAGE_BYTES;
+  static constexpr int BAR_OFFSET = CONST_OFFSET + CONST_BYTES;
+  static constexpr int SMEM_BYTES = BAR_OFFSET + (2 * STAGES + 1) * 8 + 16 + 128;
   uint32_t base;      // shared address of stage 0 (128-byte aligned)
   uint32_t bars;
   volatile int* abort_flag;
   __device__ __forceinline__ uint32_t stage(int s) const { return base + (uint32_t)(s * STAGE_BYTES); }
+  __device__ __forceinline__ uint32_t consts() const { return base + (uint32_t)CONST_OFFSET; }
   __device__ __forceinline__ uint32_t full(int s) const { return bars + 8u * s; }
   __device__ __forceinline__ uint32_t empty(int s) const { return bars + 8u * (STAGES + s); }
+  __device__ __forceinline__ uint32_t consts_full() const { return bars + 8u * (2 * STAGES); }
 };
 
-template <int STAGES, int STAGE_BYTES>
-__device__ __forceinline__ RowRing<STAGES, STAGE_BYTES> row_ring_carve(uint8_t* raw) {
-  RowRing<STAGES, STAGE_BYTES> r;
+template <int STAGES, int STAGE_BYTES, int CONST_BYTES = 0>
+__device__ __forceinline__ RowRing<STAGES, STAGE_BYTES, CONST_BYTES> row_ring_carve(uint8_t* raw) {
+  typedef RowRing<STAGES, STAGE_BYTES, CONST_BYTES> R;
+  R r;
   const uintptr_t p = (reinterpret_cast<uintptr_t>(raw) + 127) & ~uintptr_t(127);
   uint8_t* b = reinterpret_cast<uint8_t*>(p);
   r.base = smem_u32(b);
-  r.bars = smem_u32(b + RowRing<STAGES, STAGE_BYTES>::BAR_OFFSET);
-  r.abort_flag = reinterpret_cast<volatile int*>(b + RowRing<STAGES, STAGE_BYTES>::BAR_OFFSET +
-                                                 2 * STAGES * 8);
+  r.bars = smem_u32(b + R::BAR_OFFSET);
+  r.abort_flag = reinterpret_cast<volatile int*>(b + R::BAR_OFFSET + (2 * STAGES + 1) * 8);
   return r;
 }
 
-template <int STAGES, int STAGE_BYTES>
-__device__ __forceinline__ void row_ring_init(const RowRing<STAGES, STAGE_BYTES>& r) {
+template <class R>
+__device__ __forceinline__ void row_ring_init(const R& r, int stages) {
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < stages; ++s) {
       mbar_init(r.full(s), 1);
       mbar_init(r.empty(s), 1);
     }
+    mbar_init(r.consts_full(), 1);
     *r.abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }

@@ -539,6 +539,9 @@ def emit_row_tma(sk: SubKernel, name: str) -> str:
     VEC, NV, NC, ST = cfg["vec"], cfg["nv"], cfg["nc"], cfg["stages"]
     staged = list(cfg["staged"])                   # operand indices, stage order
     offs = dict(zip(staged, cfg["stage_offsets"]))
+    consts = list(cfg.get("consts", ()))           # per-column operands, copied once
+    coffs = dict(zip(consts, cfg.get("const_offsets", ())))
+    CB = cfg.get("const_bytes", 0)
     values = sk.values
     needed = set(cfg["needed"])
     materialize = {int(v): int(p) for v, p in cfg["materialize"]}
@@ -564,8 +567,8 @@ def emit_row_tma(sk: SubKernel, name: str) -> str:
     w(f"  constexpr long long COLS = {sk.cols}LL, NVEC = {cfg['nvec']}LL;")
     w(f"  constexpr uint32_t ROW_BYTES = {cfg['row_bytes']}u;")
     w("  extern __shared__ __align__(128) uint8_t smem_raw[];")
-    w("  const auto ring = row_ring_carve<STAGES, STAGE_BYTES>(smem_raw);")
-    w("  row_ring_init(ring);")
+    w(f"  const auto ring = row_ring_carve<STAGES, STAGE_BYTES, {CB}>(smem_raw);")
+    w("  row_ring_init(ring, STAGES);")
     w("  __syncthreads();")
     w("  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;")
     w("  const long long G = gridDim.x;")
@@ -574,6 +577,13 @@ def emit_row_tma(sk: SubKernel, name: str) -> str:
     w("  if (warp == 0) {")
     w("    if (lane == 0) {")
     w("      long long issued = 0;")
+    if consts:
+        w(f"      mbar_expect_tx(ring.consts_full(), {sum(sk.cols * DTYPE_SIZE_OF[sk.operands[i].dtype] for i in consts)}u);")
+        for i in consts:
+            o = sk.operands[i]
+            ct = _ctype(o.dtype)
+            w(f"      bulk_g2s(ring.consts() + {coffs[i]}u, args.in[{i}], "
+              f"{sk.cols * DTYPE_SIZE_OF[o.dtype]}u, ring.consts_full());")
     w("      for (long long j = 0; j < nloc && !*ring.abort_flag; ++j) {")
     w("        const int s = (int)(j % STAGES);")
     w("        const uint32_t ph = (uint32_t)((j / STAGES) & 1);")
@@ -602,6 +612,12 @@ def emit_row_tma(sk: SubKernel, name: str) -> str:
     w("      }")
     w("    }")
     w("  } else {")
+    if consts:
+        w("    if (!__all_sync(0xffffffffu, mbar_wait(ring.consts_full(), 0u) ? 1 : 0)) {")
+        w("      if (lane == 0) row_ring_fail(ring.abort_flag, args.status, kRowTimeoutFull);")
+        w("      return;")
+        w("    }")
+        w("    const uint32_t cb = ring.consts();")
     w("    for (long long j = warp - 1; j < nloc; j += NC) {")
     w("      const int s = (int)(j % STAGES);")
     w("      const bool got = mbar_wait(ring.full(s), (uint32_t)((j / STAGES) & 1));")
@@ -616,7 +632,7 @@ def emit_row_tma(sk: SubKernel, name: str) -> str:
     w("      (void)grow;")
     # non-staged operand pointers and outputs
     for o in sk.operands:
-        if o.index in staged:
+        if o.index in staged or o.index in consts:
             continue
         ct = _ctype(o.dtype)
         idx = _row_index_expr(o, "lrow", "grow")
@@ -673,7 +689,11 @@ def emit_row_tma(sk: SubKernel, name: str) -> str:
         for i in sorted(used_glob):
             o = sk.operands[i]
             ct = _ctype(o.dtype)
-            w(f"        const Slot<{ct}, VEC> sl{i} = load_slot<kLoadDefault, {ct}, VEC>(in{i} + j * VEC);")
+            if i in consts:
+                w(f"        const Slot<{ct}, VEC> sl{i} = lds_slot<{ct}, VEC>(cb + {coffs[i]}u + "
+                  f"(uint32_t)(j * (VEC * {DTYPE_SIZE_OF[o.dtype]})));")
+            else:
+                w(f"        const Slot<{ct}, VEC> sl{i} = load_slot<kLoadDefault, {ct}, VEC>(in{i} + j * VEC);")
         for o in outs:
             w(f"        float f{o.index}[VEC];")
         w("#pragma unroll")

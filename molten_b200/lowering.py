@@ -568,7 +568,8 @@ def choose_ew_config(sk: SubKernel, override: Optional[dict] = None) -> dict:
             "min_blocks": o.get("min_blocks", 0)}
 
 
-SMEM_RING_BUDGET = 200 * 1024
+SMEM_RING_BUDGET = 220 * 1024
+TMA_MIN_ROWS = 4096      # below this the ring's fill time outweighs its depth
 
 
 def choose_row_tma_config(sk: SubKernel, prefetch: set, materialize: dict,
@@ -580,10 +581,13 @@ def choose_row_tma_config(sk: SubKernel, prefetch: set, materialize: dict,
     slots and at least 8 stages in the shared-memory budget.
     """
     o = dict(override or {})
-    # opt-in only (the register engine measured faster on every benchmark
-    # row); never under a vec override, which the runtime uses for inputs
+    # Chosen for long row counts (measured: RMSNorm*SiLU bf16 x 3584 at 8192
+    # rows 91% of HBM peak vs 83% for the register engine, but slower at 2048
+    # rows); never under a vec override, which the runtime uses for inputs
     # that are not 16-byte aligned -- bulk copies need 16-byte alignment
-    if o.get("engine") != "tma" or "vec" in o or not prefetch:
+    if o.get("engine") == "regs" or "vec" in o or not prefetch:
+        return None
+    if o.get("engine") != "tma" and sk.rows < TMA_MIN_ROWS:
         return None
     if any(v.op == "softmax" for v in sk.values):
         return None
@@ -599,16 +603,25 @@ def choose_row_tma_config(sk: SubKernel, prefetch: set, materialize: dict,
         offsets.append(off)
         off += -(-(sk.cols * DTYPE_SIZE[sk.operands[i].dtype]) // 128) * 128
     stage_bytes = off
-    s_max = o.get("stages") or min(32, SMEM_RING_BUDGET // stage_bytes)
+    # per-column operands (weights, bias vectors) are copied into shared
+    # memory once per CTA instead of being re-read by every row
+    consts, const_offsets, coff = [], [], 0
+    for x in sk.operands:
+        if x.last == "vec" and x.row_map == "zero":
+            consts.append(x.index)
+            const_offsets.append(coff)
+            coff += -(-(sk.cols * DTYPE_SIZE[x.dtype]) // 128) * 128
+    s_max = o.get("stages") or min(32, (SMEM_RING_BUDGET - coff) // stage_bytes)
     if s_max < o.get("min_stages", 8) and o.get("engine") != "tma":
         return None
     # Stage s is always consumed by warp s % NC, which needs STAGES % NC == 0:
     # a warp then meets the stages it owns in order and can never wait on a
     # phase two ahead of the one in flight (mbarrier parity would alias).
     best = None
-    for min_nc in ((o["nc"],) if "nc" in o else (6, 2)):
+    nc_ranges = [[o["nc"]]] if "nc" in o else [range(8, 5, -1), range(14, 1, -1)]
+    for ncs in nc_ranges:          # 6..8 consumer warps measured best
         for st in range(max(2, s_max), 1, -1):
-            for nc in ([o["nc"]] if "nc" in o else range(10, min_nc - 1, -1)):
+            for nc in ncs:
                 if st % nc == 0:
                     best = (st, nc)
                     break
@@ -626,7 +639,8 @@ def choose_row_tma_config(sk: SubKernel, prefetch: set, materialize: dict,
         mat = {}                     # recompute instead of holding in registers
     return {"engine": "tma", "vec": vec, "nvec": nvec, "nv": nv, "nc": nc,
             "stages": stages, "stage_bytes": stage_bytes, "staged": staged,
-            "stage_offsets": offsets,
+            "stage_offsets": offsets, "consts": consts, "const_offsets": const_offsets,
+            "const_bytes": coff,
             "row_bytes": sum(sk.cols * DTYPE_SIZE[sk.operands[i].dtype] for i in staged),
-            "smem": stages * stage_bytes + 2 * stages * 8 + 16 + 128,
+            "smem": stages * stage_bytes + coff + (2 * stages + 1) * 8 + 16 + 128,
             "materialize": sorted(mat.items()), "prefetch": staged, "cl": 1}

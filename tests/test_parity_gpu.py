@@ -214,6 +214,32 @@ def test_rmsnorm_edge_shapes(rt, rows, cols, dtype):
                  f"rmsnorm_silu {rows}x{cols} {dtype}")
 
 
+@pytest.mark.parametrize("rows,cols,dtype", [(1, 3584, "bfloat16"), (37, 3584, "bfloat16"),
+                                             (300, 1024, "bfloat16"), (150, 5120, "float32")])
+def test_tma_ring_engine(rows, cols, dtype):
+    """The TMA-staged ring engine, forced on at sizes where the automatic
+    choice would not pick it (fewer rows than CTAs, ragged last wave)."""
+    rt = MoltenRuntime(tune={"row": {"engine": "tma"}})
+    g = graphs.rmsnorm_silu_gate(rows, cols, dtype=dtype)
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(rows + cols)
+    x = torch.randn(rows, cols, generator=gen, device=DEV).to(TORCH_DT[dtype])
+    wt = (1 + 0.1 * torch.randn(cols, generator=gen, device=DEV)).to(TORCH_DT[dtype])
+    gt = torch.randn(rows, cols, generator=gen, device=DEV).to(TORCH_DT[dtype])
+    from molten_b200.codegen import CodeGenerator
+    from molten_b200.fusion import FusionEngine
+    gk = CodeGenerator(tune=rt.tune).generate(g, FusionEngine().fuse(g)[0],
+                                              {0: (rows, cols), 1: (cols,), 2: (rows, cols)},
+                                              {0: dtype, 1: dtype, 2: dtype})
+    assert gk.plan.kernels[0].config["engine"] == "tma"
+    out = rt.compile(gk)(x, wt, gt)
+    torch.cuda.synchronize()
+    assert MoltenRuntime.read_status(0) == 0
+    res = orc.evaluate(g, {"x": to_numpy(x), "w": to_numpy(wt), "gate": to_numpy(gt)})
+    assert_close(as_f32(out), res[("f32", g.ops[g._outputs[0]].inputs[0])], dtype,
+                 f"tma ring {rows}x{cols} {dtype}")
+
+
 def test_misaligned_pointers_take_the_scalar_path(rt):
     g = graphs.rmsnorm(4, 512)
     base = torch.randn(4 * 512 + 1, device=DEV)
