@@ -585,7 +585,7 @@ def choose_row_tma_config(sk: SubKernel, prefetch: set, materialize: dict,
     # rows 91% of HBM peak vs 83% for the register engine, but slower at 2048
     # rows); never under a vec override, which the runtime uses for inputs
     # that are not 16-byte aligned -- bulk copies need 16-byte alignment
-    if o.get("engine") == "regs" or "vec" in o or not prefetch:
+    if o.get("engine") in ("regs", "ew") or "vec" in o or not prefetch:
         return None
     if o.get("engine") != "tma" and sk.rows < TMA_MIN_ROWS:
         return None

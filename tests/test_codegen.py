@@ -76,18 +76,23 @@ def test_names_follow_reference_rule():
         "molten_fused_mul_add_gelu_clamp"
 
 
-@pytest.mark.parametrize("kind,args,fam", [
-    ("rmsnorm", (2048, 5120), "row"),
-    ("rmsnorm_silu_gate", (8192, 3584), "row"),
-    ("softmax", ((32, 2048, 2048),), "row"),
-    ("chain", (16384, 8192), "ew"),
-    ("gemm_bias_gelu", (8192, 4096, 14336), "gemm"),
+@pytest.mark.parametrize("kind,args,fam,engine", [
+    ("rmsnorm", (2048, 5120), "row", "regs"),
+    ("rmsnorm_silu_gate", (2048, 3584), "row", "regs"),
+    ("rmsnorm_silu_gate", (8192, 3584), "row", "tma"),
+    ("softmax", ((32, 2048, 2048),), "row", "regs"),
+    ("chain", (64, 8192), "ew", None),
+    ("chain", (16384, 8192), "ew", None),
+    ("gemm_bias_gelu", (8192, 4096, 14336), "gemm", None),
 ])
-def test_families(kind, args, fam):
+def test_families(kind, args, fam, engine):
+    """Pattern family and engine per benchmark graph: long row counts stream
+    through the TMA ring (reductions or not), the rest keep rows in registers."""
     dt = "float32" if kind in ("rmsnorm", "softmax") else "bfloat16"
     g = graphs.BUILDERS[kind](*args, dtype=dt)
     ks = compile_graph(g, dtype=dt)
     assert len(ks) == 1 and [sk.family for sk in ks[0].plan.kernels] == [fam]
+    assert ks[0].plan.kernels[0].config.get("engine") == engine
 
 
 def test_specialised_dtypes_and_promotion():
