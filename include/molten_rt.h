@@ -100,6 +100,15 @@ int molten_module_unload(void* mod);
 int molten_kernel_info(void* mod, const char* kernel, int* num_regs,
                        int* max_threads, int* static_smem);
 
+/* How many CTAs of `kernel` fit on one SM with `cfg`'s block size and
+ * dynamic shared memory (*ctas_per_sm), and how many clusters of
+ * `cfg->cluster` fit on the whole device at once (*clusters; equals
+ * ctas_per_sm x SMs without clusters).  Persistent kernels size their
+ * grid with it.  No counterpart in the reference (its launches are one CTA
+ * per row or tile). */
+int molten_max_resident(void* mod, const char* kernel, const molten_launch_cfg* cfg,
+                        int* ctas_per_sm, int* clusters);
+
 /* Launch `kernel` of `mod` with one by-value parameter block of
  * `params_bytes` bytes (molten_row_args or molten_gemm_args).
  * Replaces the generated "<name>_launch" wrapper (molten/runtime.py:111-189)

@@ -26,6 +26,8 @@ SIGNATURES = {
     "molten_module_unload": (_c.c_int, [_c.c_void_p]),
     "molten_kernel_info": (_c.c_int, [_c.c_void_p, _c.c_char_p, _c.POINTER(_c.c_int),
                                       _c.POINTER(_c.c_int), _c.POINTER(_c.c_int)]),
+    "molten_max_resident": (_c.c_int, [_c.c_void_p, _c.c_char_p, _c.c_void_p,
+                                       _c.POINTER(_c.c_int), _c.POINTER(_c.c_int)]),
     "molten_launch": (_c.c_int, [_c.c_void_p, _c.c_char_p, _c.c_void_p, _c.c_void_p,
                                  _c.c_size_t, _c.c_void_p]),
     "molten_encode_tma_2d": (_c.c_int, [_c.c_void_p, _c.c_int, _c.c_void_p, _c.c_uint64,
@@ -125,6 +127,14 @@ class Module:
                                           ctypes.byref(thr), ctypes.byref(smem)),
               f"kernel info of {name}")
         return {"registers": regs.value, "max_threads": thr.value, "static_smem": smem.value}
+
+    def max_resident(self, name: bytes, cfg: LaunchCfg) -> tuple:
+        """(CTAs per SM, clusters on the device) that fit at once with cfg."""
+        per_sm, clusters = ctypes.c_int(), ctypes.c_int()
+        check(self.lib.molten_max_resident(self.handle, name, ctypes.byref(cfg),
+                                           ctypes.byref(per_sm), ctypes.byref(clusters)),
+              f"occupancy of {name.decode()}")
+        return per_sm.value, clusters.value
 
     def launch(self, name: bytes, cfg: LaunchCfg, params, stream: int) -> None:
         rc = self.lib.molten_launch(self.handle, name, ctypes.byref(cfg), ctypes.byref(params),

@@ -15,7 +15,12 @@ typedef __half f16;
 
 // ---------------------------------------------------------------- conversion
 __device__ __forceinline__ float to_f32(float v) { return v; }
-__device__ __forceinline__ float to_f32(bf16 v) { return __bfloat162float(v); }
+// bf16 is the upper half of an fp32: widening is a 16-bit shift (integer
+// pipe), exact, instead of a conversion instruction on the transcendental
+// pipe that the exponentials of softmax already load.
+__device__ __forceinline__ float to_f32(bf16 v) {
+  return __uint_as_float(static_cast<uint32_t>(__bfloat16_as_ushort(v)) << 16);
+}
 __device__ __forceinline__ float to_f32(f16 v) { return __half2float(v); }
 
 template <typename T> __device__ __forceinline__ T from_f32(float v);

@@ -24,7 +24,7 @@ struct RowArgs {
   long long rows;                  // rows handled by this launch
   long long row_offset;            // global index of this launch's row 0
   long long cols;                  // elements per row (must equal COLS)
-  int* status;                     // unused by row kernels; may be null
+  int* status;                     // wait-timeout bits (bounded waits); may be null
 };
 
 // ------------------------------------------------------------ reductions
@@ -62,6 +62,100 @@ __device__ __forceinline__ float ld_dsmem(const float* local, unsigned rank) {
   return v;
 }
 
+// ------------------------------------------- per-thread row staging (stream)
+// In the persistent "stream" form of a row kernel every thread copies its
+// own slots of the rows ahead into its own shared-memory lanes with
+// cp.async (16 bytes per copy, L1 bypassed), one commit group per row.
+// Only the issuing thread reads what it copied, so cp.async.wait_group is
+// the whole synchronisation; no registers are held by the copies in flight.
+__device__ __forceinline__ uint32_t shared_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" :: "r"(dst), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory");
+}
+template <typename T, int VEC>
+__device__ __forceinline__ Slot<T, VEC> lds_slot16(uint32_t addr) {
+  static_assert(sizeof(T) * VEC == 16, "staged slots are 16 bytes");
+  Slot<T, VEC> s;
+  uint4 r;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(addr) : "memory");
+  *reinterpret_cast<uint4*>(&s) = r;
+  return s;
+}
+
+// ------------------------------------------------- push-style cluster exchange
+// A persistent row kernel stores row n's outputs right before row n+1's
+// reductions.  A barrier.cluster round there would be a release fence behind
+// those stores; instead each CTA pushes its partials into its peers' shared
+// memory with st.async, which completes bytes on the receiving CTA's
+// mbarrier, and waits only on its own barrier.  One barrier per exchange
+// area, armed once per use by thread 0 of the receiving CTA; areas alternate
+// with the row's parity, so phase (use count & 1) of an area never mixes
+// rows.  Waits are bounded by a number of polls; on timeout the CTA raises a
+// shared abort flag, skips all later waits, and the kernel reports
+// kRowTimeoutExchange in *status when it ends (a timer-bounded loop or a
+// status atomic inside the wait costs ~48 registers in the row kernels).
+enum RowExchangeStatus { kRowTimeoutExchange = 128 };
+
+#ifndef MOLTEN_ROW_WAIT_TRIES
+#define MOLTEN_ROW_WAIT_TRIES (1u << 22)   // try_wait polls before a wait gives up
+#endif
+
+struct ClusterExchange {
+  float* slots;          // [areas][RPC][CL][nr_max] floats
+  uint32_t bars;         // shared address of the areas' mbarriers (8 bytes each)
+  int nr_max;            // slot stride (largest NR of any call)
+  volatile int* abort;   // shared flag: a wait timed out
+};
+
+__device__ __forceinline__ uint32_t mapa_u32(uint32_t local, unsigned rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_async_f32(uint32_t remote, float v, uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f32 [%0], %1, [%2];"
+               :: "r"(remote), "f"(v), "r"(remote_bar) : "memory");
+}
+__device__ __forceinline__ void xch_init(uint32_t bar) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" :: "r"(bar) : "memory");
+}
+__device__ __forceinline__ void xch_init_fence() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void xch_arm(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool xch_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile("{\n\t.reg .pred p;\n\t"
+               "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+               "selp.u32 %0, 1, 0, p;\n\t}"
+               : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+  return ok != 0;
+}
+// Wait for the phase of `parity` to complete; false on timeout (or when an
+// earlier wait of this CTA timed out).
+__device__ __forceinline__ bool xch_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+  if (xch_try_wait(bar, parity)) return true;
+  if (*abort) return false;
+  for (uint32_t i = 0; i < MOLTEN_ROW_WAIT_TRIES; ++i)
+    if (xch_try_wait(bar, parity)) return true;
+  *abort = 1;
+  return false;
+}
+
 template <int TPC, int RPC, int CL>
 struct RowTeam {
   static constexpr int BLOCK = TPC * RPC;
@@ -94,20 +188,16 @@ struct RowTeam {
     return (rank * TPC + t) + k * (TPC * CL);
   }
 
-  // All-reduce NR values across the row team (all CTAs of the cluster).
+  // Levels 1-2 of every all-reduce: inside the warp (or sub-warp team), then
+  // across the warps of the team through `smem` (RPC * WPR * NR floats).
   // Every thread of the CTA must call this (idle teams pass neutral values).
-  // `smem` must hold smem_floats(NR, passes) floats; `pass` selects the
-  // cluster exchange area so consecutive passes never overwrite a value a
-  // peer CTA may still be reading.
   template <int NR, class Op>
-  __device__ __forceinline__ void reduce(float (&v)[NR], Op op, float* smem, int pass) const {
-    // 1) inside the warp (or the sub-warp team)
+  __device__ __forceinline__ void reduce_cta(float (&v)[NR], Op op, float* smem) const {
     constexpr int W = TPC < 32 ? TPC : 32;
 #pragma unroll
     for (int off = W / 2; off > 0; off >>= 1)
 #pragma unroll
       for (int i = 0; i < NR; ++i) v[i] = op(v[i], __shfl_xor_sync(0xffffffffu, v[i], off));
-    // 2) across the warps of the team
     if constexpr (WPR > 1) {
       const int warp = t / 32, lane = t % 32;
       float* red = smem + team * WPR * NR;
@@ -137,9 +227,18 @@ struct RowTeam {
           v[i] = a;
         }
       }
-      __syncthreads();   // the area is reused by the next pass
+      __syncthreads();   // the area is reused by the next call
     }
-    // 3) across the CTAs of the cluster
+  }
+
+  // All-reduce NR values across the row team (all CTAs of the cluster).
+  // `smem` must hold smem_floats(NR, calls) floats; `pass` selects the
+  // cluster exchange area so consecutive calls never overwrite a value a
+  // peer CTA may still be reading.  The cluster level is a
+  // barrier.cluster round (release/acquire).
+  template <int NR, class Op>
+  __device__ __forceinline__ void reduce(float (&v)[NR], Op op, float* smem, int pass) const {
+    reduce_cta<NR>(v, op, smem);
     if constexpr (CL > 1) {
       float* part = smem + RPC * WPR * NR + pass * RPC * NR + team * NR;
       if (t == 0) {
@@ -158,6 +257,27 @@ struct RowTeam {
     }
   }
 
+  // Same, with the cluster level done by pushing (see ClusterExchange):
+  // no barrier.cluster and so no release fence behind earlier global stores.
+  template <int NR, class Op>
+  __device__ __forceinline__ void reduce_push(float (&v)[NR], Op op, float* smem,
+                                              const ClusterExchange& x, int area,
+                                              uint32_t phase) const {
+    reduce_cta<NR>(v, op, smem);
+    if constexpr (CL > 1) {
+      const float* slots = exchange<NR>(v, x, area, phase);
+      float a[NR];
+#pragma unroll
+      for (int i = 0; i < NR; ++i) a[i] = rank == 0 ? v[i] : slots[i];
+#pragma unroll
+      for (int r = 1; r < CL; ++r)
+#pragma unroll
+        for (int i = 0; i < NR; ++i) a[i] = op(a[i], r == rank ? v[i] : slots[r * x.nr_max + i]);
+#pragma unroll
+      for (int i = 0; i < NR; ++i) v[i] = a[i];
+    }
+  }
+
   // (max, sum-of-exponentials) pair of one softmax row, combined across the
   // team: (m1, s1) + (m2, s2) = (M, s1 e^(m1-M) + s2 e^(m2-M)), M = max.
   // A side whose max is -inf (all its elements masked) contributes 0.
@@ -169,9 +289,8 @@ struct RowTeam {
     s = a + b;
   }
 
-  // All-reduce of one softmax (max, sum) pair per row, in the same three
-  // levels as `reduce` (uses 2 floats per warp / per CTA of `smem`).
-  __device__ __forceinline__ void reduce_softmax(float& m, float& s, float* smem, int pass) const {
+  // Levels 1-2 of the softmax pair reduction (2 floats per warp of `smem`).
+  __device__ __forceinline__ void softmax_cta(float& m, float& s, float* smem) const {
     constexpr int W = TPC < 32 ? TPC : 32;
 #pragma unroll
     for (int off = W / 2; off > 0; off >>= 1) {
@@ -203,6 +322,12 @@ struct RowTeam {
       s = S;
       __syncthreads();
     }
+  }
+
+  // All-reduce of one softmax (max, sum) pair per row, in the same three
+  // levels as `reduce`.
+  __device__ __forceinline__ void reduce_softmax(float& m, float& s, float* smem, int pass) const {
+    softmax_cta(m, s, smem);
     if constexpr (CL > 1) {
       float* part = smem + RPC * WPR * 2 + pass * RPC * 2 + team * 2;
       if (t == 0) {
@@ -217,6 +342,50 @@ struct RowTeam {
       m = M;
       s = S;
     }
+  }
+
+  // Same, with the cluster level done by pushing.  Pairs are combined in
+  // rank order in every CTA, so all CTAs of the cluster get identical bits.
+  __device__ __forceinline__ void reduce_softmax_push(float& m, float& s, float* smem,
+                                                      const ClusterExchange& x, int area,
+                                                      uint32_t phase) const {
+    softmax_cta(m, s, smem);
+    if constexpr (CL > 1) {
+      float v[2] = {m, s};
+      const float* slots = exchange<2>(v, x, area, phase);
+      float M = rank == 0 ? m : slots[0], S = rank == 0 ? s : slots[1];
+#pragma unroll
+      for (int r = 1; r < CL; ++r)
+        softmax_combine(M, S, r == rank ? m : slots[r * x.nr_max],
+                        r == rank ? s : slots[r * x.nr_max + 1]);
+      m = M;
+      s = S;
+    }
+  }
+
+  // Push this team's NR values into slot `rank` of the team's area in every
+  // peer CTA (st.async, completing bytes on the peer's mbarrier of the
+  // area), then wait for the peers' values to land in this CTA's area.
+  // Returns the team's CL slots (stride x.nr_max).  Thread 0 of the CTA arms
+  // the area's barrier for RPC * (CL - 1) * NR * 4 bytes.
+  template <int NR>
+  __device__ __forceinline__ const float* exchange(const float (&v)[NR], const ClusterExchange& x,
+                                                   int area, uint32_t phase) const {
+    const uint32_t bar = x.bars + 8u * (uint32_t)area;
+    float* slots = x.slots + ((area * RPC + team) * CL) * x.nr_max;
+    if (threadIdx.x == 0) xch_arm(bar, (uint32_t)(RPC * (CL - 1) * NR * 4));
+    if (t == 0) {
+      const uint32_t mine = shared_addr(slots + rank * x.nr_max);
+#pragma unroll
+      for (int r = 0; r < CL; ++r) {
+        if (r == rank) continue;
+        const uint32_t dst = mapa_u32(mine, (unsigned)r), rbar = mapa_u32(bar, (unsigned)r);
+#pragma unroll
+        for (int i = 0; i < NR; ++i) st_async_f32(dst + 4u * i, v[i], rbar);
+      }
+    }
+    xch_wait(bar, phase, x.abort);
+    return slots;
   }
 
   // A CTA of a cluster must not exit while a peer may still read its shared

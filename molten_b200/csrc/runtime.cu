@@ -42,6 +42,8 @@ typedef CUresult (*PFN_FuncSetAttribute)(CUfunction, CUfunction_attribute, int);
 typedef CUresult (*PFN_FuncGetAttribute)(int*, CUfunction_attribute, CUfunction);
 typedef CUresult (*PFN_LaunchKernelEx)(const CUlaunchConfig*, CUfunction, void**, void**);
 typedef CUresult (*PFN_FuncGetParamInfo)(CUfunction, size_t, size_t*, size_t*);
+typedef CUresult (*PFN_OccupancyBlocks)(int*, CUfunction, int, size_t);
+typedef CUresult (*PFN_OccupancyClusters)(int*, CUfunction, const CUlaunchConfig*);
 typedef CUresult (*PFN_TensorMapEncodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                              const cuuint64_t*, const cuuint64_t*,
                                              const cuuint32_t*, const cuuint32_t*,
@@ -57,6 +59,8 @@ struct Driver {
   PFN_FuncGetAttribute func_get_attribute = nullptr;
   PFN_LaunchKernelEx launch_kernel_ex = nullptr;
   PFN_FuncGetParamInfo func_get_param_info = nullptr;   // optional (12.4+)
+  PFN_OccupancyBlocks occupancy_blocks = nullptr;
+  PFN_OccupancyClusters occupancy_clusters = nullptr;
   PFN_TensorMapEncodeTiled tensor_map_encode_tiled = nullptr;
   bool ok = false;
   std::string error;
@@ -87,7 +91,10 @@ Driver& driver() {
               resolve("cuFuncSetAttribute", &d.func_set_attribute, true, &err) &&
               resolve("cuFuncGetAttribute", &d.func_get_attribute, true, &err) &&
               resolve("cuLaunchKernelEx", &d.launch_kernel_ex, true, &err) &&
-              resolve("cuTensorMapEncodeTiled", &d.tensor_map_encode_tiled, true, &err);
+              resolve("cuTensorMapEncodeTiled", &d.tensor_map_encode_tiled, true, &err) &&
+              resolve("cuOccupancyMaxActiveBlocksPerMultiprocessor", &d.occupancy_blocks, true,
+                      &err) &&
+              resolve("cuOccupancyMaxActiveClusters", &d.occupancy_clusters, true, &err);
     resolve("cuFuncGetParamInfo", &d.func_get_param_info, false, &err);
     d.ok = ok;
     d.error = err;
@@ -253,6 +260,71 @@ int molten_kernel_info(void* mod, const char* kernel, int* num_regs, int* max_th
   return MOLTEN_OK;
 }
 
+// Allow `smem` bytes of dynamic shared memory for kernel `k`, once per size
+// increase.  Any nonzero request is set explicitly: the 48 KB default
+// counts static plus dynamic shared memory, so 48 KB of dynamic memory next
+// to a few static bytes already needs the opt-in.
+static int ensure_dynamic_smem(Module* m, Kernel* k, uint32_t smem) {
+  if (smem > 0 && (int)smem > k->smem_set) {
+    std::lock_guard<std::mutex> lock(m->mu);
+    CUresult r = driver().func_set_attribute(k->fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES,
+                                             (int)smem);
+    if (r != CUDA_SUCCESS) return drv_fail(r, "cuFuncSetAttribute(max dynamic smem)");
+    k->smem_set = (int)smem;
+  }
+  return MOLTEN_OK;
+}
+
+int molten_max_resident(void* mod, const char* kernel, const molten_launch_cfg* cfg,
+                        int* ctas_per_sm, int* clusters) {
+  if (!mod || !kernel || !cfg) return fail(MOLTEN_ERR_INVALID, "null module, kernel or config");
+  Module* m = static_cast<Module*>(mod);
+  const uint32_t block = cfg->block[0] * cfg->block[1] * cfg->block[2];
+  const uint32_t cl = cfg->cluster[0] * cfg->cluster[1] * cfg->cluster[2];
+  if (block == 0 || block > 1024) return fail(MOLTEN_ERR_INVALID, "bad block size");
+  Kernel* k = nullptr;
+  int rc = lookup(m, kernel, &k);
+  if (rc) return rc;
+  rc = use_device(m->device);
+  if (rc) return rc;
+  rc = ensure_dynamic_smem(m, k, cfg->smem_bytes);
+  if (rc) return rc;
+  int per_sm = 0;
+  CUresult r = driver().occupancy_blocks(&per_sm, k->fn, (int)block, cfg->smem_bytes);
+  if (r != CUDA_SUCCESS) return drv_fail(r, "cuOccupancyMaxActiveBlocksPerMultiprocessor");
+  if (ctas_per_sm) *ctas_per_sm = per_sm;
+  if (clusters) {
+    int n = 0;
+    if (cl > 1) {
+      CUlaunchConfig lc;
+      std::memset(&lc, 0, sizeof(lc));
+      lc.gridDimX = cfg->cluster[0];
+      lc.gridDimY = cfg->cluster[1];
+      lc.gridDimZ = cfg->cluster[2];
+      lc.blockDimX = cfg->block[0];
+      lc.blockDimY = cfg->block[1];
+      lc.blockDimZ = cfg->block[2];
+      lc.sharedMemBytes = cfg->smem_bytes;
+      CUlaunchAttribute attr[1];
+      attr[0].id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
+      attr[0].value.clusterDim.x = cfg->cluster[0];
+      attr[0].value.clusterDim.y = cfg->cluster[1];
+      attr[0].value.clusterDim.z = cfg->cluster[2];
+      lc.attrs = attr;
+      lc.numAttrs = 1;
+      r = driver().occupancy_clusters(&n, k->fn, &lc);
+      if (r != CUDA_SUCCESS) return drv_fail(r, "cuOccupancyMaxActiveClusters");
+    } else {
+      int sms = 0;
+      cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, m->device);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
+      n = per_sm * sms;
+    }
+    *clusters = n;
+  }
+  return MOLTEN_OK;
+}
+
 int molten_launch(void* mod, const char* kernel, const molten_launch_cfg* cfg,
                   const void* params, size_t params_bytes, void* stream) {
   if (!mod || !kernel || !cfg || !params)
@@ -279,13 +351,8 @@ int molten_launch(void* mod, const char* kernel, const molten_launch_cfg* cfg,
                                         std::to_string(params_bytes));
   rc = use_device(m->device, 0);
   if (rc) return rc;
-  if (cfg->smem_bytes > 48 * 1024 && (int)cfg->smem_bytes > k->smem_set) {
-    std::lock_guard<std::mutex> lock(m->mu);
-    CUresult r = driver().func_set_attribute(k->fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES,
-                                             (int)cfg->smem_bytes);
-    if (r != CUDA_SUCCESS) return drv_fail(r, "cuFuncSetAttribute(max dynamic smem)");
-    k->smem_set = (int)cfg->smem_bytes;
-  }
+  rc = ensure_dynamic_smem(m, k, cfg->smem_bytes);
+  if (rc) return rc;
   CUlaunchConfig lc;
   std::memset(&lc, 0, sizeof(lc));
   lc.gridDimX = cfg->grid[0];

@@ -205,9 +205,28 @@ class _Emitter:
 
 
 def emit_row(sk: SubKernel, name: str) -> str:
+    """Register-resident row kernel.
+
+    Default form: one team of TPC threads (in CL CTAs of a cluster) per row,
+    RPC teams per CTA, one launch-wide pass over the rows.
+
+    ``config["stream"] = S > 0``: a persistent form for long rows.  The grid
+    is sized to what is resident; each team walks rows ``base0 + i * step``
+    and every thread copies its own slots of the next S-1 rows into shared
+    memory with cp.async (one commit group per row), so HBM reads stay in
+    flight through the current row's reductions, barriers and stores.
+    Row-invariant operands are loaded once.  With a cluster, partials are
+    pushed into the peers' shared memory (st.async completing on the
+    receiver's mbarrier) instead of a barrier.cluster round, whose release
+    fence would wait for the previous row's output stores.  Exchange areas
+    alternate with the row's parity: a peer pushes row n+2's partials into an
+    area only after this CTA's row n+1 push, which follows its reads of row
+    n's values there.
+    """
     e = _Emitter(sk, name)
     cfg = sk.config
     VEC, NV, TPC, RPC, CL = cfg["vec"], cfg["nv"], cfg["tpc"], cfg["rpc"], cfg["cl"]
+    stream = int(cfg.get("stream", 0) or 0)
     prefetch = set(cfg["prefetch"])
     materialize = {int(v): int(p) for v, p in cfg["materialize"]}
     values = sk.values
@@ -219,14 +238,14 @@ def emit_row(sk: SubKernel, name: str) -> str:
         v = values[vid]
         if v.op in ("rsum", "rmax", "rmin"):
             reds[v.avail - 1].append(vid)
-    smx = {p: [] for p in range(sk.passes)}
-    for vid in sorted(needed):
-        if values[vid].op == "softmax":
-            smx[values[vid].avail - 1].append(vid)
-    # one exchange area per reduce call
+    smx = smx_of(values, needed, sk.passes)
+    # one exchange area per reduce call (two sets in the stream form)
     n_calls = sum(len({values[r].op for r in rs}) for rs in reds.values())
     n_calls += sum(len(v) for v in smx.values())
+    n_calls = max(n_calls, 1)
     max_nr = max([len(rs) for rs in reds.values()] + [2 if any(smx.values()) else 1]) or 1
+    n_areas = n_calls * (2 if stream else 1)
+    masked_only = _causal_masked_only_operands(sk, closures, reds, smx, materialize)
 
     e.header("row")
     e.w("using namespace molten;")
@@ -239,16 +258,152 @@ def emit_row(sk: SubKernel, name: str) -> str:
     e.w(f"  constexpr long long COLS = {sk.cols}LL;")
     e.w(f"  constexpr int NVEC = {cfg['nvec']};")
     e.w("  typedef RowTeam<TPC, RPC, CL> Team;")
-    e.w(f"  __shared__ float red_smem[Team::smem_floats({max_nr}, {max(n_calls, 1)}) > 0 ? "
-        f"Team::smem_floats({max_nr}, {max(n_calls, 1)}) : 1];")
+    e.w(f"  __shared__ float red_smem[Team::smem_floats({max_nr}, {n_areas}) > 0 ? "
+        f"Team::smem_floats({max_nr}, {n_areas}) : 1];")
     e.w("  const Team tm(args.rows, 0);")
-    e.w("  const long long lrow = tm.row;")
-    e.w("  const long long grow = args.row_offset + lrow;")
-    e.w("  const bool rok = tm.row_ok;")
-    e.w("  (void)grow;")
+    body = dict(closures=closures, reds=reds, smx=smx, materialize=materialize,
+                prefetch=prefetch, masked_only=masked_only)
+    if not stream:
+        e.w("  const long long lrow = tm.row;")
+        e.w("  const long long grow = args.row_offset + lrow;")
+        e.w("  const bool rok = tm.row_ok;")
+        e.w("  (void)grow;")
+        _emit_row_body(e, staged=[], area=lambda c: f"{c}", done_early=True, **body)
+        e.w("  tm.cluster_done_wait();")
+        e.w("}")
+        return "\n".join(e.lines) + "\n"
+
+    staged = [i for i in sorted(prefetch) if sk.operands[i].row_map != "zero"]
+    hoisted = [i for i in sorted(prefetch) if i not in staged]
+    if not staged:
+        raise LoweringError("the stream form needs a row-indexed streamed operand")
+    e.w(f"  constexpr int STAGES = {stream}, NSTAGED = {len(staged)};")
+    e.w("  constexpr uint32_t STAGE_BYTES = NSTAGED * NV * (TPC * RPC) * 16u;")
+    e.w("  extern __shared__ __align__(16) uint8_t stage_smem[];")
+    e.w("  const uint32_t lanes = shared_addr(stage_smem) + threadIdx.x * 16u;")
+    e.w("  const long long step = (long long)(gridDim.x / CL) * RPC;")
+    e.w("  const long long base0 = (long long)(blockIdx.x / CL) * RPC;")
+    for i in hoisted:
+        # row-invariant streamed operand: loaded once for every row
+        opd = sk.operands[i]
+        ct = _ctype(opd.dtype)
+        e.w(f"  Slot<{ct}, VEC> s{i}[NV];")
+        e.w("  {")
+        e.w(f"    const {ct}* __restrict__ src = static_cast<const {ct}*>(args.in[{i}]);")
+        e.w("#pragma unroll")
+        e.w("    for (int k = 0; k < NV; ++k) {")
+        e.w("      const int j = tm.slot(k);")
+        e.w(f"      if (j < NVEC) s{i}[k] = load_slot<kLoadDefault, {ct}, VEC>(src + j * VEC);")
+        e.w("    }")
+        e.w("  }")
+    push = CL > 1
+    if push:
+        # cluster partials are pushed (st.async + mbarrier), not exchanged
+        # behind a barrier.cluster round
+        e.w(f"  constexpr int NAREAS = {n_areas}, XNR = {max_nr};")
+        e.w("  __shared__ float xslots[NAREAS * RPC * CL * XNR];")
+        e.w("  __shared__ __align__(8) unsigned long long xbar[NAREAS];")
+        e.w("  __shared__ int xabort;")
+        e.w("  if (threadIdx.x == 0) {")
+        e.w("    for (int a = 0; a < NAREAS; ++a) xch_init(shared_addr(&xbar[a]));")
+        e.w("    xabort = 0;")
+        e.w("    xch_init_fence();")
+        e.w("  }")
+        e.w("  cluster_arrive();          // every peer's barriers exist before the first push")
+    e.w("#pragma unroll 1")
+    e.w("  for (int s = 0; s < STAGES - 1; ++s) {")
+    _emit_stage_row(e, staged, masked_only, "base0 + s * step + tm.team", "s", "    ")
+    e.w("    cp_async_commit();")
+    e.w("  }")
+    if push:
+        e.w("  cluster_wait();")
+        e.w("  const ClusterExchange xch{xslots, shared_addr(xbar), XNR, &xabort};")
+    e.w("  int st = 0;")
+    e.w("  uint32_t use = 0;")
+    e.w("#pragma unroll 1")
+    e.w("  for (long long base = base0; base < args.rows; base += step) {")
+    e.w("    const uint32_t par = use & 1u, xph = (use >> 1) & 1u;   // area set, barrier phase")
+    e.w("    (void)par; (void)xph;")
+    e.w("    // the row STAGES-1 ahead goes into the stage read one row ago")
+    _emit_stage_row(e, staged, masked_only, "base + (STAGES - 1) * step + tm.team",
+                    "(st == 0 ? STAGES - 1 : st - 1)", "    ")
+    e.w("    cp_async_commit();")
+    e.w("    cp_async_wait<STAGES - 1>();        // this thread's copies of row `base` landed")
+    e.w("    const long long lrow = base + tm.team;")
+    e.w("    const long long grow = args.row_offset + lrow;")
+    e.w("    const bool rok = lrow < args.rows;")
+    e.w("    (void)grow;")
+    mark = len(e.lines)
+    _emit_row_body(e, staged=staged, area=lambda c: f"{c} + (int)par * {n_calls}",
+                   done_early=False, push=push, **body)
+    e.lines[mark:] = [ln if ln.startswith("#") else "  " + ln for ln in e.lines[mark:]]
+    e.w("    st = (st + 1 == STAGES) ? 0 : st + 1;")
+    e.w("    ++use;")
+    e.w("  }")
+    e.w("  cp_async_wait<0>();")
+    if push:
+        e.w("  if (threadIdx.x == 0 && xabort && args.status) atomicOr(args.status, kRowTimeoutExchange);")
+    e.w("  tm.cluster_done_arrive();")
+    e.w("  tm.cluster_done_wait();")
+    e.w("}")
+    return "\n".join(e.lines) + "\n"
+
+
+def _emit_stage_row(e: _Emitter, staged, masked_only, row_expr: str, stage_expr: str, indent: str):
+    """cp.async this thread's slots of local row ``row_expr`` (if it exists)
+    into stage ``stage_expr``: staged operand p, slot k at lane offset
+    ((p * NV + k) * BLOCK) * 16.  Slots a causal softmax never reads are not
+    copied."""
+    sk = e.sk
+
+    def w(s):
+        e.w(indent + s)
+
+    w("{")
+    w(f"  const long long fr = {row_expr};")
+    w("  if (fr < args.rows) {")
+    w("    const long long fg = args.row_offset + fr;")
+    w("    (void)fg;")
+    for mk in sorted({masked_only[i] for i in staged if i in masked_only}):
+        v = e.values[mk]
+        period = _mask_period(v, sk.cols)
+        off = int(v.attrs.get("offset", 0))
+        w(f"    const int fl{mk} = clamp_col_limit((fg % {period}LL) + ({off}LL));")
+    for i in staged:
+        opd = sk.operands[i]
+        ct = _ctype(opd.dtype)
+        # one base per row; slot k is a constant stride further
+        w(f"    const {ct}* __restrict__ src{i} = static_cast<const {ct}*>(args.in[{i}]) + "
+          f"({_row_index_expr(opd, 'fr', 'fg')} * COLS + (long long)tm.slot(0) * VEC);")
+    w(f"    const uint32_t dst = lanes + (uint32_t)({stage_expr}) * STAGE_BYTES;")
+    e.w("#pragma unroll")
+    w("    for (int k = 0; k < NV; ++k) {")
+    w("      const int j = tm.slot(k);")
+    w("      if (j < NVEC) {")
+    for p, i in enumerate(staged):
+        cp = (f"cp_async16(dst + (uint32_t)(({p} * NV + k) * (TPC * RPC) * 16), "
+              f"src{i} + k * (TPC * CL * VEC));")
+        if i in masked_only:
+            w(f"        if (j * VEC <= fl{masked_only[i]}) {cp}")
+        else:
+            w(f"        {cp}")
+    w("      }")
+    w("    }")
+    w("  }")
+    w("}")
+
+
+def _emit_row_body(e: _Emitter, closures, reds, smx, materialize, prefetch, masked_only, staged,
+                   area, done_early: bool, push: bool = False):
+    """Everything a team does for its current row (``lrow``/``grow``/``rok``
+    in scope): pointers, per-row leaves, the streamed slots (global loads, or
+    shared-memory reads of the staged copies), the reduction passes and the
+    outputs."""
+    sk = e.sk
+    values = sk.values
+    needed = e.needed
     e.pointers("lrow", "grow", "rok")
     e.row_leaves(prefetch)
-    # row-level values available from the start
     emitted_rows = set()
 
     def emit_rows_at(p):
@@ -260,36 +415,38 @@ def emit_row(sk: SubKernel, name: str) -> str:
                 emitted_rows.add(vid)
 
     emit_rows_at(0)
-    # prefetch the row-streamed operands
-    for opd in sk.operands:
-        if opd.index in prefetch:
-            ct = _ctype(opd.dtype)
-            e.w(f"  Slot<{ct}, VEC> s{opd.index}[NV];")
-    masked_only = _causal_masked_only_operands(sk, closures, reds, smx_of(values, needed, sk.passes),
-                                               materialize)
-    if prefetch:
+    # the row-streamed operands: into registers (row-invariant ones of the
+    # stream form are already there)
+    per_row = [i for i in sorted(prefetch) if not staged or i in staged]
+    for i in per_row:
+        e.w(f"  Slot<{_ctype(sk.operands[i].dtype)}, VEC> s{i}[NV];")
+    if per_row:
         e.w("#pragma unroll")
         e.w("  for (int k = 0; k < NV; ++k) {")
         e.w("    const int j = tm.slot(k);")
         e.w("    if (rok && j < NVEC) {")
-        for opd in sk.operands:
-            if opd.index in prefetch:
+        for i in per_row:
+            opd = sk.operands[i]
+            ct = _ctype(opd.dtype)
+            if staged:
+                p = staged.index(i)
+                load = (f"s{i}[k] = lds_slot16<{ct}, VEC>(lanes + (uint32_t)(st * STAGE_BYTES + "
+                        f"({p} * NV + k) * (TPC * RPC) * 16));")
+            else:
                 hint = _LOAD_HINT[opd.row_map == "full"]
-                load = (f"s{opd.index}[k] = load_slot<{hint}, {_ctype(opd.dtype)}, VEC>"
-                        f"(in{opd.index} + j * VEC);")
-                if opd.index in masked_only:
-                    # only the causal softmax reads it: columns above the
-                    # row's limit are never needed, so they are not loaded
-                    e.w(f"      if (j * VEC <= mlim{masked_only[opd.index]}) {load}")
-                else:
-                    e.w(f"      {load}")
+                load = f"s{i}[k] = load_slot<{hint}, {ct}, VEC>(in{i} + j * VEC);"
+            if i in masked_only:
+                # only the causal softmax reads it: columns above the
+                # row's limit are never needed, so they are not loaded
+                e.w(f"      if (j * VEC <= mlim{masked_only[i]}) {load}")
+            else:
+                e.w(f"      {load}")
         e.w("    }")
         e.w("  }")
     for vid in sorted(materialize):
         e.w(f"  float m{vid}[NV][VEC];")
     mat_ready = set()
     call = 0
-    EXP = "expf" if sk.precise else "__expf"
     for p in range(sk.passes):
         rs = reds[p]
         e.w(f"  // ---- pass {p}: " + ", ".join(f"{values[r].op}(v{values[r].args[0]})"
@@ -332,7 +489,10 @@ def emit_row(sk: SubKernel, name: str) -> str:
         for v in smx[p]:
             # step 3: one pair reduction per row; scale = e^(m_thread - M) / S
             e.w(f"  float gm{v} = lm{v}, gs{v} = ls{v};")
-            e.w(f"  tm.reduce_softmax(gm{v}, gs{v}, red_smem, {call});")
+            if push:
+                e.w(f"  tm.reduce_softmax_push(gm{v}, gs{v}, red_smem, xch, {area(call)}, xph);")
+            else:
+                e.w(f"  tm.reduce_softmax(gm{v}, gs{v}, red_smem, {area(call)});")
             e.w(f"  const float sc{v} = (gs{v} > 0.0f) ? ((lm{v} == (-INFINITY)) ? 0.0f : "
                 f"fast_exp2((lm{v} - gm{v}) * MOLTEN_LOG2E) / gs{v}) : NAN;")
             call += 1
@@ -344,13 +504,17 @@ def emit_row(sk: SubKernel, name: str) -> str:
             nr = len(group)
             e.w("  {")
             e.w(f"    float red[{nr}] = {{" + ", ".join(f"v{r}" for r in group) + "};")
-            e.w(f"    tm.reduce<{nr}>(red, {_RED_OP[op]}{{}}, red_smem, {call});")
+            if push:
+                e.w(f"    tm.reduce_push<{nr}>(red, {_RED_OP[op]}{{}}, red_smem, xch, {area(call)}, xph);")
+            else:
+                e.w(f"    tm.reduce<{nr}>(red, {_RED_OP[op]}{{}}, red_smem, {area(call)});")
             for i, r in enumerate(group):
                 e.w(f"    v{r} = red[{i}];")
             e.w("  }")
             call += 1
         emit_rows_at(p + 1)
-    e.w("  tm.cluster_done_arrive();")
+    if done_early:
+        e.w("  tm.cluster_done_arrive();")
     # ---- final pass: outputs
     fin = set(closures[sk.passes])
     full_outs = [o for o in sk.outputs if o.kind == "full"]
@@ -382,9 +546,6 @@ def emit_row(sk: SubKernel, name: str) -> str:
         if o.kind == "row":
             src = e.leaf(sk.out_values[o.index], False, prefetch, set(), set())
             e.w(f"  if (rok && tm.t == 0 && tm.rank == 0) store_scalar(out{o.index}, {src});")
-    e.w("  tm.cluster_done_wait();")
-    e.w("}")
-    return "\n".join(e.lines) + "\n"
 
 
 def _emit_nonprefetched_loads(e: _Emitter, targets, prefetch, indent):

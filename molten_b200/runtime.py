@@ -100,11 +100,19 @@ class _Spec:
             cfg.cluster[:] = [1, 1, 1]
             cfg.smem_bytes = c["smem"]
         elif sk.family == "row":
-            grid = (-(-sk.rows // c["rpc"])) * c["cl"]
-            cfg.grid[:] = [max(1, grid), 1, 1]
+            teams = -(-sk.rows // c["rpc"])
             cfg.block[:] = [c["block"], 1, 1]
             cfg.cluster[:] = [c["cl"], 1, 1] if c["cl"] > 1 else [1, 1, 1]
-            cfg.smem_bytes = 0
+            cfg.smem_bytes = c.get("smem", 0) if c.get("stream") else 0
+            if c.get("stream"):
+                # persistent: as many teams (clusters) as are resident at once,
+                # never more -- a late wave would walk as many rows again
+                _, resident = self.module(device).max_resident(self.entries[i], cfg)
+                if resident < 1:
+                    raise _capi.MoltenError(f"kernel {self.entries[i].decode()} cannot be "
+                                            f"resident with {cfg.smem_bytes} bytes of shared memory")
+                teams = min(teams, resident)
+            cfg.grid[:] = [max(1, teams * c["cl"]), 1, 1]
         elif sk.family == "ew":
             rb = -(-sk.rows // (c["rpc"] * c["upt"]))
             cfg.grid[:] = [c["tiles"], max(1, min(rb, 65535)), 1]
@@ -166,7 +174,7 @@ class _Spec:
             else:
                 a = _capi.RowArgs()
                 a.rows, a.cols = sk.rows, sk.cols
-                if sk.config.get("engine") == "tma":
+                if sk.config.get("engine") == "tma" or sk.config.get("stream"):
                     a.status = _capi.status_word(di)
             a.row_offset = row_offset
             ins_al, outs_al = self.align[i]

@@ -111,6 +111,37 @@ def test_long_rows_use_a_cluster():
     assert sk.config["cl"] > 1 and k.config.cluster_x == sk.config["cl"]
 
 
+def test_long_16bit_rows_take_the_stream_form():
+    """bf16 rows long enough for a cluster run as one 1024-thread CTA per
+    row in the persistent stream form; fp32 rows keep the cluster."""
+    sk = compile_graph(graphs.softmax((4096, 32768), dtype="bfloat16"), dtype="bfloat16")[0] \
+        .plan.kernels[0]
+    assert (sk.config["tpc"], sk.config["cl"], sk.config["stream"]) == (1024, 1, 3)
+    assert sk.config["smem"] == 3 * 4 * 1024 * 16
+    sk = compile_graph(graphs.softmax((4096, 32768)))[0].plan.kernels[0]
+    assert sk.config["cl"] > 1 and not sk.config.get("stream")
+
+
+def test_stream_forms_compile_for_sm100a(tmp_path):
+    """Stream kernels: per-thread cp.async staging, row-invariant operands
+    hoisted, cluster partials pushed with st.async (cl > 1)."""
+    cases = [
+        (graphs.softmax((300, 32768), dtype="bfloat16", causal=True), {"stream": 3}, "bfloat16"),
+        (graphs.rmsnorm(999, 8192), {"stream": 3, "engine": "regs", "tpc": 128, "cl": 4}, "float32"),
+        (graphs.rmsnorm_silu_gate(1000, 3584), {"stream": 4, "engine": "regs"}, "bfloat16"),
+    ]
+    for g, tune, dt in cases:
+        grp = FusionEngine().fuse(g)[0]
+        ins = sorted(i for i, o in g.ops.items() if o.op_type.name == "INPUT")
+        shapes = {i: tuple(g.ops[i].shape.dims) for i in ins}
+        k = CodeGenerator(tune={"row": tune}).generate(g, grp, shapes, {i: dt for i in ins})
+        c = k.plan.kernels[0].config
+        assert c["stream"] >= 2
+        assert "cp_async16" in k.source
+        assert ("reduce_push" in k.source or "reduce_softmax_push" in k.source) == (c["cl"] > 1)
+        assert build_cubin(k.source, k.name, tmp_path).stat().st_size > 1000
+
+
 def test_fp16_flag_and_save(tmp_path):
     g = graphs.rmsnorm(8, 256)
     kernels = ZeroCompiler(fp16=True).compile(g)

@@ -240,6 +240,70 @@ def test_tma_ring_engine(rows, cols, dtype):
                  f"tma ring {rows}x{cols} {dtype}")
 
 
+STREAM_CASES = [
+    # (graph, rows, cols, dtype, row tune) -- persistent stream form forced on
+    ("softmax", 300, 32768, "bfloat16", {"stream": 3}),
+    ("softmax", 300, 32768, "bfloat16", {"stream": 3, "tpc": 1024, "cl": 1}),
+    ("softmax_causal", 777, 4096, "float32", {"stream": 3}),
+    ("softmax_causal", 2000, 8192, "bfloat16", {"stream": 3, "tpc": 256, "cl": 4}),
+    ("softmax", 3001, 2048, "bfloat16", {"stream": 4}),
+    ("rmsnorm", 5000, 5120, "float32", {"stream": 3, "engine": "regs"}),
+    ("rmsnorm", 999, 8192, "float32", {"stream": 3, "engine": "regs", "tpc": 128, "cl": 4}),
+    ("softmax", 1000, 32768, "float32", {"stream": 3, "tpc": 1024, "cl": 2, "min_blocks": 1}),
+    ("rmsnorm_silu", 1000, 3584, "bfloat16", {"stream": 4, "engine": "regs"}),
+]
+
+
+def _stream_graph(kind, rows, cols, dtype):
+    if kind == "rmsnorm":
+        return graphs.rmsnorm(rows, cols, dtype=dtype), ["x", "w"]
+    if kind == "rmsnorm_silu":
+        return graphs.rmsnorm_silu_gate(rows, cols, dtype=dtype), ["x", "w", "gate"]
+    return graphs.softmax((rows, cols), dtype=dtype, causal=kind.endswith("causal")), ["logits"]
+
+
+@pytest.mark.parametrize("kind,rows,cols,dtype,tune", STREAM_CASES)
+def test_stream_row_engine(kind, rows, cols, dtype, tune):
+    """The persistent stream form of the register engine (rows staged per
+    thread with cp.async, several rows per team, cluster partials pushed into
+    exchange areas that alternate by row parity), forced on; also launched
+    as two row-offset halves, which must give the same bits."""
+    from molten_b200.codegen import CodeGenerator
+    from molten_b200.fusion import FusionEngine
+    rt = MoltenRuntime(tune={"row": dict(tune)})
+    g, names = _stream_graph(kind, rows, cols, dtype)
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(rows * 7 + cols)
+    xs = []
+    for nm in names:
+        if nm == "w":
+            xs.append((1 + 0.1 * torch.randn(cols, generator=gen, device=DEV)).to(TORCH_DT[dtype]))
+        else:
+            scale = 3.0 if kind.startswith("softmax") else 1.0
+            xs.append((scale * torch.randn(rows, cols, generator=gen, device=DEV)).to(TORCH_DT[dtype]))
+    shapes = {i: tuple(t.shape) for i, t in enumerate(xs)}
+    gk = CodeGenerator(tune=rt.tune).generate(g, FusionEngine().fuse(g)[0], shapes,
+                                              {i: dtype for i in shapes})
+    assert gk.plan.kernels[0].config.get("stream", 0) >= 2, gk.plan.kernels[0].config
+    ck = rt.compile(gk)
+    out = ck(*xs)
+    torch.cuda.synchronize()
+    assert MoltenRuntime.read_status(0) == 0, "a bounded wait gave up"
+    res = orc.evaluate(g, {nm: to_numpy(t) for nm, t in zip(names, xs)})
+    ref = res[("f32", g.ops[g._outputs[0]].inputs[0])]
+    assert_close(as_f32(out), ref, dtype, f"stream {kind} {rows}x{cols} {dtype} {tune}")
+    # two launches over row halves, each told its first global row
+    half = rows // 2 + 1
+    outs = []
+    for a, b in ((0, half), (half, rows)):
+        part = [t if t.dim() == 1 else t[a:b] for t in xs]
+        outs.append(ck(*part, row_offset=a))
+    torch.cuda.synchronize()
+    bits = (lambda t: t.view(torch.int16)) if out.dtype != torch.float32 else \
+        (lambda t: t.view(torch.int32))
+    assert torch.equal(bits(torch.cat(outs)), bits(out))
+
+
 def test_misaligned_pointers_take_the_scalar_path(rt):
     g = graphs.rmsnorm(4, 512)
     base = torch.randn(4 * 512 + 1, device=DEV)
