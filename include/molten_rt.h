@@ -41,12 +41,19 @@ extern "C" {
 #define MOLTEN_ALIGN64 _Alignas(64)
 #endif
 
+/* molten_launch_cfg.flags: launch with programmatic stream serialization
+ * (programmatic dependent launch).  The kernel may start launching while
+ * the previous kernel of the stream is finishing; every generated kernel
+ * waits (griddepcontrol.wait) for it before touching global memory. */
+#define MOLTEN_LAUNCH_PDL 1u
+
 /* Launch geometry of one kernel.  cluster = {0,0,0} or {1,1,1}: no cluster. */
 typedef struct molten_launch_cfg {
   uint32_t grid[3];
   uint32_t block[3];
   uint32_t cluster[3];
   uint32_t smem_bytes;           /* dynamic shared memory per CTA */
+  uint32_t flags;                /* MOLTEN_LAUNCH_* bits */
 } molten_launch_cfg;
 
 /* Parameter block of every generated row / elementwise kernel

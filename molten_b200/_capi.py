@@ -41,9 +41,13 @@ SIGNATURES = {
 }
 
 
+LAUNCH_PDL = 1          # MOLTEN_LAUNCH_PDL
+
+
 class LaunchCfg(ctypes.Structure):
     _fields_ = [("grid", ctypes.c_uint32 * 3), ("block", ctypes.c_uint32 * 3),
-                ("cluster", ctypes.c_uint32 * 3), ("smem_bytes", ctypes.c_uint32)]
+                ("cluster", ctypes.c_uint32 * 3), ("smem_bytes", ctypes.c_uint32),
+                ("flags", ctypes.c_uint32)]
 
 
 class RowArgs(ctypes.Structure):

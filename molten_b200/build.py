@@ -10,6 +10,7 @@ import hashlib
 import os
 import shutil
 import subprocess
+import threading
 import tempfile
 from pathlib import Path
 
@@ -80,7 +81,9 @@ def build_cubin(source: str, name: str, cache_dir: os.PathLike = None, verbose: 
         return cubin
     cu = cache / f"{name}_{key}.cu"
     cu.write_text(source)
-    tmp = cache / f".{name}_{key}.{os.getpid()}.cubin"
+    # private temporary per build (process and thread): two builders of the
+    # same source each publish a complete file with an atomic rename
+    tmp = cache / f".{name}_{key}.{os.getpid()}.{threading.get_ident()}.cubin"
     cmd = [nvcc_path(), *CUBIN_FLAGS, *extra_flags, f"-I{ENGINE_INCLUDE}", "-o", str(tmp), str(cu)]
     if verbose:
         print(" ".join(cmd))

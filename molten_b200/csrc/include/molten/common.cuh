@@ -13,6 +13,19 @@ namespace molten {
 typedef __nv_bfloat16 bf16;
 typedef __half f16;
 
+// ------------------------------------------- programmatic dependent launch
+// Every generated kernel starts with this.  With the launch attribute
+// (MOLTEN_LAUNCH_PDL) the next kernel of the stream may begin launching as
+// soon as every CTA of this one is running, and this kernel waits here until
+// the previous one has completed and its writes are visible -- before any
+// global memory access, so no producer/consumer order is ever relaxed; what
+// overlaps is launch processing, CTA scheduling and the prologue.  Both
+// instructions are no-ops for a launch without the attribute.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- conversion
 __device__ __forceinline__ float to_f32(float v) { return v; }
 // bf16 is the upper half of an fp32: widening is a 16-bit shift (integer

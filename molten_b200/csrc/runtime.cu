@@ -363,14 +363,23 @@ int molten_launch(void* mod, const char* kernel, const molten_launch_cfg* cfg,
   lc.blockDimZ = cfg->block[2];
   lc.sharedMemBytes = cfg->smem_bytes;
   lc.hStream = static_cast<CUstream>(stream);
-  CUlaunchAttribute attr[1];
+  CUlaunchAttribute attr[2];
+  unsigned n_attr = 0;
   if (cl > 1) {
-    attr[0].id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
-    attr[0].value.clusterDim.x = cfg->cluster[0];
-    attr[0].value.clusterDim.y = cfg->cluster[1];
-    attr[0].value.clusterDim.z = cfg->cluster[2];
+    attr[n_attr].id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
+    attr[n_attr].value.clusterDim.x = cfg->cluster[0];
+    attr[n_attr].value.clusterDim.y = cfg->cluster[1];
+    attr[n_attr].value.clusterDim.z = cfg->cluster[2];
+    ++n_attr;
+  }
+  if (cfg->flags & MOLTEN_LAUNCH_PDL) {
+    attr[n_attr].id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+    attr[n_attr].value.programmaticStreamSerializationAllowed = 1;
+    ++n_attr;
+  }
+  if (n_attr) {
     lc.attrs = attr;
-    lc.numAttrs = 1;
+    lc.numAttrs = n_attr;
   }
   void* args[1] = {const_cast<void*>(params)};
   CUresult r = driver().launch_kernel_ex(&lc, k->fn, args, nullptr);

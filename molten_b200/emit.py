@@ -254,6 +254,7 @@ def emit_row(sk: SubKernel, name: str) -> str:
     lb = f"{TPC * RPC}, {minb}" if minb else f"{TPC * RPC}"
     e.w(f"extern \"C\" __global__ void __launch_bounds__({lb}) "
         f"{name}(const __grid_constant__ RowArgs args) {{")
+    e.w("  pdl_enter();")
     e.w(f"  constexpr int VEC = {VEC}, NV = {NV}, TPC = {TPC}, RPC = {RPC}, CL = {CL};")
     e.w(f"  constexpr long long COLS = {sk.cols}LL;")
     e.w(f"  constexpr int NVEC = {cfg['nvec']};")
@@ -581,6 +582,7 @@ def emit_ew(sk: SubKernel, name: str) -> str:
     lb = f"{TPC * RPC}, {minb}" if minb else f"{TPC * RPC}"
     e.w(f"extern \"C\" __global__ void __launch_bounds__({lb}) "
         f"{name}(const __grid_constant__ RowArgs args) {{")
+    e.w("  pdl_enter();")
     e.w(f"  constexpr int VEC = {VEC}, NV = {NV}, TPC = {TPC}, RPC = {RPC}, UPT = {UPT};")
     e.w(f"  constexpr long long COLS = {sk.cols}LL, NVEC = {cfg['nvec']}LL;")
     e.w("  const int t = threadIdx.x % TPC, team = threadIdx.x / TPC;")
@@ -723,6 +725,7 @@ def emit_row_tma(sk: SubKernel, name: str) -> str:
     w("")
     w(f"extern \"C\" __global__ void __launch_bounds__({32 * (NC + 1)}, 1) "
       f"{name}(const __grid_constant__ RowArgs args) {{")
+    w("  pdl_enter();")
     w(f"  constexpr int VEC = {VEC}, NV = {NV}, NC = {NC}, STAGES = {ST}, "
       f"STAGE_BYTES = {cfg['stage_bytes']};")
     w(f"  constexpr long long COLS = {sk.cols}LL, NVEC = {cfg['nvec']}LL;")

@@ -102,6 +102,7 @@ def emit_gemm(sk: SubKernel, name: str) -> str:
     w("  extern __shared__ __align__(1024) uint8_t smem_raw[];")
     w(f"  const GemmShared sh = gemm_carve<Layout_{name}>(smem_raw);")
     w(f"  gemm_init<Layout_{name}>(sh, args);     // mbarriers + TMEM allocation")
+    w("  pdl_enter();                            // no global access before this")
     w("  __syncthreads();")
     w(f"  gemm_roles<Layout_{name}, {f16in}, Epilogue_{name}>(sh, args);")
     w("  __syncthreads();")

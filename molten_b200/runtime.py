@@ -56,6 +56,11 @@ def _torch_dtype(name: str):
 
 _TMA_CODE = {"bfloat16": _capi.DT_BF16, "float16": _capi.DT_F16, "float32": _capi.DT_F32}
 
+# Programmatic dependent launch for every kernel (MOLTEN_PDL=0 turns it off):
+# consecutive launches overlap launch processing and CTA scheduling; each
+# kernel still waits for its predecessor before touching global memory.
+PDL = os.environ.get("MOLTEN_PDL", "1") != "0"
+
 
 class _Spec:
     """One shape/dtype specialisation of a group, ready to launch."""
@@ -127,6 +132,7 @@ class _Spec:
             cfg.block[:] = [128, c["threads"] // 128, 1]
             cfg.cluster[:] = [1, 1, 1]
             cfg.smem_bytes = c["smem_bytes"]
+        cfg.flags = _capi.LAUNCH_PDL if PDL else 0
         self._cfgs[key] = cfg
         return cfg
 
