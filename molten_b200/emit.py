@@ -265,12 +265,20 @@ def emit_row(sk: SubKernel, name: str) -> str:
     body = dict(closures=closures, reds=reds, smx=smx, materialize=materialize,
                 prefetch=prefetch, masked_only=masked_only)
     if not stream:
+        push = CL > 1
+        if push:
+            _emit_exchange_setup(e, n_areas, max_nr)
+            e.w("  constexpr uint32_t xph = 0u;            // one row per team: phase 0 only")
         e.w("  const long long lrow = tm.row;")
         e.w("  const long long grow = args.row_offset + lrow;")
         e.w("  const bool rok = tm.row_ok;")
         e.w("  (void)grow;")
-        _emit_row_body(e, staged=[], area=lambda c: f"{c}", done_early=True, **body)
-        e.w("  tm.cluster_done_wait();")
+        _emit_row_body(e, staged=[], area=lambda c: f"{c}", done_early=not push, push=push,
+                       wait_exchange=push, **body)
+        if push:
+            _emit_exchange_teardown(e)
+        else:
+            e.w("  tm.cluster_done_wait();")
         e.w("}")
         return "\n".join(e.lines) + "\n"
 
@@ -299,18 +307,7 @@ def emit_row(sk: SubKernel, name: str) -> str:
         e.w("  }")
     push = CL > 1
     if push:
-        # cluster partials are pushed (st.async + mbarrier), not exchanged
-        # behind a barrier.cluster round
-        e.w(f"  constexpr int NAREAS = {n_areas}, XNR = {max_nr};")
-        e.w("  __shared__ float xslots[NAREAS * RPC * CL * XNR];")
-        e.w("  __shared__ __align__(8) unsigned long long xbar[NAREAS];")
-        e.w("  __shared__ int xabort;")
-        e.w("  if (threadIdx.x == 0) {")
-        e.w("    for (int a = 0; a < NAREAS; ++a) xch_init(shared_addr(&xbar[a]));")
-        e.w("    xabort = 0;")
-        e.w("    xch_init_fence();")
-        e.w("  }")
-        e.w("  cluster_arrive();          // every peer's barriers exist before the first push")
+        _emit_exchange_setup(e, n_areas, max_nr)
     e.w("#pragma unroll 1")
     e.w("  for (int s = 0; s < STAGES - 1; ++s) {")
     _emit_stage_row(e, staged, masked_only, "base0 + s * step + tm.team", "s", "    ")
@@ -318,7 +315,6 @@ def emit_row(sk: SubKernel, name: str) -> str:
     e.w("  }")
     if push:
         e.w("  cluster_wait();")
-        e.w("  const ClusterExchange xch{xslots, shared_addr(xbar), XNR, &xabort};")
     e.w("  int st = 0;")
     e.w("  uint32_t use = 0;")
     e.w("#pragma unroll 1")
@@ -343,11 +339,37 @@ def emit_row(sk: SubKernel, name: str) -> str:
     e.w("  }")
     e.w("  cp_async_wait<0>();")
     if push:
-        e.w("  if (threadIdx.x == 0 && xabort && args.status) atomicOr(args.status, kRowTimeoutExchange);")
-    e.w("  tm.cluster_done_arrive();")
-    e.w("  tm.cluster_done_wait();")
+        _emit_exchange_teardown(e)
     e.w("}")
     return "\n".join(e.lines) + "\n"
+
+
+def _emit_exchange_setup(e: _Emitter, n_areas: int, max_nr: int):
+    """Shared state of the push exchange (cluster kernels): one mbarrier per
+    exchange area, initialised by thread 0 and published to the cluster by a
+    release arrive; the matching cluster_wait() comes before the first
+    push."""
+    e.w("  // cluster partials are pushed (st.async + mbarrier), not exchanged")
+    e.w("  // behind a barrier.cluster round")
+    e.w(f"  constexpr int NAREAS = {n_areas}, XNR = {max_nr};")
+    e.w("  __shared__ float xslots[NAREAS * RPC * CL * XNR];")
+    e.w("  __shared__ __align__(8) unsigned long long xbar[NAREAS];")
+    e.w("  __shared__ int xabort;")
+    e.w("  if (threadIdx.x == 0) {")
+    e.w("    for (int a = 0; a < NAREAS; ++a) xch_init(shared_addr(&xbar[a]));")
+    e.w("    xabort = 0;")
+    e.w("    xch_init_fence();")
+    e.w("  }")
+    e.w("  cluster_arrive();          // every peer's barriers exist before the first push")
+    e.w("  const ClusterExchange xch{xslots, shared_addr(xbar), XNR, &xabort};")
+
+
+def _emit_exchange_teardown(e: _Emitter):
+    """Report a timed-out exchange wait; keep every CTA of the cluster alive
+    until all have finished (a relaxed barrier: it hands over no data)."""
+    e.w("  if (threadIdx.x == 0 && xabort && args.status) atomicOr(args.status, kRowTimeoutExchange);")
+    e.w("  cluster_arrive_relaxed();")
+    e.w("  cluster_wait();")
 
 
 def _emit_stage_row(e: _Emitter, staged, masked_only, row_expr: str, stage_expr: str, indent: str):
@@ -395,7 +417,7 @@ def _emit_stage_row(e: _Emitter, staged, masked_only, row_expr: str, stage_expr:
 
 
 def _emit_row_body(e: _Emitter, closures, reds, smx, materialize, prefetch, masked_only, staged,
-                   area, done_early: bool, push: bool = False):
+                   area, done_early: bool, push: bool = False, wait_exchange: bool = False):
     """Everything a team does for its current row (``lrow``/``grow``/``rok``
     in scope): pointers, per-row leaves, the streamed slots (global loads, or
     shared-memory reads of the staged copies), the reduction passes and the
@@ -444,6 +466,8 @@ def _emit_row_body(e: _Emitter, closures, reds, smx, materialize, prefetch, mask
                 e.w(f"      {load}")
         e.w("    }")
         e.w("  }")
+    if wait_exchange:
+        e.w("  cluster_wait();          // peers' exchange barriers are initialised")
     for vid in sorted(materialize):
         e.w(f"  float m{vid}[NV][VEC];")
     mat_ready = set()
@@ -519,30 +543,34 @@ def _emit_row_body(e: _Emitter, closures, reds, smx, materialize, prefetch, mask
     # ---- final pass: outputs
     fin = set(closures[sk.passes])
     full_outs = [o for o in sk.outputs if o.kind == "full"]
-    if full_outs:
-        e.w("  // ---- final pass: outputs")
+
+    def output_loop(packer, ind):
         e.w("#pragma unroll")
-        e.w("  for (int k = 0; k < NV; ++k) {")
-        e.w("    const int j = tm.slot(k);")
-        e.w("    if (!(rok && j < NVEC)) continue;")
-        _emit_nonprefetched_loads(e, fin, prefetch, "    ")
+        e.w(f"{ind}for (int k = 0; k < NV; ++k) {{")
+        e.w(f"{ind}  const int j = tm.slot(k);")
+        e.w(f"{ind}  if (!(rok && j < NVEC)) continue;")
+        _emit_nonprefetched_loads(e, fin, prefetch, ind + "  ")
         for o in full_outs:
-            e.w(f"    float f{o.index}[VEC];")
+            e.w(f"{ind}  float f{o.index}[VEC];")
         e.w("#pragma unroll")
-        e.w("    for (int e = 0; e < VEC; ++e) {")
+        e.w(f"{ind}  for (int e = 0; e < VEC; ++e) {{")
         if any(values[t].op == "mask" for t in fin):
-            e.w("      const int col = (int)(j * VEC) + e;")
-        for st in e.elem_statements(fin, prefetch, mat_ready, "      "):
+            e.w(f"{ind}    const int col = (int)(j * VEC) + e;")
+        for st in e.elem_statements(fin, prefetch, mat_ready, ind + "    "):
             e.w(st)
         for o in full_outs:
             src = e.leaf(sk.out_values[o.index], True, prefetch, mat_ready, set())
-            e.w(f"      f{o.index}[e] = {src};")
-        e.w("    }")
+            e.w(f"{ind}    f{o.index}[e] = {src};")
+        e.w(f"{ind}  }}")
         for o in full_outs:
             ct = _ctype(o.dtype)
-            e.w(f"    Slot<{ct}, VEC> o{o.index}; pack_slot<{ct}, VEC>(o{o.index}, f{o.index});")
-            e.w(f"    store_slot<kStoreDefault, {ct}, VEC>(out{o.index} + j * VEC, o{o.index});")
-        e.w("  }")
+            e.w(f"{ind}  Slot<{ct}, VEC> o{o.index}; {packer}<{ct}, VEC>(o{o.index}, f{o.index});")
+            e.w(f"{ind}  store_slot<kStoreDefault, {ct}, VEC>(out{o.index} + j * VEC, o{o.index});")
+        e.w(f"{ind}}}")
+
+    if full_outs:
+        e.w("  // ---- final pass: outputs")
+        output_loop("pack_slot", "  ")
     for o in sk.outputs:
         if o.kind == "row":
             src = e.leaf(sk.out_values[o.index], False, prefetch, set(), set())

@@ -180,7 +180,8 @@ class _Spec:
             else:
                 a = _capi.RowArgs()
                 a.rows, a.cols = sk.rows, sk.cols
-                if sk.config.get("engine") == "tma" or sk.config.get("stream"):
+                if (sk.config.get("engine") == "tma" or sk.config.get("stream")
+                        or sk.config.get("cl", 1) > 1):
                     a.status = _capi.status_word(di)
             a.row_offset = row_offset
             ins_al, outs_al = self.align[i]
