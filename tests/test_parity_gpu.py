@@ -304,6 +304,40 @@ def test_stream_row_engine(kind, rows, cols, dtype, tune):
     assert torch.equal(bits(torch.cat(outs)), bits(out))
 
 
+FP16_CASES = [
+    ("rmsnorm", {"rows": 300, "cols": 5120}),
+    ("rmsnorm_silu_gate", {"rows": 257, "cols": 3584}),
+    ("softmax", {"shape": (600, 2048), "causal": True}),
+    ("softmax", {"shape": (64, 32768), "causal": False}),      # stream form (16-bit long rows)
+    ("chain", {"rows": 512, "cols": 8192}),
+]
+
+
+@pytest.mark.parametrize("kind,params", FP16_CASES)
+def test_fp16_row_patterns(rt, kind, params):
+    """fp16 I/O through the reference's own switch, ZeroCompiler(fp16=True)
+    (compiler.py / cli.py --fp16), for every row pattern."""
+    from molten_b200.compiler import ZeroCompiler
+    w = workloads.Workload(f"{kind}_fp16", kind, params, "float16")
+    g = w.graph()
+    xs = workloads.make_inputs(w, seed=3, device=DEV)
+    ks = ZeroCompiler(fp16=True).compile(g)
+    assert len(ks) == 1 and ks[0].plan.input_dtypes == ["float16"] * len(xs)
+    out = rt.compile(ks[0])(*xs)
+    torch.cuda.synchronize()
+    assert out.dtype == torch.float16
+    names = [g.ops[i].name for i in sorted(i for i, o in g.ops.items() if o.op_type.name == "INPUT")]
+    res = orc.evaluate(g, {nm: to_numpy(t) for nm, t in zip(names, xs)})
+    assert_close(as_f32(out), res[("f32", g.ops[g._outputs[0]].inputs[0])], "float16",
+                 f"fp16 {kind} {params}")
+
+
+def test_cli_benchmark_runs_on_the_gpu(capsys):
+    from molten_b200 import cli
+    assert cli.main(["benchmark", "--dim", "3584", "--seq", "256", "--dtype", "float16", "--run"]) == 0
+    assert "us/call" in capsys.readouterr().out
+
+
 def test_misaligned_pointers_take_the_scalar_path(rt):
     g = graphs.rmsnorm(4, 512)
     base = torch.randn(4 * 512 + 1, device=DEV)
