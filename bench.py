@@ -145,6 +145,9 @@ def cpu_sample(w, fraction_rows=None):
         p["shape"] = (rows, cols)
     elif w.kind == "gemm_bias_gelu":
         p["m"] = min(p["m"], fraction_rows or 256)
+    elif w.kind == "rope":
+        p["batch"] = 1
+        p["seq"] = max(1, min(p["seq"], (fraction_rows or 1024) // max(1, p["heads"] // 8)))
     return workloads.scaled(w, **p)
 
 
@@ -252,7 +255,7 @@ def run_molten(args, w):
     gen = CodeGenerator(tune=tune)
     shapes = {i: tuple(t.shape) for i, t in zip(sorted(i for i, o in g.ops.items()
                                                       if o.op_type.name == "INPUT"), xs)}
-    dtypes = {i: w.dtype for i in shapes}
+    dtypes = {i: str(t.dtype).replace("torch.", "") for i, t in zip(sorted(shapes), xs)}
     gk = gen.generate(g, grp, shapes, dtypes)
     ck = rt.compile(gk)
     work = w_local.flops_per_call if is_gemm else w_local.bytes_per_call

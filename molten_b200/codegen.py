@@ -97,6 +97,8 @@ def launch_records(plan: GroupPlan, name: str) -> list:
             rec.update(engine="regs", block=c["block"], rpc=c["rpc"], cl=c["cl"], smem=0)
         elif sk.family == "ew":
             rec.update(block=c["block"], rpc=c["rpc"], upt=c["upt"], tiles=c["tiles"], smem=0)
+        elif sk.family == "rope":
+            rec.update(block=c["block"], vec=c["vec"], slots_per_row=c["spr"], smem=0)
         else:
             rec.update(block=c["threads"], bm=c["bm"], bn=c["bn"], bk=c["bk"],
                        stages=c["stages"], smem=c.get("smem_bytes", 0))
@@ -158,6 +160,7 @@ class CodeGenerator:
     def generate_from_plan(self, plan: GroupPlan, name: str, graph=None, group=None):
         from .emit import emit_ew, emit_row, emit_row_tma
         from .emit_gemm import emit_gemm
+        from .emit_rope import emit_rope
         chunks = []
         ops_txt = " -> ".join(graph.ops[i].op_type.name for i in group.op_ids) if graph else ""
         chunks.append(f"// Molten auto-generated for {ARCH}: {name}")
@@ -179,6 +182,9 @@ class CodeGenerator:
                 block_x = c["block"]
             elif sk.family == "ew":
                 chunks.append(emit_ew(sk, entry))
+                block_x = sk.config["block"]
+            elif sk.family == "rope":
+                chunks.append(emit_rope(sk, entry))
                 block_x = sk.config["block"]
             else:
                 chunks.append(emit_gemm(sk, entry))

@@ -7,6 +7,8 @@ Each builder returns a DataflowGraph whose fusion yields exactly one group:
 * ``softmax``          [ADD(causal mask) ->] SOFTMAX, fp32 or bf16
 * ``chain``            gelu(x*a+b)*s + r -> clamp(-6, 6) -> *0.5 + r, bf16
 * ``gemm_bias_gelu``   MATMUL -> ADD(bias) -> GELU, bf16
+
+and the RoPE pattern of ``benchmarks/ops.py:24-35`` (``rope``).
 """
 
 from __future__ import annotations
@@ -79,3 +81,23 @@ BUILDERS = {
     "chain": chain,
     "gemm_bias_gelu": gemm_bias_gelu,
 }
+
+
+def rope(batch=1, seq=4096, heads=32, head_dim=128, dtype="bfloat16", table_dtype="float32",
+         style=None, packed=False) -> DataflowGraph:
+    """ROTATE(x, cos, sin) on x [batch, seq, heads, head_dim] with cos/sin
+    [seq, head_dim/2] (``ops.py:24-35``); ``packed`` uses the reference
+    builder's two-input form, one [seq, head_dim] table of (cos, sin) pairs."""
+    g = DataflowGraph("rope")
+    x = g.add_input("x", TensorShape([batch, seq, heads, head_dim]), dtype=dtype)
+    if packed:
+        f = g.add_input("freqs", TensorShape([seq, head_dim]), dtype=table_dtype)
+        g.add_output(g.rope(x, f, "rope", style=style))
+    else:
+        c = g.add_input("cos", TensorShape([seq, head_dim // 2]), dtype=table_dtype)
+        s = g.add_input("sin", TensorShape([seq, head_dim // 2]), dtype=table_dtype)
+        g.add_output(g.rope(x, c, "rope", sin=s, style=style))
+    return g
+
+
+BUILDERS["rope"] = rope

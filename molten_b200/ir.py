@@ -177,8 +177,20 @@ class DataflowGraph:
         div_id = self.div(x, rms_id, f"{name}_div")
         return self.mul(div_id, weight, f"{name}_scale")
 
-    def rope(self, x: int, freqs: int, name: str = "") -> int:
-        return self.add_op(OpType.ROTATE, [x, freqs], name)
+    def rope(self, x: int, freqs: int, name: str = "", sin: Optional[int] = None,
+             style: Optional[str] = None) -> int:
+        """ROTATE: rotary position embedding of x [..., seq, heads, head_dim].
+
+        ``rope(x, freqs)`` is the reference's builder (``ir.py:175-176``);
+        its table layout is not specified there, so here ``freqs`` is
+        [seq, head_dim] holding each pair's (cos, sin) interleaved.  With
+        ``sin`` given, ``freqs`` is the cos table and both are
+        [seq, head_dim/2] -- the form of ``benchmarks/ops.py:24-35``.
+        ``style``: "interleaved" pairs (2i, 2i+1) as in ops.py (default) or
+        "half" pairs (i, i + head_dim/2).  The result has x's dtype."""
+        inputs = [x, freqs] + ([sin] if sin is not None else [])
+        attrs = {"style": style} if style else {}
+        return self.add_op(OpType.ROTATE, inputs, name, **attrs)
 
     def unary(self, op_type: OpType, x: int, name: str = "", **attrs) -> int:
         return self.add_op(op_type, [x], name, **attrs)

@@ -114,6 +114,9 @@ def infer_shapes(graph: DataflowGraph, op_ids, known: dict) -> dict:
             if not _reduces_last_dim(op, len(s)):
                 raise LoweringError(f"{t.name} only over the last dim")
             s = tuple(s[:-1]) + (1,) if len(s) else (1,)
+        elif t == OpType.ROTATE:
+            s = ins[0]
+            check_rope_shapes(op, ins)
         elif t == OpType.MATMUL:
             a, b = ins
             if len(b) != 2 or len(a) < 2:
@@ -125,6 +128,36 @@ def infer_shapes(graph: DataflowGraph, op_ids, known: dict) -> dict:
             raise LoweringError(f"{t.name} has no sm_100a lowering")
         shapes[oid] = tuple(int(d) for d in s)
     return shapes
+
+
+ROPE_STYLES = ("interleaved", "half")
+
+
+def check_rope_shapes(op, ins):
+    """ROTATE(x, cos, sin) / ROTATE(x, freqs) shapes (``ops.py:24-35``): x is
+    [..., seq, heads, head_dim] with an even head_dim; cos and sin are
+    [seq, head_dim/2]; a packed freqs table is [seq, head_dim]."""
+    x = tuple(ins[0])
+    if len(x) < 3:
+        raise LoweringError(f"ROTATE needs x of rank >= 3 ([..., seq, heads, head_dim]), got {x}")
+    seq, d = int(x[-3]), int(x[-1])
+    if d % 2:
+        raise LoweringError(f"ROTATE needs an even head_dim, got {d}")
+    style = op.attrs.get("style") or "interleaved"
+    if style not in ROPE_STYLES:
+        raise LoweringError(f"ROTATE style {style!r} (interleaved, half)")
+    if len(ins) == 2:
+        want = [(seq, d)]
+    elif len(ins) == 3:
+        want = [(seq, d // 2), (seq, d // 2)]
+    else:
+        raise LoweringError("ROTATE takes (x, freqs) or (x, cos, sin)")
+    for t, w in zip(ins[1:], want):
+        t = tuple(int(v) for v in t)
+        while len(t) > 2 and t[0] == 1:
+            t = t[1:]
+        if t != w:
+            raise LoweringError(f"ROTATE table of shape {tuple(t)}; expected {w}")
 
 
 # ----------------------------------------------------------- plan objects
@@ -245,7 +278,20 @@ def group_boundary(graph: DataflowGraph, op_ids):
 
 
 def split_group(graph: DataflowGraph, ordered: list) -> list:
-    """Split a group's live ops into (family, ops) sub-kernels."""
+    """Split a group's live ops into (family, ops) sub-kernels.
+
+    ROTATE (RoPE) reads each element's pair partner, so it runs as a
+    sub-kernel of its own between what it depends on and what follows (the
+    fusion rules put it in any group: it is neither elementwise nor a
+    reduction, ``fusion.py:65``)."""
+    rot = [i for i in ordered if graph.ops[i].op_type == OpType.ROTATE]
+    if rot:
+        r = rot[0]
+        pre_set = _deps_within(graph, r, set(ordered))
+        pre = [i for i in ordered if i in pre_set]
+        rest = [i for i in ordered if i not in pre_set and i != r]
+        return ((split_group(graph, pre) if pre else []) + [("rope", [r])]
+                + (split_group(graph, rest) if rest else []))
     mm = [i for i in ordered if graph.ops[i].op_type == OpType.MATMUL]
     if not mm:
         fam = "row" if any(graph.is_reduction(i) for i in ordered) else "ew"
@@ -601,6 +647,32 @@ def choose_ew_config(sk: SubKernel, override: Optional[dict] = None) -> dict:
     upt = o.get("upt") or 4
     return {"vec": vec, "nvec": nvec, "tpc": tpc, "nv": nv, "rpc": rpc, "upt": upt,
             "block": tpc * rpc, "tiles": -(-nvec // (tpc * nv)),
+            "min_blocks": o.get("min_blocks", 0)}
+
+
+def choose_rope_config(sk: SubKernel, style: str, seq: int, heads: int,
+                       override: Optional[dict] = None) -> dict:
+    """RoPE launch shape: one 16-byte slot of x (VEC elements, VEC/2 pairs;
+    VEC pairs of the two halves with style "half") per thread, grid-stride.
+    ``vec`` = 1 (set by the runtime for pointers that are not 16-byte
+    aligned) moves single elements, one pair per thread."""
+    o = dict(override or {})
+    d = sk.cols
+    x, out = sk.operands[0], sk.outputs[0]
+    packed = len(sk.operands) == 2
+    span = d // 2 if style == "half" else d           # elements one thread row covers
+    scalar = o.get("vec") == 1
+    if scalar:
+        vec = 2 if style != "half" else 1
+    else:
+        vec = o.get("vec") or 16 // min(DTYPE_SIZE[x.dtype], DTYPE_SIZE[out.dtype])
+        while vec > 1 and (span % vec or (style != "half" and vec % 2)):
+            vec //= 2
+        if style != "half" and vec < 2:
+            vec, scalar = 2, True
+    block = o.get("block") or 256
+    return {"vec": vec, "scalar": scalar, "style": style, "packed": packed, "seq": seq,
+            "heads": heads, "spr": span // vec, "block": block,
             "min_blocks": o.get("min_blocks", 0)}
 
 

@@ -8,7 +8,8 @@ from .ir import DataflowGraph, OpType, TensorShape
 from .lowering import (
     DTYPE_SIZE, GroupPlan, LoweringError, Operand, OutputSpec, SubKernel,
     broadcast_shapes, build_dag, canon_dtype, choose_ew_config,
-    choose_row_config, choose_row_tma_config, classify_operand, group_boundary, infer_shapes,
+    choose_row_config, choose_row_tma_config, choose_rope_config, classify_operand,
+    group_boundary, infer_shapes,
     is_mask_const, prod, promote, split_group, EXPENSIVE,
 )
 
@@ -40,6 +41,9 @@ def _op_dtypes(graph, ordered, dtypes: dict) -> dict:
             if src.op_type == OpType.CONSTANT:
                 continue
             ds.append(out[i])
+        if op.op_type == OpType.ROTATE:
+            out[oid] = out[op.inputs[0]]          # out.to(x.dtype), ops.py:35
+            continue
         out[oid] = promote(ds) if ds else "float32"
     return out
 
@@ -113,6 +117,8 @@ def plan_group(graph: DataflowGraph, group_op_ids, input_shapes: dict,
 def _plan_sub(graph, family, ops, ext, outs, shapes, dts, tune) -> SubKernel:
     if family == "gemm":
         return _plan_gemm(graph, ops, ext, outs, shapes, dts, tune)
+    if family == "rope":
+        return _plan_rope(graph, ops, outs, shapes, dts, tune)
     it = ()
     for o in ops:
         it = broadcast_shapes(it, shapes[o])
@@ -246,6 +252,29 @@ def _row_storage(sk: SubKernel, needed: set):
         if opd.last == "vec" and opd.row_map != "zero":
             prefetch.add(opd.index)
     return prefetch, materialize
+
+
+def _plan_rope(graph, ops, outs, shapes, dts, tune) -> SubKernel:
+    """One ROTATE: operands x, then freqs or cos and sin, in input order."""
+    r = ops[0]
+    op = graph.ops[r]
+    x_shape = shapes[op.inputs[0]]
+    operands = []
+    for j in op.inputs:
+        src = graph.ops[j]
+        if src.op_type == OpType.CONSTANT:
+            raise LoweringError("ROTATE operands must be tensors")
+        operands.append(Operand(index=len(operands), op_id=j, name=src.name or f"op{j}",
+                                dtype=dts[j], shape=shapes[j], last="vec", row_map="full"))
+    if outs != [r]:
+        raise LoweringError("the ROTATE sub-kernel has one output")
+    outputs = [OutputSpec(index=0, op_id=r, dtype=dts[r], shape=shapes[r], kind="full")]
+    sk = SubKernel(family="rope", op_ids=[r], operands=operands, outputs=outputs,
+                   rows=prod(x_shape[:-1]), cols=int(x_shape[-1]))
+    sk.precise = True
+    sk.config = choose_rope_config(sk, op.attrs.get("style") or "interleaved",
+                                   int(x_shape[-3]), int(x_shape[-2]), tune.get("rope") or {})
+    return sk
 
 
 def _plan_gemm(graph, ops, ext, outs, shapes, dts, tune) -> SubKernel:

@@ -118,6 +118,12 @@ class _Spec:
                                             f"resident with {cfg.smem_bytes} bytes of shared memory")
                 teams = min(teams, resident)
             cfg.grid[:] = [max(1, teams * c["cl"]), 1, 1]
+        elif sk.family == "rope":
+            total = sk.rows * c["spr"]
+            cfg.grid[:] = [max(1, min(-(-total // c["block"]), 2 ** 31 - 1)), 1, 1]
+            cfg.block[:] = [c["block"], 1, 1]
+            cfg.cluster[:] = [1, 1, 1]
+            cfg.smem_bytes = 0
         elif sk.family == "ew":
             rb = -(-sk.rows // (c["rpc"] * c["upt"]))
             cfg.grid[:] = [c["tiles"], max(1, min(rb, 65535)), 1]
@@ -209,6 +215,16 @@ def _alignment_rules(sk):
     if sk.family == "gemm":
         ins = [16 if o.last == "vec" else DTYPE_SIZE[o.dtype] for o in sk.operands]
         return ins, [16 for _ in sk.outputs]
+    if sk.family == "rope":
+        if c["scalar"]:
+            return ([DTYPE_SIZE[o.dtype] for o in sk.operands],
+                    [DTYPE_SIZE[o.dtype] for o in sk.outputs])
+        from .emit_rope import rope_table_slot
+        vec, tab = c["vec"], rope_table_slot(c)
+        x = sk.operands[0]
+        ins = [min(16, vec * DTYPE_SIZE[x.dtype])]
+        ins += [min(16, tab * DTYPE_SIZE[o.dtype]) for o in sk.operands[1:]]
+        return ins, [min(16, vec * DTYPE_SIZE[o.dtype]) for o in sk.outputs]
     vec = c.get("vec", 1)
     staged = set(c.get("staged", ())) if c.get("engine") == "tma" else set()
     ins = []
@@ -289,7 +305,7 @@ class CompiledKernel:
                                    f"{plan.input_dtypes} and cannot be re-specialised")
             tune = dict(self.runtime.tune)
             if not sig[-1]:
-                for fam in ("row", "ew"):
+                for fam in ("row", "ew", "rope"):
                     tune[fam] = dict(tune.get(fam) or {}, vec=1)
             gen = CodeGenerator(dtype=None, tune=tune)
             gk = gen.generate(self.kernel.graph, self.kernel.group, shapes, dtypes)

@@ -75,6 +75,15 @@ def _softmax(name, shape, dtype, causal):
                     (reads + n) * _esz(dtype), 0, ["logits"])
 
 
+def _rope(name, batch, seq, heads, head_dim, dtype):
+    """RoPE (ops.py:24-35): x [batch, seq, heads, head_dim] in dtype, fp32
+    cos/sin tables [seq, head_dim/2]; bytes = x in + out + both tables."""
+    n = batch * seq * heads * head_dim
+    nbytes = 2 * n * _esz(dtype) + 2 * seq * (head_dim // 2) * 4
+    return Workload(name, "rope", {"batch": batch, "seq": seq, "heads": heads,
+                                   "head_dim": head_dim}, dtype, nbytes, 0, ["x", "cos", "sin"])
+
+
 WORKLOADS = {w.name: w for w in [
     _rms("rmsnorm_f32_2048x5120", 2048, 5120, "float32", False),
     _rms("rmsnorm_silu_bf16_1x3584", 1, 3584, "bfloat16", True),
@@ -90,6 +99,7 @@ WORKLOADS = {w.name: w for w in [
     _softmax("softmax_bf16_4096x32768_causal", (4096, 32768), "bfloat16", True),
     Workload("chain_bf16_16384x8192", "chain", {"rows": 16384, "cols": 8192}, "bfloat16",
              3 * 16384 * 8192 * 2 + 3 * 8192 * 2, 0, ["x", "r", "a", "b", "s"]),
+    _rope("rope_bf16_4x4096x32x128", 4, 4096, 32, 128, "bfloat16"),
     Workload("gemm_bias_gelu_bf16_8192x4096x14336", "gemm_bias_gelu",
              {"m": 8192, "k": 4096, "n": 14336}, "bfloat16",
              (8192 * 4096 + 4096 * 14336 + 14336 + 8192 * 14336) * 2,
@@ -111,6 +121,8 @@ def scaled(w: Workload, **params) -> Workload:
         r, c = p["rows"], p["cols"]
         return Workload(w.name + "_scaled", "chain", {"rows": r, "cols": c}, w.dtype,
                         3 * r * c * 2 + 3 * c * 2, 0, list(w.input_names))
+    if w.kind == "rope":
+        return _rope(w.name + "_scaled", p["batch"], p["seq"], p["heads"], p["head_dim"], w.dtype)
     m, k, n = p["m"], p["k"], p["n"]
     return Workload(w.name + "_scaled", "gemm_bias_gelu", {"m": m, "k": k, "n": n}, w.dtype,
                     (m * k + k * n + n + m * n) * 2, 2 * m * k * n, list(w.input_names))
@@ -155,6 +167,11 @@ def make_inputs(w: Workload, seed: int = 0, device="cpu") -> list:
         b = uniform((cols,), -1.0, 1.0)
         s = uniform((cols,), -1.0, 1.0)
         return [x, r, a, b, s]
+    if w.kind == "rope":
+        x = normal((p["batch"], p["seq"], p["heads"], p["head_dim"]))
+        ang = torch.rand(p["seq"], p["head_dim"] // 2, generator=g, device=dev,
+                         dtype=torch.float32) * 6.283185307179586
+        return [x, torch.cos(ang), torch.sin(ang)]
     if w.kind == "gemm_bias_gelu":
         m, k, n = p["m"], p["k"], p["n"]
         A = normal((m, k))
@@ -178,4 +195,15 @@ def input_shapes(w: Workload) -> list:
         return [(r, c), (r, c), (c,), (c,), (c,)]
     if w.kind == "gemm_bias_gelu":
         return [(p["m"], p["k"]), (p["k"], p["n"]), (p["n"],)]
+    if w.kind == "rope":
+        half = (p["seq"], p["head_dim"] // 2)
+        return [(p["batch"], p["seq"], p["heads"], p["head_dim"]), half, half]
     raise KeyError(w.kind)
+
+
+def input_dtypes(w: Workload) -> list:
+    """Dtypes of ``make_inputs(w)`` (RoPE tables are fp32)."""
+    n = len(input_shapes(w))
+    if w.kind == "rope":
+        return [w.dtype, "float32", "float32"]
+    return [w.dtype] * n

@@ -13,6 +13,7 @@ caller's tensors, in their dtype, on the host's cores.
 * gelu (tanh)        benchmarks/ops.py:50-52
 * chain              the 8-op chain composed from the ops above
 * gemm_bias_gelu     torch.matmul as benchmarks/ops.py:58, + bias, GELU
+* rope               benchmarks/ops.py:24-35
 """
 
 from __future__ import annotations
@@ -63,6 +64,16 @@ def gemm_bias_gelu(A, B, bias):
     return gelu(torch.matmul(A, B) + bias)
 
 
+def rope(x, cos, sin):
+    """x (batch, seq, heads, head_dim), cos/sin (seq, head_dim/2)."""
+    xr = x.float().reshape(*x.shape[:-1], -1, 2)
+    x0, x1 = xr[..., 0], xr[..., 1]
+    c = cos.unsqueeze(0).unsqueeze(2)
+    s = sin.unsqueeze(0).unsqueeze(2)
+    out = torch.stack([x0 * c - x1 * s, x0 * s + x1 * c], dim=-1).flatten(-2)
+    return out.to(x.dtype)
+
+
 def run_workload(kind: str, tensors, params: dict):
     """Evaluate a named workload kind on CPU tensors."""
     if kind == "rmsnorm":
@@ -75,4 +86,6 @@ def run_workload(kind: str, tensors, params: dict):
         return chain(*tensors)
     if kind == "gemm_bias_gelu":
         return gemm_bias_gelu(*tensors)
+    if kind == "rope":
+        return rope(*tensors)
     raise KeyError(kind)

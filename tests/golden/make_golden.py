@@ -161,6 +161,21 @@ def make_numeric(ops):
     ref = F.gelu(torch.matmul(A.double(), B.double()).float() + bias.float(), approximate="tanh")
     save("gemm_bias_gelu_bf16", bf16, {"A": A, "B": B, "bias": bias}, ref,
          {"kind": "gemm_bias_gelu"})
+    # 6) RoPE exactly as the reference's helper (ops.py:24-35): x (batch,
+    #    seq, heads, head_dim), cos/sin (seq, head_dim/2); fp32 tables
+    g = gen(6)
+    x = normal(g, (2, 16, 4, 64))
+    ang = torch.rand(16, 32, generator=g) * 6.2831853
+    cos, sin = torch.cos(ang), torch.sin(ang)
+    save("rope_f32", torch.float32, {"x": x, "cos": cos, "sin": sin},
+         ops.rope_pytorch(x, cos, sin), {"kind": "rope"})
+    g = gen(7)
+    x = normal(g, (1, 8, 8, 128), dtype=bf16)
+    ang = torch.rand(8, 64, generator=g) * 6.2831853
+    cos, sin = torch.cos(ang), torch.sin(ang)
+    # the fp32 result before the helper's final cast to x.dtype
+    save("rope_bf16", bf16, {"x": x, "cos": cos, "sin": sin},
+         ops.rope_pytorch(x.float(), cos, sin), {"kind": "rope"})
 
 
 def make_fusion(ir, fusion, compiler):
@@ -250,6 +265,14 @@ def make_fusion(ir, fusion, compiler):
     k = g.add_input("k", TS([512, 4]))
     g.add_output(g.softmax(g.matmul(q, k)))
     cases["transformer_block"] = groups(g)
+
+    # RoPE after RMSNorm (the reference builder's two-input rope, ir.py:175)
+    g = DG("norm_rope")
+    x = g.add_input("x", TS([2, 16, 4, 64]))
+    w = g.add_input("w", TS([64]))
+    f = g.add_input("freqs", TS([16, 64]))
+    g.add_output(g.rope(g.rms_norm(x, w, "norm"), f))
+    cases["norm_rope"] = groups(g)
 
     # mixed reductions with different dims, and a reduction feeding a matmul
     g = DG("mixed")

@@ -153,12 +153,56 @@ def test_fp16_flag_and_save(tmp_path):
 
 
 def test_unsupported_ops_raise():
-    g = DataflowGraph("rope")
+    g = DataflowGraph("transpose")
+    x = g.add_input("x", TS([4, 8]))
+    g.add_output(g.add_op(OpType.TRANSPOSE, [x]))
+    with pytest.raises(LoweringError):
+        compile_graph(g)
+
+
+def test_rope_shapes_are_checked():
+    g = DataflowGraph("rope2d")
     x = g.add_input("x", TS([4, 8]))
     f = g.add_input("f", TS([4, 8]))
     g.add_output(g.rope(x, f))
+    with pytest.raises(LoweringError):          # x must be [..., seq, heads, head_dim]
+        compile_graph(g)
+    g = DataflowGraph("rope_bad_table")
+    x = g.add_input("x", TS([1, 16, 4, 64]))
+    c = g.add_input("cos", TS([16, 64]))
+    sn = g.add_input("sin", TS([16, 32]))
+    g.add_output(g.rope(x, c, sin=sn))
     with pytest.raises(LoweringError):
         compile_graph(g)
+
+
+@pytest.mark.parametrize("style,packed", [(None, False), ("half", False), (None, True),
+                                          ("half", True)])
+def test_rope_kernels(tmp_path, style, packed):
+    g = graphs.rope(2, 64, 8, 128, style=style, packed=packed)
+    ins = sorted(i for i, o in g.ops.items() if o.op_type == OpType.INPUT)
+    dts = {ins[0]: "bfloat16", **{i: "float32" for i in ins[1:]}}
+    k = CodeGenerator().generate(g, FusionEngine().fuse(g)[0],
+                                 {i: tuple(g.ops[i].shape.dims) for i in ins}, dts)
+    (sk,) = k.plan.kernels
+    assert sk.family == "rope" and k.plan.output_dtypes == ["bfloat16"]   # out.to(x.dtype)
+    assert sk.config["vec"] == 8 and not sk.config["scalar"]
+    assert "pdl_enter" in k.source and "% SEQ" in k.source
+    assert build_cubin(k.source, k.name, tmp_path).stat().st_size > 1000
+
+
+def test_rope_after_rmsnorm_splits_the_group():
+    """The reference fuses [RMS, DIV, MUL, ROTATE] into one group; it runs as
+    a row kernel and a RoPE kernel with an fp32 intermediate."""
+    g = DataflowGraph("norm_rope")
+    x = g.add_input("x", TS([2, 16, 4, 64]))
+    w = g.add_input("w", TS([64]))
+    f = g.add_input("freqs", TS([16, 64]))
+    g.add_output(g.rope(g.rms_norm(x, w, "norm"), f))
+    (k,) = compile_graph(g, dtype="bfloat16")
+    assert [sk.family for sk in k.plan.kernels] == ["row", "rope"]
+    assert [d for _, d in k.plan.temps.values()] == ["float32"]
+    assert k.name == "molten_fused_rms_div_mul_rotate"
 
 
 def test_float32_gemm_is_rejected():

@@ -122,6 +122,12 @@ def _reference_graphs():
     k = g.add_input("k", TS([512, 4]))
     g.add_output(g.softmax(g.matmul(q, k)))
     out["transformer_block"] = g
+    g = DataflowGraph("norm_rope")
+    x = g.add_input("x", TS([2, 16, 4, 64]))
+    w = g.add_input("w", TS([64]))
+    f = g.add_input("freqs", TS([16, 64]))
+    g.add_output(g.rope(g.rms_norm(x, w, "norm"), f))
+    out["norm_rope"] = g
     g = DataflowGraph("mixed")
     x = g.add_input("x", TS([16, 32]))
     s1 = g.add_op(OpType.SUM, [x])

@@ -96,6 +96,7 @@ FULL = [
     "softmax_f32_4096x32768",
     "softmax_bf16_4096x32768_causal",
     "chain_bf16_16384x8192",
+    "rope_bf16_4x4096x32x128",
 ]
 
 
@@ -139,6 +140,15 @@ def test_full_size_row_workloads(rt, name):
             r = np.arange(full.shape[0]) % cols
             masked = np.arange(cols)[None, :] > r[:, None]
             assert np.all(full[masked] == 0.0), "masked entries must be exactly 0"
+    elif w.kind == "rope":
+        # each sampled row at its own position ((row // heads) % seq)
+        p = w.params
+        xr = orc.to_f32(sub_inputs["x"], w.dtype)
+        cos, sin = sub_inputs["cos"], sub_inputs["sin"]
+        pos = (pick // p["heads"]) % p["seq"]
+        ref = np.concatenate([
+            orc.rope(xr[i].reshape(1, 1, 1, -1), [cos[q:q + 1], sin[q:q + 1]]).reshape(1, -1)
+            for i, q in enumerate(pos)])
     else:
         sg = w.graph(rows=len(pick))
         res = orc.evaluate(sg, sub_inputs)
@@ -336,6 +346,80 @@ def test_cli_benchmark_runs_on_the_gpu(capsys):
     from molten_b200 import cli
     assert cli.main(["benchmark", "--dim", "3584", "--seq", "256", "--dtype", "float16", "--run"]) == 0
     assert "us/call" in capsys.readouterr().out
+
+
+ROPE_CASES = [
+    # batch, seq, heads, head_dim, x dtype, table dtype, style, packed table
+    (2, 64, 8, 128, "bfloat16", "float32", None, False),
+    (1, 33, 5, 64, "float32", "float32", None, False),
+    (2, 64, 8, 128, "bfloat16", "float32", "half", False),
+    (2, 24, 4, 128, "float16", "float16", None, True),
+    (1, 40, 4, 80, "bfloat16", "bfloat16", "half", True),
+]
+
+
+def _rope_inputs(b, sq, h, d, xdt, tdt, packed, seed):
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(seed)
+    x = torch.randn(b, sq, h, d, generator=gen, device=DEV).to(TORCH_DT[xdt])
+    ang = torch.rand(sq, d // 2, generator=gen, device=DEV) * 6.283185307179586
+    c, s = torch.cos(ang).to(TORCH_DT[tdt]), torch.sin(ang).to(TORCH_DT[tdt])
+    if packed:
+        return [x, torch.stack([c, s], -1).reshape(sq, d)], ["x", "freqs"]
+    return [x, c, s], ["x", "cos", "sin"]
+
+
+@pytest.mark.parametrize("b,sq,h,d,xdt,tdt,style,packed", ROPE_CASES)
+def test_rope(rt, b, sq, h, d, xdt, tdt, style, packed):
+    """RoPE (ops.py:24-35) against the oracle: both pairings, separate or
+    packed tables, fp32 / bf16 / fp16; batch halves launched with their
+    global row offset give the same bits; a misaligned x runs the scalar
+    kernel."""
+    g = graphs.rope(b, sq, h, d, xdt, tdt, style=style, packed=packed)
+    xs, names = _rope_inputs(b, sq, h, d, xdt, tdt, packed, seed=b * 1000 + sq + d)
+    ck = rt.compile(compile_graph(g, dtype=xdt)[0])
+    out = ck(*xs)
+    torch.cuda.synchronize()
+    assert out.dtype == TORCH_DT[xdt] and ck.specialization(*xs).plan.kernels[0].family == "rope"
+    res = orc.evaluate(g, {nm: to_numpy(t) for nm, t in zip(names, xs)})
+    ref = res[("f32", g.ops[g._outputs[0]].inputs[0])]
+    assert_close(as_f32(out), ref, xdt, f"rope {b}x{sq}x{h}x{d} {xdt}/{tdt} {style} {packed}")
+    bits = (lambda t: t.view(torch.int32)) if xdt == "float32" else (lambda t: t.view(torch.int16))
+    if b >= 2:
+        parts = [ck(xs[0][i:i + 1], *xs[1:], row_offset=i * sq * h) for i in range(b)]
+        torch.cuda.synchronize()
+        assert torch.equal(bits(torch.cat(parts)), bits(out))
+    # x at an odd element offset: not 16-byte aligned -> the scalar form
+    base = torch.empty(xs[0].numel() + 1, dtype=xs[0].dtype, device=DEV)
+    xm = base[1:].view(xs[0].shape)
+    xm.copy_(xs[0])
+    out_m = ck(xm, *xs[1:])
+    torch.cuda.synchronize()
+    assert ck.specialization(xm, *xs[1:]).plan.kernels[0].config["scalar"]
+    assert_close(as_f32(out_m), ref, xdt, "rope misaligned")
+
+
+def test_rmsnorm_then_rope_group(rt):
+    """One fusion group (as the reference groups it): row kernel, fp32
+    intermediate, RoPE kernel."""
+    from molten_b200.ir import DataflowGraph, TensorShape as TS
+    g = DataflowGraph("norm_rope")
+    x = g.add_input("x", TS([2, 16, 4, 64]), dtype="bfloat16")
+    w = g.add_input("w", TS([64]), dtype="bfloat16")
+    f = g.add_input("freqs", TS([16, 64]), dtype="bfloat16")
+    g.add_output(g.rope(g.rms_norm(x, w, "norm"), f))
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(11)
+    xt = torch.randn(2, 16, 4, 64, generator=gen, device=DEV).to(torch.bfloat16)
+    wt = (1 + 0.1 * torch.randn(64, generator=gen, device=DEV)).to(torch.bfloat16)
+    ang = torch.rand(16, 32, generator=gen, device=DEV) * 6.283185307179586
+    ft = torch.stack([torch.cos(ang), torch.sin(ang)], -1).reshape(16, 64).to(torch.bfloat16)
+    (k,) = compile_graph(g, dtype="bfloat16")
+    assert [sk.family for sk in k.plan.kernels] == ["row", "rope"]
+    out = rt.compile(k)(xt, wt, ft)
+    torch.cuda.synchronize()
+    res = orc.evaluate(g, {"x": to_numpy(xt), "w": to_numpy(wt), "freqs": to_numpy(ft)})
+    assert_close(as_f32(out), res[("f32", g.ops[g._outputs[0]].inputs[0])], "bfloat16", "norm+rope")
 
 
 def test_misaligned_pointers_take_the_scalar_path(rt):
