@@ -10,12 +10,14 @@ Pairs are (2i, 2i+1) ("interleaved", as in ops.py) or (i, i + head_dim/2)
 [seq, head_dim] table of (cos, sin) per pair.  fp32 arithmetic, one
 rounding to x's dtype.
 
-One thread handles one 16-byte slot of x per grid-stride step (VEC
-elements, VEC/2 pairs; with "half" the slot and its partner slot in the
-second half, VEC pairs): one vector load of x (two for "half"), vector
-loads of the pair's table entries (cached: every head of a position reads
-the same table row), one (two) vector store(s).  ``scalar`` kernels, for
-pointers that are not 16-byte aligned, move single elements.
+Vector form: per grid-stride step a thread takes UPT items one block apart,
+an item being one 16-byte slot of x (VEC elements, VEC/2 pairs; with
+"half" the slot and its partner slot in the second half, VEC pairs); it
+issues all the items' x loads and table loads (cached: every head of a
+position reads the same table row) before rotating and storing any, so
+UPT loads per operand are in flight per thread.  The ``scalar`` form, for
+pointers that are not 16-byte aligned, moves one pair per thread per step
+with element accesses.
 """
 
 from __future__ import annotations
@@ -55,116 +57,114 @@ def emit_rope(sk: SubKernel, name: str) -> str:
         w(f"  const {T2}* __restrict__ t2 = static_cast<const {T2}*>(args.in[2]);")
     w(f"  {OT}* __restrict__ out = static_cast<{OT}*>(args.out[0]);")
     w("  const long long total = args.rows * SPR;")
+    if not SCALAR:
+        _emit_vector_body(w, c, XT, T1, T2, OT, half, PACKED)
+        w("}")
+        return "\n".join(L) + "\n"
+    # scalar form: one pair per thread per step, element accesses only
     w("  const long long stride = (long long)gridDim.x * blockDim.x;")
     w("  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; "
       "i += stride) {")
     w("    const long long row = i / SPR;")
     w("    const int j = (int)(i - row * SPR);")
     w("    const long long pos = ((args.row_offset + row) / HEADS) % SEQ;")
-    w("    const long long xo = row * D + (long long)j * VEC;")
-    # ---- gather the slot's elements and its pairs' cos / sin as fp32
     if half:
-        npair = VEC
-        w(f"    float a[VEC], b[VEC], cs[VEC], sn[VEC];      // pairs (a[e], b[e])")
-        if SCALAR:
-            w("#pragma unroll")
-            w("    for (int e = 0; e < VEC; ++e) {")
-            w("      a[e] = to_f32(x[xo + e]);")
-            w("      b[e] = to_f32(x[xo + D / 2 + e]);")
-            w("    }")
-        else:
-            w(f"    {{ const Slot<{XT}, VEC> s = load_slot<kLoadStream, {XT}, VEC>(x + xo);")
-            w("#pragma unroll")
-            w("      for (int e = 0; e < VEC; ++e) a[e] = to_f32(s.v[e]); }")
-            w(f"    {{ const Slot<{XT}, VEC> s = load_slot<kLoadStream, {XT}, VEC>(x + xo + D / 2);")
-            w("#pragma unroll")
-            w("      for (int e = 0; e < VEC; ++e) b[e] = to_f32(s.v[e]); }")
-        pair0 = "(long long)j * VEC"
+        # pair j: elements j and j + D/2 (VEC == 1)
+        w("    const long long ia = row * D + j, ib = ia + D / 2;")
     else:
-        npair = max(1, VEC // 2)
-        w(f"    float a[VEC / 2], b[VEC / 2], cs[VEC / 2], sn[VEC / 2];   // pairs (a[p], b[p])")
-        if SCALAR:
-            w("#pragma unroll")
-            w("    for (int p = 0; p < VEC / 2; ++p) {")
-            w("      a[p] = to_f32(x[xo + 2 * p]);")
-            w("      b[p] = to_f32(x[xo + 2 * p + 1]);")
-            w("    }")
-        else:
-            w(f"    {{ const Slot<{XT}, VEC> s = load_slot<kLoadStream, {XT}, VEC>(x + xo);")
-            w("#pragma unroll")
-            w("      for (int p = 0; p < VEC / 2; ++p) { a[p] = to_f32(s.v[2 * p]); "
-              "b[p] = to_f32(s.v[2 * p + 1]); } }")
-        pair0 = "(long long)j * (VEC / 2)"
-    NP = "VEC" if half else "VEC / 2"
-    w(f"    const long long p0 = {pair0};                  // first pair of this thread")
+        # pair j: elements 2j and 2j + 1 (VEC == 2)
+        w("    const long long ia = row * D + 2LL * j, ib = ia + 1;")
+    w("    const float a = to_f32(x[ia]), b = to_f32(x[ib]);")
     if PACKED:
-        # (cos, sin) of pair q at t1[pos * D + 2 q], t1[pos * D + 2 q + 1]
-        if SCALAR:
-            w("#pragma unroll")
-            w(f"    for (int p = 0; p < {NP}; ++p) {{")
-            w("      cs[p] = to_f32(t1[pos * D + 2 * (p0 + p)]);")
-            w("      sn[p] = to_f32(t1[pos * D + 2 * (p0 + p) + 1]);")
-            w("    }")
-        else:
-            w(f"    {{ const Slot<{T1}, 2 * ({NP})> s = "
-              f"load_slot<kLoadDefault, {T1}, 2 * ({NP})>(t1 + pos * D + 2 * p0);")
-            w("#pragma unroll")
-            w(f"      for (int p = 0; p < {NP}; ++p) {{ cs[p] = to_f32(s.v[2 * p]); "
-              "sn[p] = to_f32(s.v[2 * p + 1]); } }")
+        w("    const float cs = to_f32(t1[pos * D + 2LL * j]);")
+        w("    const float sn = to_f32(t1[pos * D + 2LL * j + 1]);")
     else:
-        if SCALAR:
-            w("#pragma unroll")
-            w(f"    for (int p = 0; p < {NP}; ++p) {{")
-            w("      cs[p] = to_f32(t1[pos * (D / 2) + p0 + p]);")
-            w("      sn[p] = to_f32(t2[pos * (D / 2) + p0 + p]);")
-            w("    }")
-        else:
-            w(f"    {{ const Slot<{T1}, {NP}> s = "
-              f"load_slot<kLoadDefault, {T1}, {NP}>(t1 + pos * (D / 2) + p0);")
-            w("#pragma unroll")
-            w(f"      for (int p = 0; p < {NP}; ++p) cs[p] = to_f32(s.v[p]); }}")
-            w(f"    {{ const Slot<{T2}, {NP}> s = "
-              f"load_slot<kLoadDefault, {T2}, {NP}>(t2 + pos * (D / 2) + p0);")
-            w("#pragma unroll")
-            w(f"      for (int p = 0; p < {NP}; ++p) sn[p] = to_f32(s.v[p]); }}")
-    # ---- rotate and store
-    if half:
-        w("    float o1[VEC], o2[VEC];")
-        w("#pragma unroll")
-        w("    for (int e = 0; e < VEC; ++e) {")
-        w("      o1[e] = a[e] * cs[e] - b[e] * sn[e];")
-        w("      o2[e] = a[e] * sn[e] + b[e] * cs[e];")
-        w("    }")
-        if SCALAR:
-            w("#pragma unroll")
-            w("    for (int e = 0; e < VEC; ++e) {")
-            w(f"      out[xo + e] = from_f32<{OT}>(o1[e]);")
-            w(f"      out[xo + D / 2 + e] = from_f32<{OT}>(o2[e]);")
-            w("    }")
-        else:
-            w(f"    Slot<{OT}, VEC> s1, s2;")
-            w(f"    pack_slot<{OT}, VEC>(s1, o1);")
-            w(f"    pack_slot<{OT}, VEC>(s2, o2);")
-            w(f"    store_slot<kStoreDefault, {OT}, VEC>(out + xo, s1);")
-            w(f"    store_slot<kStoreDefault, {OT}, VEC>(out + xo + D / 2, s2);")
-    else:
-        w("    float o[VEC];")
-        w("#pragma unroll")
-        w("    for (int p = 0; p < VEC / 2; ++p) {")
-        w("      o[2 * p] = a[p] * cs[p] - b[p] * sn[p];")
-        w("      o[2 * p + 1] = a[p] * sn[p] + b[p] * cs[p];")
-        w("    }")
-        if SCALAR:
-            w("#pragma unroll")
-            w(f"    for (int e = 0; e < VEC; ++e) out[xo + e] = from_f32<{OT}>(o[e]);")
-        else:
-            w(f"    Slot<{OT}, VEC> so;")
-            w(f"    pack_slot<{OT}, VEC>(so, o);")
-            w(f"    store_slot<kStoreDefault, {OT}, VEC>(out + xo, so);")
+        w("    const float cs = to_f32(t1[pos * (D / 2) + j]);")
+        w("    const float sn = to_f32(t2[pos * (D / 2) + j]);")
+    w(f"    out[ia] = from_f32<{OT}>(a * cs - b * sn);")
+    w(f"    out[ib] = from_f32<{OT}>(a * sn + b * cs);")
     w("  }")
     w("}")
-    del npair
     return "\n".join(L) + "\n"
+
+
+def _emit_vector_body(w, c, XT, T1, T2, OT, half: bool, packed: bool):
+    """Vector form: each thread takes UPT items (x slots) spaced one block
+    apart per grid-stride step; all their x and table loads are issued
+    before any rotation or store, so UPT 16-byte loads per operand are in
+    flight per thread."""
+    UPT = c.get("upt", 2)
+    NP = "VEC" if half else "VEC / 2"                  # pairs per item
+    NT = f"2 * ({NP})" if packed else NP              # table entries per item and table
+    w(f"  constexpr int UPT = {UPT};")
+    w("  const long long step = (long long)gridDim.x * blockDim.x * UPT;")
+    w("  for (long long base = (long long)blockIdx.x * blockDim.x * UPT + threadIdx.x; "
+      "base < total; base += step) {")
+    w(f"    Slot<{XT}, VEC> xa[UPT];")
+    if half:
+        w(f"    Slot<{XT}, VEC> xb[UPT];")
+    w(f"    Slot<{T1}, {NT}> ta[UPT];")
+    if not packed:
+        w(f"    Slot<{T2}, {NT}> tb[UPT];")
+    w("    long long xo[UPT];")
+    w("#pragma unroll")
+    w("    for (int u = 0; u < UPT; ++u) {             // loads")
+    w("      const long long i = base + (long long)u * blockDim.x;")
+    w("      xo[u] = -1;")
+    w("      if (i >= total) continue;")
+    w("      const long long row = i / SPR;")
+    w("      const int j = (int)(i - row * SPR);")
+    w("      const long long pos = ((args.row_offset + row) / HEADS) % SEQ;")
+    w("      xo[u] = row * D + (long long)j * VEC;")
+    w(f"      const long long p0 = (long long)j * ({NP});")
+    w(f"      xa[u] = load_slot<kLoadStream, {XT}, VEC>(x + xo[u]);")
+    if half:
+        w(f"      xb[u] = load_slot<kLoadStream, {XT}, VEC>(x + xo[u] + D / 2);")
+    if packed:
+        w(f"      ta[u] = load_slot<kLoadDefault, {T1}, {NT}>(t1 + pos * D + 2 * p0);")
+    else:
+        w(f"      ta[u] = load_slot<kLoadDefault, {T1}, {NT}>(t1 + pos * (D / 2) + p0);")
+        w(f"      tb[u] = load_slot<kLoadDefault, {T2}, {NT}>(t2 + pos * (D / 2) + p0);")
+    w("    }")
+    w("#pragma unroll")
+    w("    for (int u = 0; u < UPT; ++u) {             // rotate, round once, store")
+    w("      if (xo[u] < 0) continue;")
+    w(f"      float cs[{NP}], sn[{NP}];")
+    w("#pragma unroll")
+    w(f"      for (int p = 0; p < {NP}; ++p) {{")
+    if packed:
+        w("        cs[p] = to_f32(ta[u].v[2 * p]);")
+        w("        sn[p] = to_f32(ta[u].v[2 * p + 1]);")
+    else:
+        w("        cs[p] = to_f32(ta[u].v[p]);")
+        w("        sn[p] = to_f32(tb[u].v[p]);")
+    w("      }")
+    if half:
+        w("      float o1[VEC], o2[VEC];")
+        w("#pragma unroll")
+        w("      for (int e = 0; e < VEC; ++e) {")
+        w("        const float a = to_f32(xa[u].v[e]), b = to_f32(xb[u].v[e]);")
+        w("        o1[e] = a * cs[e] - b * sn[e];")
+        w("        o2[e] = a * sn[e] + b * cs[e];")
+        w("      }")
+        w(f"      Slot<{OT}, VEC> s1, s2;")
+        w(f"      pack_slot<{OT}, VEC>(s1, o1);")
+        w(f"      pack_slot<{OT}, VEC>(s2, o2);")
+        w(f"      store_slot<kStoreDefault, {OT}, VEC>(out + xo[u], s1);")
+        w(f"      store_slot<kStoreDefault, {OT}, VEC>(out + xo[u] + D / 2, s2);")
+    else:
+        w("      float o[VEC];")
+        w("#pragma unroll")
+        w("      for (int p = 0; p < VEC / 2; ++p) {")
+        w("        const float a = to_f32(xa[u].v[2 * p]), b = to_f32(xa[u].v[2 * p + 1]);")
+        w("        o[2 * p] = a * cs[p] - b * sn[p];")
+        w("        o[2 * p + 1] = a * sn[p] + b * cs[p];")
+        w("      }")
+        w(f"      Slot<{OT}, VEC> so;")
+        w(f"      pack_slot<{OT}, VEC>(so, o);")
+        w(f"      store_slot<kStoreDefault, {OT}, VEC>(out + xo[u], so);")
+    w("    }")
+    w("  }")
 
 
 def rope_table_slot(config: dict) -> int:

@@ -671,8 +671,11 @@ def choose_rope_config(sk: SubKernel, style: str, seq: int, heads: int,
         if style != "half" and vec < 2:
             vec, scalar = 2, True
     block = o.get("block") or 256
+    # 2 items per thread at 256 threads (measured on bf16 [4, 4096, 32, 128]:
+    # 94.6% of HBM peak; 1 item 77%, 4 items 89%, 512 threads 70%)
+    upt = 1 if scalar else (o.get("upt") or 2)
     return {"vec": vec, "scalar": scalar, "style": style, "packed": packed, "seq": seq,
-            "heads": heads, "spr": span // vec, "block": block,
+            "heads": heads, "spr": span // vec, "block": block, "upt": upt,
             "min_blocks": o.get("min_blocks", 0)}
 
 

@@ -120,7 +120,8 @@ class _Spec:
             cfg.grid[:] = [max(1, teams * c["cl"]), 1, 1]
         elif sk.family == "rope":
             total = sk.rows * c["spr"]
-            cfg.grid[:] = [max(1, min(-(-total // c["block"]), 2 ** 31 - 1)), 1, 1]
+            per_cta = c["block"] * c.get("upt", 1)
+            cfg.grid[:] = [max(1, min(-(-total // per_cta), 2 ** 31 - 1)), 1, 1]
             cfg.block[:] = [c["block"], 1, 1]
             cfg.cluster[:] = [1, 1, 1]
             cfg.smem_bytes = 0
