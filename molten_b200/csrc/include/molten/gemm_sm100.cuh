@@ -28,7 +28,7 @@ namespace molten {
 // Kernel parameter block; mirrored by `molten_gemm_args` in include/molten_rt.h.
 struct alignas(64) GemmArgs {
   CUtensorMap tmap_a;              // A [M, K], box {BK, BM}, 128B swizzle
-  CUtensorMap tmap_b;              // B [K, N], box {64, BK}, 128B swizzle
+  CUtensorMap tmap_b;              // B [K, N], box {64, BK}; or Bt [N, K], box {64, BN}
   const void* in[8];               // epilogue operands (kernel order)
   void* out[8];                    // outputs
   long long m, n, k;
@@ -100,14 +100,15 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo_bytes
 }
 
 // Instruction descriptor, kind::f16: D f32, A/B bf16 (or f16), A K-major,
-// B MN-major, shape M x N.
-template <int M, int N, bool F16IN>
+// B MN-major (B [K, N] row-major) or K-major (B given as the rows of an
+// [N, K] matrix, i.e. a transposed operand), shape M x N.
+template <int M, int N, bool F16IN, bool B_KMAJOR = false>
 __device__ __forceinline__ constexpr uint32_t umma_idesc() {
   return (1u << 4)                                  // D format f32
        | ((F16IN ? 0u : 1u) << 7)                    // A format
        | ((F16IN ? 0u : 1u) << 10)                   // B format
        | (0u << 15)                                  // A K-major
-       | (1u << 16)                                  // B MN-major
+       | ((B_KMAJOR ? 0u : 1u) << 16)                // B MN-major / K-major
        | ((uint32_t)(N >> 3) << 17)
        | ((uint32_t)(M >> 4) << 24);
 }
@@ -245,7 +246,9 @@ __device__ __forceinline__ void gemm_init(const GemmShared& s, const GemmArgs& a
 }
 
 // The three roles.  Epi::apply(args, row, col0, acc[32]) writes C[row, col0..col0+31].
-template <class L, bool F16IN, class Epi>
+// B_KMAJOR: tmap_b describes Bt [N, K] (inner K) with box {64, BN}; a stage
+// holds BN rows of 128 bytes, the same 128-byte-swizzled K-major layout as A.
+template <class L, bool F16IN, class Epi, bool B_KMAJOR = false>
 __device__ __forceinline__ void gemm_roles(const GemmShared& s, const GemmArgs& args) {
   tc_fence_after();
   const int tid = gemm_tid(), warp = tid / 32, lane = tid % 32;
@@ -271,9 +274,14 @@ __device__ __forceinline__ void gemm_roles(const GemmShared& s, const GemmArgs& 
           const uint32_t b_dst = a_dst + L::A_BYTES;
           mbar_expect_tx(bar.full(st), (uint32_t)L::STAGE_BYTES);
           tma_load_2d(a_dst, &args.tmap_a, bar.full(st), kb * L::BK, m0);
+          if constexpr (B_KMAJOR) {
+            tma_load_2d(b_dst, &args.tmap_b, bar.full(st), kb * L::BK, n0);
+          } else {
 #pragma unroll
-          for (int c = 0; c < L::BN / 64; ++c)
-            tma_load_2d(b_dst + c * L::B_CHUNK_BYTES, &args.tmap_b, bar.full(st), n0 + 64 * c, kb * L::BK);
+            for (int c = 0; c < L::BN / 64; ++c)
+              tma_load_2d(b_dst + c * L::B_CHUNK_BYTES, &args.tmap_b, bar.full(st), n0 + 64 * c,
+                          kb * L::BK);
+          }
           ++issued;
           if (++st == (uint32_t)L::STAGES) { st = 0; ph ^= 1u; }
         }
@@ -290,7 +298,7 @@ __device__ __forceinline__ void gemm_roles(const GemmShared& s, const GemmArgs& 
   } else if (warp == 1) {
     // ----------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      constexpr uint32_t IDESC = umma_idesc<L::BM, L::BN, F16IN>();
+      constexpr uint32_t IDESC = umma_idesc<L::BM, L::BN, F16IN, B_KMAJOR>();
       uint32_t st = 0, ph = 0;
       long long i = 0;
       bool ok = true;
@@ -308,7 +316,9 @@ __device__ __forceinline__ void gemm_roles(const GemmShared& s, const GemmArgs& 
 #pragma unroll
           for (int kk = 0; kk < L::BK / 16; ++kk) {
             const uint64_t ad = umma_desc(a_base + 32u * kk, 16u, 1024u);
-            const uint64_t bd = umma_desc(b_base + 2048u * kk, (uint32_t)L::B_CHUNK_BYTES, 1024u);
+            const uint64_t bd = B_KMAJOR
+                ? umma_desc(b_base + 32u * kk, 16u, 1024u)
+                : umma_desc(b_base + 2048u * kk, (uint32_t)L::B_CHUNK_BYTES, 1024u);
             umma_f16(d, ad, bd, IDESC, (kb | kk) != 0 ? 1u : 0u);
           }
           umma_commit(bar.empty(st));

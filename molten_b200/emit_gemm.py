@@ -10,7 +10,7 @@ stores 16 bytes at a time.
 from __future__ import annotations
 
 from .emit import _mask_period, _row_index_expr, c_float, value_expr
-from .lowering import DTYPE_CTYPE, LoweringError, SubKernel
+from .lowering import DTYPE_CTYPE, DTYPE_SIZE, LoweringError, SubKernel
 
 
 def emit_gemm(sk: SubKernel, name: str) -> str:
@@ -57,18 +57,33 @@ def emit_gemm(sk: SubKernel, name: str) -> str:
         if v.kind in ("row", "const") and v.op not in ("load", "const"):
             args = [_leaf(sk, x) for x in v.args]
             w(f"    const float v{vid} = {value_expr(v, args, True)};")
+    vec_ops = sorted({values[v].attrs["operand"] for v in needed
+                      if values[v].op == "load" and values[v].kind == "elem"})
+    # 16-byte chunk accesses need every row of every row-indexed operand and
+    # output to start on a 16-byte boundary; otherwise (and for the last,
+    # partial chunk of a row) elements are moved one at a time
+    strides = [DTYPE_SIZE[o.dtype] for o in sk.outputs]
+    strides += [DTYPE_SIZE[sk.operands[i].dtype] for i in vec_ops
+                if sk.operands[i].row_map != "zero"]
+    vec_ok = all((sk.n * e) % 16 == 0 for e in strides)
+    w(f"    constexpr bool ROWS_ALIGNED = {'true' if vec_ok else 'false'};")
     w("#pragma unroll")
     w("    for (int q = 0; q < 4; ++q) {")
     w("      const long long c = col0 + 8 * q;")
     w("      if (c >= N) break;")
-    vec_ops = sorted({values[v].attrs["operand"] for v in needed
-                      if values[v].op == "load" and values[v].kind == "elem"})
+    w("      const bool whole = ROWS_ALIGNED && c + 8 <= N;")
+    w("      const int valid = (int)(N - c < 8 ? N - c : 8);")
     for i in vec_ops:
         o = sk.operands[i]
         ct = DTYPE_CTYPE[o.dtype]
         idx = _row_index_expr(o, "row", "grow")
-        w(f"      const Slot<{ct}, 8> sl{i} = load_slot<kLoadDefault, {ct}, 8>("
-          f"static_cast<const {ct}*>(args.in[{i}]) + {idx} * N + c);")
+        w(f"      const {ct}* src{i} = static_cast<const {ct}*>(args.in[{i}]) + {idx} * N + c;")
+        w(f"      Slot<{ct}, 8> sl{i};")
+        w(f"      if (whole) {{ sl{i} = load_slot<kLoadDefault, {ct}, 8>(src{i}); }}")
+        w("      else {")
+        w("#pragma unroll")
+        w(f"        for (int e = 0; e < 8; ++e) sl{i}.v[e] = e < valid ? src{i}[e] : from_f32<{ct}>(0.0f);")
+        w("      }")
     for o in sk.outputs:
         w(f"      float f{o.index}[8];")
     w("#pragma unroll")
@@ -89,9 +104,13 @@ def emit_gemm(sk: SubKernel, name: str) -> str:
     w("      }")
     for o in sk.outputs:
         ct = DTYPE_CTYPE[o.dtype]
-        w(f"      Slot<{ct}, 8> o{o.index}; pack_slot<{ct}, 8>(o{o.index}, f{o.index});")
-        w(f"      store_slot<kStoreDefault, {ct}, 8>(static_cast<{ct}*>(args.out[{o.index}]) "
-          f"+ row * N + c, o{o.index});")
+        w(f"      {ct}* dst{o.index} = static_cast<{ct}*>(args.out[{o.index}]) + row * N + c;")
+        w(f"      if (whole) {{ Slot<{ct}, 8> o{o.index}; pack_slot<{ct}, 8>(o{o.index}, f{o.index}); "
+          f"store_slot<kStoreDefault, {ct}, 8>(dst{o.index}, o{o.index}); }}")
+        w("      else {")
+        w("#pragma unroll")
+        w(f"        for (int e = 0; e < 8; ++e) if (e < valid) dst{o.index}[e] = from_f32<{ct}>(f{o.index}[e]);")
+        w("      }")
     w("    }")
     w("  }")
     w("};")
@@ -104,7 +123,8 @@ def emit_gemm(sk: SubKernel, name: str) -> str:
     w(f"  gemm_init<Layout_{name}>(sh, args);     // mbarriers + TMEM allocation")
     w("  pdl_enter();                            // no global access before this")
     w("  __syncthreads();")
-    w(f"  gemm_roles<Layout_{name}, {f16in}, Epilogue_{name}>(sh, args);")
+    kmaj = "true" if cfg.get("b_kmajor") else "false"
+    w(f"  gemm_roles<Layout_{name}, {f16in}, Epilogue_{name}, {kmaj}>(sh, args);")
     w("  __syncthreads();")
     w(f"  gemm_teardown<Layout_{name}>(sh);       // TMEM release")
     w("}")

@@ -8,7 +8,8 @@ Each builder returns a DataflowGraph whose fusion yields exactly one group:
 * ``chain``            gelu(x*a+b)*s + r -> clamp(-6, 6) -> *0.5 + r, bf16
 * ``gemm_bias_gelu``   MATMUL -> ADD(bias) -> GELU, bf16
 
-and the RoPE pattern of ``benchmarks/ops.py:24-35`` (``rope``).
+and the RoPE pattern of ``benchmarks/ops.py:24-35`` (``rope``) and the
+attention-score pattern of ``benchmarks/ops.py:55-59`` (``attention_score``).
 """
 
 from __future__ import annotations
@@ -101,3 +102,17 @@ def rope(batch=1, seq=4096, heads=32, head_dim=128, dtype="bfloat16", table_dtyp
 
 
 BUILDERS["rope"] = rope
+
+
+def attention_score(m=2048, n=2048, d=128, dtype="bfloat16", scale=None) -> DataflowGraph:
+    """softmax(Q @ K^T * scale) with Q [m, d], K [n, d] (``ops.py:55-59``);
+    scale defaults to 1/sqrt(d)."""
+    g = DataflowGraph("attention_score")
+    q = g.add_input("q", TensorShape([m, d]), dtype=dtype)
+    k = g.add_input("k", TensorShape([n, d]), dtype=dtype)
+    s = g.add_constant("scale", float(scale if scale is not None else d ** -0.5))
+    g.add_output(g.softmax(g.mul(g.matmul(q, g.transpose(k, "kT"), "scores"), s), -1, "probs"))
+    return g
+
+
+BUILDERS["attention_score"] = attention_score

@@ -192,6 +192,12 @@ class DataflowGraph:
         attrs = {"style": style} if style else {}
         return self.add_op(OpType.ROTATE, inputs, name, **attrs)
 
+    def transpose(self, x: int, name: str = "") -> int:
+        """TRANSPOSE of the last two dims (a matrix [N, K] -> [K, N]).  As
+        a MATMUL's B operand it costs nothing: the GEMM reads the original
+        rows K-major."""
+        return self.add_op(OpType.TRANSPOSE, [x], name)
+
     def unary(self, op_type: OpType, x: int, name: str = "", **attrs) -> int:
         return self.add_op(op_type, [x], name, **attrs)
 

@@ -117,6 +117,10 @@ def infer_shapes(graph: DataflowGraph, op_ids, known: dict) -> dict:
         elif t == OpType.ROTATE:
             s = ins[0]
             check_rope_shapes(op, ins)
+        elif t == OpType.TRANSPOSE:
+            if len(ins[0]) < 2:
+                raise LoweringError("TRANSPOSE needs rank >= 2")
+            s = tuple(ins[0][:-2]) + (ins[0][-1], ins[0][-2])
         elif t == OpType.MATMUL:
             a, b = ins
             if len(b) != 2 or len(a) < 2:
@@ -299,8 +303,17 @@ def split_group(graph: DataflowGraph, ordered: list) -> list:
     m = mm[0]
     members = set(ordered)
     pre_set = _deps_within(graph, m, members)
+    # a TRANSPOSE that is only this MATMUL's B operand is no kernel: the GEMM
+    # reads the untransposed matrix's rows K-major
+    absorbed = []
+    bt = graph.ops[m].inputs[1]
+    if bt in pre_set and graph.ops[bt].op_type == OpType.TRANSPOSE:
+        users = [o for o in members if bt in graph.ops[o].inputs]
+        if users == [m] and graph.ops[m].inputs[0] != bt:
+            absorbed = [bt]
+            pre_set = pre_set - {bt}        # what bt reads is still computed first
     pre = [i for i in ordered if i in pre_set]
-    post = [i for i in ordered if i not in pre_set and i != m]
+    post = [i for i in ordered if i not in pre_set and i != m and i not in absorbed]
     post_set = set(post)
     epi, rest = [m], []
     epi_set = {m}
@@ -316,7 +329,7 @@ def split_group(graph: DataflowGraph, ordered: list) -> list:
     out = []
     if pre:
         out.append(("row" if any(graph.is_reduction(i) for i in pre) else "ew", pre))
-    out.append(("gemm", epi))
+    out.append(("gemm", epi + absorbed))
     if rest:
         out.append(("row" if any(graph.is_reduction(i) for i in rest) else "ew", rest))
     return out

@@ -280,8 +280,17 @@ def _plan_rope(graph, ops, outs, shapes, dts, tune) -> SubKernel:
 def _plan_gemm(graph, ops, ext, outs, shapes, dts, tune) -> SubKernel:
     mm = ops[0]
     a_id, b_id = graph.ops[mm].inputs
+    # B given as TRANSPOSE(Bt) with Bt [N, K]: read K-major, no copy
+    b_kmajor = graph.ops[b_id].op_type == OpType.TRANSPOSE and b_id in ops
+    if b_kmajor:
+        if b_id in outs:
+            raise LoweringError("a transposed GEMM operand cannot also be an output")
+        b_id = graph.ops[b_id].inputs[0]
+        if len(shapes[b_id]) != 2:
+            raise LoweringError("the transposed GEMM operand must be a matrix [N, K]")
+        ops = [o for o in ops if graph.ops[o].op_type != OpType.TRANSPOSE]
     a_shape, b_shape = shapes[a_id], shapes[b_id]
-    K, N = int(b_shape[0]), int(b_shape[1])
+    K, N = (int(b_shape[1]), int(b_shape[0])) if b_kmajor else (int(b_shape[0]), int(b_shape[1]))
     M = prod(a_shape[:-1])
     it = shapes[mm]
     for o in ops:
@@ -328,5 +337,6 @@ def _plan_gemm(graph, ops, ext, outs, shapes, dts, tune) -> SubKernel:
         raise LoweringError("GEMM epilogues are elementwise only")
     from .gemm_config import choose_gemm_config
     sk.config = choose_gemm_config(sk, tune.get("gemm") or {})
+    sk.config["b_kmajor"] = bool(b_kmajor)
     sk.config["needed"] = sorted(needed)
     return sk

@@ -181,7 +181,11 @@ class _Spec:
                 dt = sk.operands[sk.a_operand].dtype
                 A2 = A.reshape(-1, A.shape[-1])
                 ctypes.memmove(a.tmap_a, self.tmap(A2, dt, sk.m, sk.k, 64, 128), 128)
-                ctypes.memmove(a.tmap_b, self.tmap(B, dt, sk.k, sk.n, 64, 64), 128)
+                if sk.config.get("b_kmajor"):
+                    # B is the transpose of Bt [N, K]: its rows, K-major
+                    ctypes.memmove(a.tmap_b, self.tmap(B, dt, sk.n, sk.k, 64, sk.config["bn"]), 128)
+                else:
+                    ctypes.memmove(a.tmap_b, self.tmap(B, dt, sk.k, sk.n, 64, 64), 128)
                 a.m, a.n, a.k = sk.m, sk.n, sk.k
                 a.status = _capi.status_word(di)
             else:

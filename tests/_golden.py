@@ -45,6 +45,9 @@ def graph_for(meta, inputs):
         m, k = first.shape
         n = inputs["B"].shape[1]
         return graphs.gemm_bias_gelu(m, k, n, dtype=dt)
+    if kind == "attention_score":
+        m, d = first.shape
+        return graphs.attention_score(m, inputs["k"].shape[0], d, dtype=dt, scale=meta["scale"])
     if kind == "rope":
         b, sq, h, d = first.shape
         return graphs.rope(b, sq, h, d, dtype=dt, table_dtype=input_dtype(inputs["cos"]))

@@ -176,6 +176,15 @@ def make_numeric(ops):
     # the fp32 result before the helper's final cast to x.dtype
     save("rope_bf16", bf16, {"x": x, "cos": cos, "sin": sin},
          ops.rope_pytorch(x.float(), cos, sin), {"kind": "rope"})
+    # 7) attention scores exactly as the reference's helper (ops.py:55-59),
+    #    bf16 Q and K, fp32 arithmetic (fp64-accumulated product)
+    g = gen(8)
+    q = normal(g, (64, 128), dtype=bf16)
+    k = normal(g, (192, 128), dtype=bf16)
+    scale = 1.0 / 128 ** 0.5
+    save("attention_score_bf16", bf16, {"q": q, "k": k},
+         ops.attention_score_pytorch(q.double(), k.double(), scale).float(),
+         {"kind": "attention_score", "scale": scale})
 
 
 def make_fusion(ir, fusion, compiler):
@@ -265,6 +274,15 @@ def make_fusion(ir, fusion, compiler):
     k = g.add_input("k", TS([512, 4]))
     g.add_output(g.softmax(g.matmul(q, k)))
     cases["transformer_block"] = groups(g)
+
+    # attention scores, ops.py:55-59: softmax(Q @ K^T * scale)
+    g = DG("attention_score")
+    q = g.add_input("q", TS([256, 128]))
+    k = g.add_input("k", TS([512, 128]))
+    kt = g.add_op(OT.TRANSPOSE, [k], "kT")
+    sc = g.add_constant("scale", 0.08838834764831845)
+    g.add_output(g.softmax(g.mul(g.matmul(q, kt), sc)))
+    cases["attention_score"] = groups(g)
 
     # RoPE after RMSNorm (the reference builder's two-input rope, ir.py:175)
     g = DG("norm_rope")

@@ -191,6 +191,27 @@ def test_rope_kernels(tmp_path, style, packed):
     assert build_cubin(k.source, k.name, tmp_path).stat().st_size > 1000
 
 
+def test_attention_score_plan(tmp_path):
+    """[TRANSPOSE, MATMUL, MUL, SOFTMAX] (one group, as the reference fuses
+    it): a K-major-B GEMM with the scale in its epilogue, then a row
+    softmax; the TRANSPOSE is no kernel."""
+    (k,) = compile_graph(graphs.attention_score(256, 512, 128), dtype="bfloat16")
+    assert k.name == "molten_fused_transpose_matmul_mul_softmax"
+    gemm, row = k.plan.kernels
+    assert gemm.family == "gemm" and gemm.config["b_kmajor"] and (gemm.m, gemm.n, gemm.k) == (256, 512, 128)
+    assert row.family == "row"
+    assert ", true>(sh, args)" in k.source
+    assert build_cubin(k.source, k.name, tmp_path).stat().st_size > 1000
+
+
+def test_transpose_elsewhere_is_rejected():
+    g = DataflowGraph("t")
+    x = g.add_input("x", TS([8, 16]))
+    g.add_output(g.relu(g.transpose(x)))
+    with pytest.raises(LoweringError):
+        compile_graph(g)
+
+
 def test_rope_after_rmsnorm_splits_the_group():
     """The reference fuses [RMS, DIV, MUL, ROTATE] into one group; it runs as
     a row kernel and a RoPE kernel with an fp32 intermediate."""

@@ -122,6 +122,13 @@ def _reference_graphs():
     k = g.add_input("k", TS([512, 4]))
     g.add_output(g.softmax(g.matmul(q, k)))
     out["transformer_block"] = g
+    g = DataflowGraph("attention_score")
+    q = g.add_input("q", TS([256, 128]))
+    k = g.add_input("k", TS([512, 128]))
+    kt = g.add_op(OpType.TRANSPOSE, [k], "kT")
+    sc = g.add_constant("scale", 0.08838834764831845)
+    g.add_output(g.softmax(g.mul(g.matmul(q, kt), sc)))
+    out["attention_score"] = g
     g = DataflowGraph("norm_rope")
     x = g.add_input("x", TS([2, 16, 4, 64]))
     w = g.add_input("w", TS([64]))

@@ -422,6 +422,53 @@ def test_rmsnorm_then_rope_group(rt):
     assert_close(as_f32(out), res[("f32", g.ops[g._outputs[0]].inputs[0])], "bfloat16", "norm+rope")
 
 
+@pytest.mark.parametrize("m,n,d,dtype", [(256, 512, 128, "bfloat16"), (200, 300, 64, "bfloat16"),
+                                         (130, 1000, 256, "float16"), (64, 4096, 128, "bfloat16")])
+def test_attention_score(rt, m, n, d, dtype):
+    """softmax(Q @ K^T * scale) (ops.py:55-59): the GEMM reads K's rows
+    K-major (the TRANSPOSE costs nothing), scale in its epilogue, fp32
+    scores, row softmax."""
+    g = graphs.attention_score(m, n, d, dtype=dtype)
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(m + n + d)
+    q = torch.randn(m, d, generator=gen, device=DEV).to(TORCH_DT[dtype])
+    k = torch.randn(n, d, generator=gen, device=DEV).to(TORCH_DT[dtype])
+    (kern,) = compile_graph(g, dtype=dtype)
+    assert [sk.family for sk in kern.plan.kernels] == ["gemm", "row"]
+    assert kern.plan.kernels[0].config["b_kmajor"]
+    out = rt.compile(kern)(q, k)
+    torch.cuda.synchronize()
+    assert MoltenRuntime.read_status(0) == 0
+    res = orc.evaluate(g, {"q": to_numpy(q), "k": to_numpy(k)})
+    ref = res[("f32", g.ops[g._outputs[0]].inputs[0])]
+    assert_close(as_f32(out), ref, dtype, f"attention {m}x{n}x{d} {dtype}")
+    sums = as_f32(out).astype(np.float64).sum(axis=1)
+    assert np.all(np.abs(sums - 1.0) < 2e-2)
+
+
+def test_gemm_with_transposed_b(rt):
+    """GELU(A @ Bt^T + bias) with Bt [N, K]: the K-major B path on its own."""
+    from molten_b200.ir import DataflowGraph, TensorShape as TS
+    m, k, n = 300, 512, 384
+    g = DataflowGraph("gemm_bt")
+    a = g.add_input("A", TS([m, k]), dtype="bfloat16")
+    bt = g.add_input("Bt", TS([n, k]), dtype="bfloat16")
+    bias = g.add_input("bias", TS([n]), dtype="bfloat16")
+    g.add_output(g.gelu(g.add(g.matmul(a, g.transpose(bt)), bias)))
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(77)
+    A = torch.randn(m, k, generator=gen, device=DEV).to(torch.bfloat16)
+    Bt = (torch.randn(n, k, generator=gen, device=DEV) / k ** 0.5).to(torch.bfloat16)
+    bb = (0.02 * torch.randn(n, generator=gen, device=DEV)).to(torch.bfloat16)
+    (kern,) = compile_graph(g, dtype="bfloat16")
+    assert [sk.family for sk in kern.plan.kernels] == ["gemm"] and kern.plan.kernels[0].config["b_kmajor"]
+    out = rt.compile(kern)(A, Bt, bb)
+    torch.cuda.synchronize()
+    assert MoltenRuntime.read_status(0) == 0
+    res = orc.evaluate(g, {"A": to_numpy(A), "Bt": to_numpy(Bt), "bias": to_numpy(bb)})
+    assert_close(as_f32(out), res[("f32", g.ops[g._outputs[0]].inputs[0])], "bfloat16", "gemm Bt")
+
+
 def test_misaligned_pointers_take_the_scalar_path(rt):
     g = graphs.rmsnorm(4, 512)
     base = torch.randn(4 * 512 + 1, device=DEV)
