@@ -86,6 +86,17 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory");
 }
+// Bulk form (one CTA per row): one thread copies a whole row of a staged
+// operand with one untiled bulk copy into this CTA's shared memory,
+// completing bytes on the stage's mbarrier.  Source and size are 16-byte
+// multiples.
+__device__ __forceinline__ void bulk_row_g2s(uint32_t dst, const void* src, uint32_t bytes,
+                                             uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               :: "r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+}
+enum RowStageStatus { kRowTimeoutStage = 256 };
+
 template <typename T, int VEC>
 __device__ __forceinline__ Slot<T, VEC> lds_slot16(uint32_t addr) {
   static_assert(sizeof(T) * VEC == 16, "staged slots are 16 bytes");

@@ -286,10 +286,26 @@ def emit_row(sk: SubKernel, name: str) -> str:
     hoisted = [i for i in sorted(prefetch) if i not in staged]
     if not staged:
         raise LoweringError("the stream form needs a row-indexed streamed operand")
+    bulk = bool(cfg.get("bulk"))
     e.w(f"  constexpr int STAGES = {stream}, NSTAGED = {len(staged)};")
-    e.w("  constexpr uint32_t STAGE_BYTES = NSTAGED * NV * (TPC * RPC) * 16u;")
-    e.w("  extern __shared__ __align__(16) uint8_t stage_smem[];")
-    e.w("  const uint32_t lanes = shared_addr(stage_smem) + threadIdx.x * 16u;")
+    if bulk:
+        offs = cfg["bulk_offsets"]
+        e.w(f"  constexpr uint32_t STAGE_BYTES = {cfg['stage_bytes']}u;   // whole rows, 128-byte aligned")
+        e.w("  constexpr uint32_t " + ", ".join(f"OFF{p} = {o}u" for p, o in enumerate(offs)) + ";")
+        e.w("  extern __shared__ __align__(128) uint8_t stage_smem[];")
+        e.w("  __shared__ __align__(8) unsigned long long sbar[STAGES];")
+        e.w("  __shared__ int sabort;")
+        e.w("  const uint32_t sbase = shared_addr(stage_smem);")
+        e.w("  if (threadIdx.x == 0) {")
+        e.w("    for (int s = 0; s < STAGES; ++s) xch_init(shared_addr(&sbar[s]));")
+        e.w("    sabort = 0;")
+        e.w("    xch_init_fence();")
+        e.w("  }")
+        e.w("  __syncthreads();")
+    else:
+        e.w("  constexpr uint32_t STAGE_BYTES = NSTAGED * NV * (TPC * RPC) * 16u;")
+        e.w("  extern __shared__ __align__(16) uint8_t stage_smem[];")
+        e.w("  const uint32_t lanes = shared_addr(stage_smem) + threadIdx.x * 16u;")
     e.w("  const long long step = (long long)(gridDim.x / CL) * RPC;")
     e.w("  const long long base0 = (long long)(blockIdx.x / CL) * RPC;")
     for i in hoisted:
@@ -308,10 +324,12 @@ def emit_row(sk: SubKernel, name: str) -> str:
     push = CL > 1
     if push:
         _emit_exchange_setup(e, n_areas, max_nr)
+    stage_row = _emit_bulk_row if bulk else _emit_stage_row
     e.w("#pragma unroll 1")
     e.w("  for (int s = 0; s < STAGES - 1; ++s) {")
-    _emit_stage_row(e, staged, masked_only, "base0 + s * step + tm.team", "s", "    ")
-    e.w("    cp_async_commit();")
+    stage_row(e, staged, masked_only, "base0 + s * step + tm.team", "s", "    ")
+    if not bulk:
+        e.w("    cp_async_commit();")
     e.w("  }")
     if push:
         e.w("  cluster_wait();")
@@ -322,10 +340,15 @@ def emit_row(sk: SubKernel, name: str) -> str:
     e.w("    const uint32_t par = use & 1u, xph = (use >> 1) & 1u;   // area set, barrier phase")
     e.w("    (void)par; (void)xph;")
     e.w("    // the row STAGES-1 ahead goes into the stage read one row ago")
-    _emit_stage_row(e, staged, masked_only, "base + (STAGES - 1) * step + tm.team",
-                    "(st == 0 ? STAGES - 1 : st - 1)", "    ")
-    e.w("    cp_async_commit();")
-    e.w("    cp_async_wait<STAGES - 1>();        // this thread's copies of row `base` landed")
+    stage_row(e, staged, masked_only, "base + (STAGES - 1) * step + tm.team",
+              "(st == 0 ? STAGES - 1 : st - 1)", "    ")
+    if bulk:
+        # every thread read that stage before the previous row's reduction
+        # barrier, which all threads have passed: it is free to refill
+        e.w("    xch_wait(shared_addr(&sbar[st]), (use / STAGES) & 1u, &sabort);   // row `base` landed")
+    else:
+        e.w("    cp_async_commit();")
+        e.w("    cp_async_wait<STAGES - 1>();        // this thread's copies of row `base` landed")
     e.w("    const long long lrow = base + tm.team;")
     e.w("    const long long grow = args.row_offset + lrow;")
     e.w("    const bool rok = lrow < args.rows;")
@@ -337,7 +360,10 @@ def emit_row(sk: SubKernel, name: str) -> str:
     e.w("    st = (st + 1 == STAGES) ? 0 : st + 1;")
     e.w("    ++use;")
     e.w("  }")
-    e.w("  cp_async_wait<0>();")
+    if bulk:
+        e.w("  if (threadIdx.x == 0 && sabort && args.status) atomicOr(args.status, kRowTimeoutStage);")
+    else:
+        e.w("  cp_async_wait<0>();")
     if push:
         _emit_exchange_teardown(e)
     e.w("}")
@@ -370,6 +396,49 @@ def _emit_exchange_teardown(e: _Emitter):
     e.w("  if (threadIdx.x == 0 && xabort && args.status) atomicOr(args.status, kRowTimeoutExchange);")
     e.w("  cluster_arrive_relaxed();")
     e.w("  cluster_wait();")
+
+
+def _emit_bulk_row(e: _Emitter, staged, masked_only, row_expr: str, stage_expr: str, indent: str):
+    """Thread 0 arms stage ``stage_expr``'s mbarrier with the byte count of
+    local row ``row_expr`` (if it exists) and copies each staged operand's
+    row with one bulk copy; a causal softmax's operand is copied only up to
+    its last visible slot."""
+    sk = e.sk
+
+    def w(s):
+        e.w(indent + s)
+
+    w("if (threadIdx.x == 0) {")
+    w(f"  const long long fr = {row_expr};")
+    w("  if (fr < args.rows) {")
+    w("    const long long fg = args.row_offset + fr;")
+    w("    (void)fg;")
+    w(f"    const uint32_t bar = shared_addr(&sbar[{stage_expr}]);")
+    w(f"    const uint32_t dst = sbase + (uint32_t)({stage_expr}) * STAGE_BYTES;")
+    terms = []
+    for p, i in enumerate(staged):
+        opd = sk.operands[i]
+        ct = _ctype(opd.dtype)
+        row_bytes = sk.cols * (2 if opd.dtype != "float32" else 4)
+        w(f"    const {ct}* src{p} = static_cast<const {ct}*>(args.in[{i}]) + "
+          f"{_row_index_expr(opd, 'fr', 'fg')} * COLS;")
+        if i in masked_only:
+            mk = masked_only[i]
+            v = e.values[mk]
+            period = _mask_period(v, sk.cols)
+            off = int(v.attrs.get("offset", 0))
+            w(f"    const int fl{p} = clamp_col_limit((fg % {period}LL) + ({off}LL));")
+            # visible slots 0 .. fl / VEC, 16 bytes each
+            w(f"    const uint32_t nb{p} = fl{p} < 0 ? 0u : "
+              f"(uint32_t)min((long long){row_bytes}, ((long long)fl{p} / VEC + 1) * 16LL);")
+        else:
+            w(f"    const uint32_t nb{p} = {row_bytes}u;")
+        terms.append(f"nb{p}")
+    w(f"    xch_arm(bar, {' + '.join(terms)});")
+    for p, i in enumerate(staged):
+        w(f"    if (nb{p}) bulk_row_g2s(dst + OFF{p}, src{p}, nb{p}, bar);")
+    w("  }")
+    w("}")
 
 
 def _emit_stage_row(e: _Emitter, staged, masked_only, row_expr: str, stage_expr: str, indent: str):
@@ -451,7 +520,11 @@ def _emit_row_body(e: _Emitter, closures, reds, smx, materialize, prefetch, mask
         for i in per_row:
             opd = sk.operands[i]
             ct = _ctype(opd.dtype)
-            if staged:
+            if staged and sk.config.get("bulk"):
+                p = staged.index(i)
+                load = (f"s{i}[k] = lds_slot16<{ct}, VEC>(sbase + (uint32_t)(st * STAGE_BYTES + "
+                        f"OFF{p} + j * 16));")
+            elif staged:
                 p = staged.index(i)
                 load = (f"s{i}[k] = lds_slot16<{ct}, VEC>(lanes + (uint32_t)(st * STAGE_BYTES + "
                         f"({p} * NV + k) * (TPC * RPC) * 16));")

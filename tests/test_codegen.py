@@ -117,7 +117,7 @@ def test_long_16bit_rows_take_the_stream_form():
     sk = compile_graph(graphs.softmax((4096, 32768), dtype="bfloat16"), dtype="bfloat16")[0] \
         .plan.kernels[0]
     assert (sk.config["tpc"], sk.config["cl"], sk.config["stream"]) == (1024, 1, 3)
-    assert sk.config["smem"] == 3 * 4 * 1024 * 16
+    assert sk.config["bulk"] and sk.config["smem"] == 3 * 32768 * 2
     sk = compile_graph(graphs.softmax((4096, 32768)))[0].plan.kernels[0]
     assert sk.config["cl"] > 1 and not sk.config.get("stream")
 

@@ -261,6 +261,10 @@ STREAM_CASES = [
     ("rmsnorm", 999, 8192, "float32", {"stream": 3, "engine": "regs", "tpc": 128, "cl": 4}),
     ("softmax", 1000, 32768, "float32", {"stream": 3, "tpc": 1024, "cl": 2, "min_blocks": 1}),
     ("rmsnorm_silu", 1000, 3584, "bfloat16", {"stream": 4, "engine": "regs"}),
+    # bulk staging: one bulk copy per row and staged operand, mbarrier per stage
+    ("softmax", 300, 32768, "bfloat16", {"stream": 3, "tpc": 1024, "cl": 1, "bulk": True}),
+    ("softmax_causal", 700, 8192, "bfloat16", {"stream": 3, "tpc": 1024, "cl": 1, "bulk": True}),
+    ("rmsnorm_silu", 1000, 3584, "bfloat16", {"stream": 4, "engine": "regs", "bulk": True}),
 ]
 
 
@@ -295,6 +299,7 @@ def test_stream_row_engine(kind, rows, cols, dtype, tune):
     gk = CodeGenerator(tune=rt.tune).generate(g, FusionEngine().fuse(g)[0], shapes,
                                               {i: dtype for i in shapes})
     assert gk.plan.kernels[0].config.get("stream", 0) >= 2, gk.plan.kernels[0].config
+    assert bool(gk.plan.kernels[0].config.get("bulk")) == bool(tune.get("bulk"))
     ck = rt.compile(gk)
     out = ck(*xs)
     torch.cuda.synchronize()
