@@ -143,7 +143,7 @@ def cpu_sample(w, fraction_rows=None):
         cols = shape[-1]
         rows = max(1, min(int(__import__("numpy").prod(shape[:-1])), (fraction_rows or 1024)))
         p["shape"] = (rows, cols)
-    elif w.kind == "gemm_bias_gelu":
+    elif w.kind in workloads.GEMM_KINDS:
         p["m"] = min(p["m"], fraction_rows or 256)
     elif w.kind == "rope":
         p["batch"] = 1
@@ -172,13 +172,14 @@ def time_cpu(w, budget_s: float, threads: int):
         if len(times) >= 200:
             break
     t = statistics.median(times)
-    work = sw.flops_per_call if w.kind == "gemm_bias_gelu" else sw.bytes_per_call
+    work = sw.flops_per_call if w.kind in workloads.GEMM_KINDS else sw.bytes_per_call
     desc = f"{sw.kind} {sw.params} {sw.dtype}, median of {len(times)} calls"
     return work / t, desc, t
 
 
 def metric_of(w):
-    if w.kind == "gemm_bias_gelu":
+    from molten_b200 import workloads
+    if w.kind in workloads.GEMM_KINDS:
         return "epilogue GEMM TFLOP/s", "TFLOP/s", 1e12
     return "fused-kernel HBM GB/s", "GB/s", 1e9
 
@@ -234,7 +235,7 @@ def run_molten(args, w):
     tune = json.loads(args.tune) if args.tune else None
     rt = MoltenRuntime(tune=tune)
     metric, unit, scale = metric_of(w)
-    is_gemm = w.kind == "gemm_bias_gelu"
+    is_gemm = w.kind in workloads.GEMM_KINDS
 
     # ---- inputs (this rank's rows, or its column block for the GEMM)
     xs = workloads.make_inputs(w, seed=rank if not is_gemm else 0, device=dev)
@@ -242,8 +243,8 @@ def run_molten(args, w):
     if is_gemm:
         n = w.params["n"]
         n0, n1 = col_shards(n, world)[rank]
-        A, B, bias = xs
-        xs = [A, B[:, n0:n1].contiguous(), bias[n0:n1].contiguous()]
+        *lead, B, bias = xs             # [A, B, bias] or [x, w, B, bias]
+        xs = [*lead, B[:, n0:n1].contiguous(), bias[n0:n1].contiguous()]
         w_local = workloads.scaled(w, n=n1 - n0)
         scaling = "strong" if world > 1 else "weak"
     else:

@@ -149,9 +149,12 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&r)[32]) {
 }
 
 // ------------------------------------------------------------ the engine
-template <int BM_, int BN_, int BK_, int STAGES_, int GROUP_M_ = 16>
+// PRO_: an RMSNorm prologue (see gemm_roles): 4 more warps, a "ready"
+// barrier per stage, a double-buffered per-row 1/rms and its barriers.
+template <int BM_, int BN_, int BK_, int STAGES_, int GROUP_M_ = 16, bool PRO_ = false>
 struct GemmLayout {
   static constexpr int BM = BM_, BN = BN_, BK = BK_, STAGES = STAGES_, GROUP_M = GROUP_M_;
+  static constexpr bool PRO = PRO_;
   static_assert(BM == 128, "one CTA owns the 128 TMEM lanes");
   static_assert(BK == 64, "BK is one 128-byte swizzle row of 16-bit elements");
   static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be 64..256, a multiple of 64");
@@ -162,10 +165,14 @@ struct GemmLayout {
   static constexpr int ACC_BUFS = 2;
   static constexpr int TMEM_COLS = (2 * BN <= 128) ? 128 : ((2 * BN <= 256) ? 256 : 512);
   // barriers: full[S], empty[S], acc_full[2], acc_empty[2], done
+  //           [+ ready[S], rms_full[2], rms_empty[2] with the prologue]
   static constexpr int BAR_OFFSET = STAGES * STAGE_BYTES;
-  static constexpr int NUM_BARS = 2 * STAGES + 5;
-  static constexpr int SMEM_BYTES = BAR_OFFSET + NUM_BARS * 8 + 16 + 1024;  // + alignment slack
-  static constexpr int THREADS = 256;                        // 8 warps
+  static constexpr int NUM_BARS = 2 * STAGES + 5 + (PRO ? STAGES + 4 : 0);
+  static constexpr int RSQ_BYTES = PRO ? 2 * BM * 4 : 0;     // 1/rms of the tile rows, x2
+  static constexpr int SMEM_BYTES = BAR_OFFSET + NUM_BARS * 8 + 16 + RSQ_BYTES + 1024;
+  static constexpr int THREADS = PRO ? 512 : 256;            // 8 warps (+8 prologue warps)
+  static constexpr int PRO_WARP0 = 8;
+  static constexpr int PRO_WARPS = 8;                         // 2 threads per A-tile row
   static constexpr int EPI_WARP0 = 4;                        // warps 4..7: TMEM lane quarters 0..3
   static constexpr int EPI_WARPS = 4;
 };
@@ -175,6 +182,17 @@ struct GemmShared {
   uint64_t* bars;
   uint32_t* tmem_slot;
   volatile int* abort_flag;
+  float* rsq;              // prologue only: [2][BM] per-row 1/rms
+};
+
+// No prologue: A is used as loaded.
+struct NoPrologue {
+  static constexpr bool ENABLED = false;
+  static constexpr float EPS = 0.0f;
+  __device__ __forceinline__ static void w32(const GemmArgs&, long long, float (&w)[32]) {
+#pragma unroll
+    for (int e = 0; e < 32; ++e) w[e] = 1.0f;
+  }
 };
 
 template <class L>
@@ -185,6 +203,7 @@ __device__ __forceinline__ GemmShared gemm_carve(uint8_t* raw) {
   s.bars = reinterpret_cast<uint64_t*>(s.tiles + L::BAR_OFFSET);
   s.tmem_slot = reinterpret_cast<uint32_t*>(s.bars + L::NUM_BARS);
   s.abort_flag = reinterpret_cast<volatile int*>(s.tmem_slot + 1);
+  s.rsq = reinterpret_cast<float*>(s.tmem_slot + 4);      // 16-byte aligned
   return s;
 }
 
@@ -215,6 +234,9 @@ template <class L> struct Bars {
   __device__ __forceinline__ uint32_t acc_full(int b) const { return base + 8u * (2 * L::STAGES + b); }
   __device__ __forceinline__ uint32_t acc_empty(int b) const { return base + 8u * (2 * L::STAGES + 2 + b); }
   __device__ __forceinline__ uint32_t done() const { return base + 8u * (2 * L::STAGES + 4); }
+  __device__ __forceinline__ uint32_t ready(int i) const { return base + 8u * (2 * L::STAGES + 5 + i); }
+  __device__ __forceinline__ uint32_t rms_full(int b) const { return base + 8u * (3 * L::STAGES + 5 + b); }
+  __device__ __forceinline__ uint32_t rms_empty(int b) const { return base + 8u * (3 * L::STAGES + 7 + b); }
 };
 
 __device__ __forceinline__ void gemm_fail(const GemmShared& s, const GemmArgs& args, int code) {
@@ -232,6 +254,10 @@ __device__ __forceinline__ void gemm_init(const GemmShared& s, const GemmArgs& a
     for (int i = 0; i < L::STAGES; ++i) { mbar_init(b.full(i), 1); mbar_init(b.empty(i), 1); }
     for (int i = 0; i < 2; ++i) { mbar_init(b.acc_full(i), 1); mbar_init(b.acc_empty(i), L::EPI_WARPS); }
     mbar_init(b.done(), 1);
+    if constexpr (L::PRO) {
+      for (int i = 0; i < L::STAGES; ++i) mbar_init(b.ready(i), L::PRO_WARPS);   // one per warp
+      for (int i = 0; i < 2; ++i) { mbar_init(b.rms_full(i), L::PRO_WARPS); mbar_init(b.rms_empty(i), L::EPI_WARPS); }
+    }
     *s.abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" :: "l"(&args.tmap_a) : "memory");
@@ -248,7 +274,16 @@ __device__ __forceinline__ void gemm_init(const GemmShared& s, const GemmArgs& a
 // The three roles.  Epi::apply(args, row, col0, acc[32]) writes C[row, col0..col0+31].
 // B_KMAJOR: tmap_b describes Bt [N, K] (inner K) with box {64, BN}; a stage
 // holds BN rows of 128 bytes, the same 128-byte-swizzled K-major layout as A.
-template <class L, bool F16IN, class Epi, bool B_KMAJOR = false>
+// Pro (ENABLED): C = diag(1/rms(x)) ((x * w) B) for A = rmsnorm(x, w) with
+// rms(x) = sqrt(mean_k x^2 + EPS): warps 8..11 (one tile row per thread)
+// take each landed A stage, multiply row r's elements by w[k] in shared
+// memory (one bf16/fp16 rounding of x*w; the 128-byte swizzle puts logical
+// 16-byte chunk c of row r at chunk c ^ (r mod 8)), accumulate sum x^2,
+// make the writes visible to the tensor core (async proxy) and arrive on
+// the stage's "ready" barrier, which the MMA waits for instead of "full".
+// After a tile's K loop they publish 1/rms per row; the epilogue scales the
+// accumulator rows by it.
+template <class L, bool F16IN, class Epi, bool B_KMAJOR = false, class Pro = NoPrologue>
 __device__ __forceinline__ void gemm_roles(const GemmShared& s, const GemmArgs& args) {
   tc_fence_after();
   const int tid = gemm_tid(), warp = tid / 32, lane = tid % 32;
@@ -309,7 +344,8 @@ __device__ __forceinline__ void gemm_roles(const GemmShared& s, const GemmArgs& 
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(b * L::BN);
         for (int kb = 0; kb < KB; ++kb) {
-          if (!mbar_wait(bar.full(st), ph)) { gemm_fail(s, args, kGemmTimeoutFull); ok = false; break; }
+          const uint32_t in_bar = Pro::ENABLED ? bar.ready(st) : bar.full(st);
+          if (!mbar_wait(in_bar, ph)) { gemm_fail(s, args, kGemmTimeoutFull); ok = false; break; }
           tc_fence_after();
           const uint32_t a_base = smem_u32(s.tiles + st * L::STAGE_BYTES);
           const uint32_t b_base = a_base + L::A_BYTES;
@@ -330,7 +366,73 @@ __device__ __forceinline__ void gemm_roles(const GemmShared& s, const GemmArgs& 
       umma_commit(bar.done());
       if (!mbar_wait(bar.done(), 0u)) { if (args.status) atomicOr(args.status, kGemmTimeoutDrain); }
     }
-  } else if (warp >= L::EPI_WARP0) {
+  } else if (Pro::ENABLED && warp >= L::PRO_WARP0) {
+    // ------------------------------------------------------------- prologue
+    if constexpr (Pro::ENABLED) {
+      const int p = tid - L::PRO_WARP0 * 32;       // 0 .. 2*BM-1
+      const int r = p >> 1, half = p & 1;          // tile row; 16-byte chunks 4*half .. +3
+      const uint32_t swz = (uint32_t)(r & 7);
+      uint32_t st = 0, ph = 0;
+      long long i = 0;
+      bool ok = true;
+      for (long long tile = blockIdx.x; tile < T && ok && !*s.abort_flag; tile += gridDim.x, ++i) {
+        float ss = 0.0f;
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(bar.full(st), ph)) { gemm_fail(s, args, kGemmTimeoutFull); ok = false; break; }
+          const uint32_t row_addr = smem_u32(s.tiles + st * L::STAGE_BYTES) + (uint32_t)r * 128u;
+          const long long kh = (long long)kb * L::BK + 32 * half;       // first k of this half
+          // all loads first: 4 chunks of A, 32 weights
+          uint4 v[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t a = row_addr + ((((uint32_t)(4 * half + j)) ^ swz) << 4);
+            asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                         : "=r"(v[j].x), "=r"(v[j].y), "=r"(v[j].z), "=r"(v[j].w) : "r"(a));
+          }
+          float w[32];
+          Pro::w32(args, kh, w);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if (kh + 8 * j >= args.k) break;          // K is a multiple of 8; the rest is zero
+            uint32_t* u = reinterpret_cast<uint32_t*>(&v[j]);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              float x0, x1;
+              if constexpr (F16IN) {
+                const __half2 hx = *reinterpret_cast<const __half2*>(&u[q]);
+                x0 = __low2float(hx); x1 = __high2float(hx);
+                const __half2 y = __floats2half2_rn(x0 * w[8 * j + 2 * q], x1 * w[8 * j + 2 * q + 1]);
+                u[q] = *reinterpret_cast<const uint32_t*>(&y);
+              } else {
+                x0 = __uint_as_float(u[q] << 16);
+                x1 = __uint_as_float(u[q] & 0xFFFF0000u);
+                const __nv_bfloat162 y = __floats2bfloat162_rn(x0 * w[8 * j + 2 * q], x1 * w[8 * j + 2 * q + 1]);
+                u[q] = *reinterpret_cast<const uint32_t*>(&y);
+              }
+              ss = fmaf(x0, x0, fmaf(x1, x1, ss));
+            }
+            const uint32_t a = row_addr + ((((uint32_t)(4 * half + j)) ^ swz) << 4);
+            asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};"
+                         :: "r"(a), "r"(v[j].x), "r"(v[j].y), "r"(v[j].z), "r"(v[j].w) : "memory");
+          }
+          // generic-proxy writes -> visible to the tensor core's reads; one
+          // arrival per warp once all its lanes are done
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar.ready(st));
+          if (++st == (uint32_t)L::STAGES) { st = 0; ph ^= 1u; }
+        }
+        if (!ok) break;
+        ss += __shfl_xor_sync(0xffffffffu, ss, 1);    // the row's two halves
+        const int b = (int)(i & 1);
+        const uint32_t rph = (uint32_t)((i >> 1) & 1);
+        if (!mbar_wait(bar.rms_empty(b), rph ^ 1u)) { gemm_fail(s, args, kGemmTimeoutAcc); break; }
+        if (half == 0) s.rsq[b * L::BM + r] = rsqrtf(ss / (float)args.k + Pro::EPS);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar.rms_full(b));
+      }
+    }
+  } else if (warp >= L::EPI_WARP0 && warp < L::EPI_WARP0 + L::EPI_WARPS) {
     // ------------------------------------------------------------- epilogue
     const int quarter = warp % 4;                  // TMEM lanes 32*quarter .. +31
     long long i = 0;
@@ -347,10 +449,25 @@ __device__ __forceinline__ void gemm_roles(const GemmShared& s, const GemmArgs& 
       gemm_tile_coords<L>(tile, MB, NB, m0, n0);
       const long long row = (long long)m0 + quarter * 32 + lane;
       const long long nbase = n0;
+      float rinv = 1.0f;
+      if constexpr (Pro::ENABLED) {
+        const bool gr = mbar_wait(bar.rms_full(b), acc_ph);
+        if (!__all_sync(0xffffffffu, gr ? 1 : 0)) {
+          if (lane == 0) gemm_fail(s, args, kGemmTimeoutAcc);
+          break;
+        }
+        rinv = s.rsq[b * L::BM + quarter * 32 + lane];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar.rms_empty(b));
+      }
 #pragma unroll 1
       for (int c = 0; c < L::BN / 32; ++c) {
         float acc[32];
         tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * L::BN + c * 32), acc);
+        if constexpr (Pro::ENABLED) {
+#pragma unroll
+          for (int q = 0; q < 32; ++q) acc[q] *= rinv;
+        }
         const long long col0 = nbase + 32 * c;
         if (col0 < args.n) Epi::apply(args, row, col0, acc);
       }

@@ -31,7 +31,31 @@ def emit_gemm(sk: SubKernel, name: str) -> str:
     w("")
     w("namespace {")
     w(f"constexpr int TILE_M = {BM}, TILE_N = {BN}, TILE_K = {BK}, STAGES = {ST};")
-    w(f"typedef GemmLayout<TILE_M, TILE_N, TILE_K, STAGES, {cfg.get('group_m', 16)}> Layout_{name};")
+    pro = cfg.get("prologue")
+    w(f"typedef GemmLayout<TILE_M, TILE_N, TILE_K, STAGES, {cfg.get('group_m', 16)}, "
+      f"{'true' if pro else 'false'}> Layout_{name};")
+    if pro:
+        wt = DTYPE_CTYPE[pro["w_dtype"]]
+        w(f"// RMSNorm prologue: A = x / sqrt(mean(x^2) + eps) * w, normalised as it is staged")
+        w(f"struct Prologue_{name} {{")
+        w("  static constexpr bool ENABLED = true;")
+        w(f"  static constexpr float EPS = {c_float(pro['eps'])};")
+        w("  // w[k0 .. k0 + 31] (k0 a multiple of 8; 0 beyond K, which is a multiple of 8)")
+        w("  __device__ __forceinline__ static void w32(const GemmArgs& args, long long k0, float (&w)[32]) {")
+        w(f"    const {wt}* p = static_cast<const {wt}*>(args.in[{pro['w']}]);")
+        w("#pragma unroll")
+        w("    for (int q = 0; q < 4; ++q) {")
+        w(f"      Slot<{wt}, 8> s;")
+        w(f"      if (k0 + 8 * q < args.k) s = load_slot<kLoadDefault, {wt}, 8>(p + k0 + 8 * q);")
+        w("      else {")
+        w("#pragma unroll")
+        w(f"        for (int e = 0; e < 8; ++e) s.v[e] = from_f32<{wt}>(0.0f);")
+        w("      }")
+        w("#pragma unroll")
+        w("      for (int e = 0; e < 8; ++e) w[8 * q + e] = to_f32(s.v[e]);")
+        w("    }")
+        w("  }")
+        w("};")
     w(f"struct Epilogue_{name} {{")
     w("  // C[row, col0 .. col0 + 31] from the fp32 accumulators of one TMEM row")
     w("  __device__ __forceinline__ static void apply(const GemmArgs& args, long long row,")
@@ -116,7 +140,7 @@ def emit_gemm(sk: SubKernel, name: str) -> str:
     w("};")
     w("}  // namespace")
     w("")
-    w(f"extern \"C\" __global__ void __launch_bounds__(256, 1) "
+    w(f"extern \"C\" __global__ void __launch_bounds__({cfg['threads']}, 1) "
       f"{name}(const __grid_constant__ GemmArgs args) {{")
     w("  extern __shared__ __align__(1024) uint8_t smem_raw[];")
     w(f"  const GemmShared sh = gemm_carve<Layout_{name}>(smem_raw);")
@@ -124,7 +148,8 @@ def emit_gemm(sk: SubKernel, name: str) -> str:
     w("  pdl_enter();                            // no global access before this")
     w("  __syncthreads();")
     kmaj = "true" if cfg.get("b_kmajor") else "false"
-    w(f"  gemm_roles<Layout_{name}, {f16in}, Epilogue_{name}, {kmaj}>(sh, args);")
+    pro_t = f"Prologue_{name}" if pro else "NoPrologue"
+    w(f"  gemm_roles<Layout_{name}, {f16in}, Epilogue_{name}, {kmaj}, {pro_t}>(sh, args);")
     w("  __syncthreads();")
     w(f"  gemm_teardown<Layout_{name}>(sh);       // TMEM release")
     w("}")

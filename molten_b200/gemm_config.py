@@ -12,7 +12,7 @@ def choose_gemm_config(sk, override: dict) -> dict:
     BK = 64 bf16 = one 128-byte swizzle row.  BN is chosen to balance the
     persistent tile loop over the SMs.
     """
-    o = dict(override or {})
+    o = {k: v for k, v in dict(override or {}).items() if k != "prologue"}
     M, N, K = sk.m, sk.n, sk.k
     bm = o.get("bm", 128)
     bk = o.get("bk", 64)

@@ -116,3 +116,18 @@ def attention_score(m=2048, n=2048, d=128, dtype="bfloat16", scale=None) -> Data
 
 
 BUILDERS["attention_score"] = attention_score
+
+
+def rmsnorm_gemm(m=8192, k=4096, n=14336, dtype="bfloat16", eps=1e-6) -> DataflowGraph:
+    """GELU(rmsnorm(x, w) @ B + bias): the RMSNorm -> GEMM prologue pattern
+    (one fusion group [RMS, DIV, MUL, MATMUL, ADD, GELU])."""
+    g = DataflowGraph("rmsnorm_gemm")
+    x = g.add_input("x", TensorShape([m, k]), dtype=dtype)
+    w = g.add_input("w", TensorShape([k]), dtype=dtype)
+    B = g.add_input("B", TensorShape([k, n]), dtype=dtype)
+    bias = g.add_input("bias", TensorShape([n]), dtype=dtype)
+    g.add_output(g.gelu(g.add(g.matmul(g.rms_norm(x, w, "norm", eps=eps), B, "mm"), bias)))
+    return g
+
+
+BUILDERS["rmsnorm_gemm"] = rmsnorm_gemm

@@ -281,7 +281,34 @@ def group_boundary(graph: DataflowGraph, op_ids):
     return ext, outs, ordered
 
 
-def split_group(graph: DataflowGraph, ordered: list) -> list:
+def rms_prologue(graph: DataflowGraph, m: int, members: set, outs=()):
+    """(rms, div, mul) op ids when MATMUL ``m``'s A operand is
+    ``x / RMS(x) * w`` (``DataflowGraph.rms_norm``, ``ir.py:169-173``) and each
+    of those ops is used only along that chain and is not a group output;
+    else None.  Such a group runs as one GEMM that normalises A as it is
+    staged (the RMSNorm -> GEMM prologue)."""
+    a = graph.ops[m].inputs[0]
+    mul = graph.ops[a]
+    if a not in members or mul.op_type != OpType.MUL or a in outs or a == graph.ops[m].inputs[1]:
+        return None
+    for d_id, w_id in ((mul.inputs[0], mul.inputs[1]), (mul.inputs[1], mul.inputs[0])):
+        d = graph.ops[d_id]
+        if d_id not in members or d.op_type != OpType.DIV or d_id in outs:
+            continue
+        x_id, r_id = d.inputs
+        r = graph.ops[r_id]
+        if r_id not in members or r.op_type != OpType.RMS or r.inputs != [x_id] or r_id in outs:
+            continue
+        chain = {r_id, d_id, a}
+        if x_id in chain or w_id in chain:
+            continue
+        users = {o: [u for u in members if o in graph.ops[u].inputs] for o in chain}
+        if users[r_id] == [d_id] and users[d_id] == [a] and users[a] == [m]:
+            return [r_id, d_id, a]
+    return None
+
+
+def split_group(graph: DataflowGraph, ordered: list, outs=(), fuse_prologue: bool = True) -> list:
     """Split a group's live ops into (family, ops) sub-kernels.
 
     ROTATE (RoPE) reads each element's pair partner, so it runs as a
@@ -294,8 +321,8 @@ def split_group(graph: DataflowGraph, ordered: list) -> list:
         pre_set = _deps_within(graph, r, set(ordered))
         pre = [i for i in ordered if i in pre_set]
         rest = [i for i in ordered if i not in pre_set and i != r]
-        return ((split_group(graph, pre) if pre else []) + [("rope", [r])]
-                + (split_group(graph, rest) if rest else []))
+        return ((split_group(graph, pre, outs, fuse_prologue) if pre else []) + [("rope", [r])]
+                + (split_group(graph, rest, outs, fuse_prologue) if rest else []))
     mm = [i for i in ordered if graph.ops[i].op_type == OpType.MATMUL]
     if not mm:
         fam = "row" if any(graph.is_reduction(i) for i in ordered) else "ew"
@@ -312,6 +339,10 @@ def split_group(graph: DataflowGraph, ordered: list) -> list:
         if users == [m] and graph.ops[m].inputs[0] != bt:
             absorbed = [bt]
             pre_set = pre_set - {bt}        # what bt reads is still computed first
+    # RMSNorm feeding A only: normalised inside the GEMM as A is staged
+    prologue = (rms_prologue(graph, m, members, set(outs)) or []) if fuse_prologue else []
+    pre_set = pre_set - set(prologue)
+    absorbed = absorbed + prologue
     pre = [i for i in ordered if i in pre_set]
     post = [i for i in ordered if i not in pre_set and i != m and i not in absorbed]
     post_set = set(post)

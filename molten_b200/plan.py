@@ -9,6 +9,7 @@ from .lowering import (
     DTYPE_SIZE, GroupPlan, LoweringError, Operand, OutputSpec, SubKernel,
     broadcast_shapes, build_dag, canon_dtype, choose_ew_config,
     choose_row_config, choose_row_tma_config, choose_rope_config, classify_operand,
+    rms_prologue,
     group_boundary, infer_shapes,
     is_mask_const, prod, promote, split_group, EXPENSIVE,
 )
@@ -71,7 +72,13 @@ def plan_group(graph: DataflowGraph, group_op_ids, input_shapes: dict,
     dts = {i: canon_dtype(input_dtypes[i]) for i in inputs}
     dts = _op_dtypes(graph, ordered, dts)
 
-    parts = split_group(graph, ordered)
+    # {"gemm": {"prologue": True}} runs RMSNorm -> GEMM as one GEMM that
+    # normalises A as it is staged; off by default: measured slower than the
+    # row kernel + GEMM pair (bf16 8192x4096x14336: 1308 vs 892 us; 64 rows:
+    # 64 vs 44 us) -- the in-place transform of every A stage competes with
+    # the tensor core for the same shared memory and lengthens each stage
+    parts = split_group(graph, ordered, outs,
+                        fuse_prologue=(tune.get("gemm") or {}).get("prologue", False))
     # intermediates between the sub-kernels of one group are stored in fp32,
     # so a split group still rounds once (at its outputs); a MATMUL operand
     # keeps its 16-bit type because the tensor cores read it
@@ -280,6 +287,16 @@ def _plan_rope(graph, ops, outs, shapes, dts, tune) -> SubKernel:
 def _plan_gemm(graph, ops, ext, outs, shapes, dts, tune) -> SubKernel:
     mm = ops[0]
     a_id, b_id = graph.ops[mm].inputs
+    # RMSNorm prologue: A = x / RMS(x) * w, computed as the GEMM stages x
+    pro = rms_prologue(graph, mm, set(ops), set(outs))
+    prologue = None
+    if pro is not None and all(o in ops for o in pro):
+        r_id, d_id, mul_id = pro
+        x_id = graph.ops[d_id].inputs[0]
+        w_id = [i for i in graph.ops[mul_id].inputs if i != d_id][0]
+        prologue = {"eps": float(graph.ops[r_id].attrs.get("eps", 1e-6)), "w_op": w_id}
+        a_id = x_id
+        ops = [o for o in ops if o not in pro]
     # B given as TRANSPOSE(Bt) with Bt [N, K]: read K-major, no copy
     b_kmajor = graph.ops[b_id].op_type == OpType.TRANSPOSE and b_id in ops
     if b_kmajor:
@@ -305,6 +322,9 @@ def _plan_gemm(graph, ops, ext, outs, shapes, dts, tune) -> SubKernel:
             continue
         if j in (a_id, b_id) and not any(j in graph.ops[o].inputs for o in ops[1:]):
             last, row_map, terms = "vec", "full", ()
+        elif prologue is not None and j == prologue["w_op"] \
+                and not any(j in graph.ops[o].inputs for o in ops[1:]):
+            last, row_map, terms = "vec", "zero", ()        # per-K weight of the prologue
         else:
             last, row_map, terms = classify_operand(shapes[j], it)
         operands.append(Operand(index=len(operands), op_id=j, name=src.name or f"op{j}",
@@ -318,6 +338,13 @@ def _plan_gemm(graph, ops, ext, outs, shapes, dts, tune) -> SubKernel:
         b_idx = a_idx
     if dts[a_id] != dts[b_id] or dts[a_id] == "float32":
         raise LoweringError("the tensor-core GEMM takes bf16 x bf16 or fp16 x fp16 operands")
+    if prologue is not None:
+        w_id = prologue["w_op"]
+        w_shape = tuple(int(v) for v in shapes[w_id])
+        if prod(w_shape) != K or w_shape[-1] != K or graph.ops[w_id].op_type == OpType.CONSTANT:
+            raise LoweringError("the RMSNorm prologue needs a weight vector of length K")
+        prologue["w"] = [o.index for o in operands if o.op_id == w_id][0]
+        prologue["w_dtype"] = dts[w_id]
     outputs = []
     for o in outs:
         s = shapes[o]
@@ -338,5 +365,11 @@ def _plan_gemm(graph, ops, ext, outs, shapes, dts, tune) -> SubKernel:
     from .gemm_config import choose_gemm_config
     sk.config = choose_gemm_config(sk, tune.get("gemm") or {})
     sk.config["b_kmajor"] = bool(b_kmajor)
+    if prologue is not None:
+        sk.config["prologue"] = {"kind": "rmsnorm", "eps": prologue["eps"], "w": prologue["w"],
+                                 "w_dtype": prologue["w_dtype"]}
+        sk.config["threads"] = 512
+        # GemmLayout<..., PRO>: ready[S], rms_full[2], rms_empty[2], 1/rms [2][BM]
+        sk.config["smem_bytes"] += (sk.config["stages"] + 4) * 8 + 2 * sk.config["bm"] * 4
     sk.config["needed"] = sorted(needed)
     return sk

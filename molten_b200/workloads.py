@@ -11,6 +11,8 @@ softmax                    logits ~ N(0, 3^2), [32*2048, 2048] (as
                            [32, 2048, 2048]) or [4096, 32768]; fp32 / bf16;
                            optional causal mask
 chain                      x, r bf16 [16384, 8192] ~ N(0,1); a, b, s ~ U(-1,1)
+rmsnorm_gemm               x bf16 [8192, 4096] ~ N(0,1), w = 1 + 0.1 N(0,1), then
+                           B and bias as gemm_bias_gelu (GELU(rmsnorm(x, w) @ B + bias))
 gemm_bias_gelu             A bf16 [8192, 4096] ~ N(0,1); B [4096, 14336] ~
                            N(0, 1/4096); bias [14336] ~ N(0, 0.02^2)
 =========================  ==============================================
@@ -100,6 +102,14 @@ WORKLOADS = {w.name: w for w in [
     Workload("chain_bf16_16384x8192", "chain", {"rows": 16384, "cols": 8192}, "bfloat16",
              3 * 16384 * 8192 * 2 + 3 * 8192 * 2, 0, ["x", "r", "a", "b", "s"]),
     _rope("rope_bf16_4x4096x32x128", 4, 4096, 32, 128, "bfloat16"),
+    Workload("rmsnorm_gemm_bf16_64x4096x14336", "rmsnorm_gemm",
+             {"m": 64, "k": 4096, "n": 14336}, "bfloat16",
+             (64 * 4096 + 4096 + 4096 * 14336 + 14336 + 64 * 14336) * 2,
+             2 * 64 * 4096 * 14336, ["x", "w", "B", "bias"]),
+    Workload("rmsnorm_gemm_bf16_8192x4096x14336", "rmsnorm_gemm",
+             {"m": 8192, "k": 4096, "n": 14336}, "bfloat16",
+             (8192 * 4096 + 4096 + 4096 * 14336 + 14336 + 8192 * 14336) * 2,
+             2 * 8192 * 4096 * 14336, ["x", "w", "B", "bias"]),
     Workload("gemm_bias_gelu_bf16_8192x4096x14336", "gemm_bias_gelu",
              {"m": 8192, "k": 4096, "n": 14336}, "bfloat16",
              (8192 * 4096 + 4096 * 14336 + 14336 + 8192 * 14336) * 2,
@@ -124,6 +134,9 @@ def scaled(w: Workload, **params) -> Workload:
     if w.kind == "rope":
         return _rope(w.name + "_scaled", p["batch"], p["seq"], p["heads"], p["head_dim"], w.dtype)
     m, k, n = p["m"], p["k"], p["n"]
+    if w.kind == "rmsnorm_gemm":
+        return Workload(w.name + "_scaled", "rmsnorm_gemm", {"m": m, "k": k, "n": n}, w.dtype,
+                        (m * k + k + k * n + n + m * n) * 2, 2 * m * k * n, list(w.input_names))
     return Workload(w.name + "_scaled", "gemm_bias_gelu", {"m": m, "k": k, "n": n}, w.dtype,
                     (m * k + k * n + n + m * n) * 2, 2 * m * k * n, list(w.input_names))
 
@@ -172,6 +185,13 @@ def make_inputs(w: Workload, seed: int = 0, device="cpu") -> list:
         ang = torch.rand(p["seq"], p["head_dim"] // 2, generator=g, device=dev,
                          dtype=torch.float32) * 6.283185307179586
         return [x, torch.cos(ang), torch.sin(ang)]
+    if w.kind == "rmsnorm_gemm":
+        m, k, n = p["m"], p["k"], p["n"]
+        x = normal((m, k))
+        wt = normal((k,), 1.0, 0.1)
+        B = normal((k, n), 0.0, (1.0 / k) ** 0.5)
+        bias = normal((n,), 0.0, 0.02)
+        return [x, wt, B, bias]
     if w.kind == "gemm_bias_gelu":
         m, k, n = p["m"], p["k"], p["n"]
         A = normal((m, k))
@@ -195,6 +215,8 @@ def input_shapes(w: Workload) -> list:
         return [(r, c), (r, c), (c,), (c,), (c,)]
     if w.kind == "gemm_bias_gelu":
         return [(p["m"], p["k"]), (p["k"], p["n"]), (p["n"],)]
+    if w.kind == "rmsnorm_gemm":
+        return [(p["m"], p["k"]), (p["k"],), (p["k"], p["n"]), (p["n"],)]
     if w.kind == "rope":
         half = (p["seq"], p["head_dim"] // 2)
         return [(p["batch"], p["seq"], p["heads"], p["head_dim"]), half, half]
@@ -207,3 +229,6 @@ def input_dtypes(w: Workload) -> list:
     if w.kind == "rope":
         return [w.dtype, "float32", "float32"]
     return [w.dtype] * n
+
+
+GEMM_KINDS = ("gemm_bias_gelu", "rmsnorm_gemm")

@@ -14,6 +14,7 @@ caller's tensors, in their dtype, on the host's cores.
 * chain              the 8-op chain composed from the ops above
 * gemm_bias_gelu     torch.matmul as benchmarks/ops.py:58, + bias, GELU
 * rope               benchmarks/ops.py:24-35
+* rmsnorm_gemm       rmsnorm, then gemm_bias_gelu
 """
 
 from __future__ import annotations
@@ -74,6 +75,10 @@ def rope(x, cos, sin):
     return out.to(x.dtype)
 
 
+def rmsnorm_gemm(x, w, B, bias, eps=1e-6):
+    return gemm_bias_gelu(rmsnorm(x, w, eps), B, bias)
+
+
 def run_workload(kind: str, tensors, params: dict):
     """Evaluate a named workload kind on CPU tensors."""
     if kind == "rmsnorm":
@@ -88,4 +93,6 @@ def run_workload(kind: str, tensors, params: dict):
         return gemm_bias_gelu(*tensors)
     if kind == "rope":
         return rope(*tensors)
+    if kind == "rmsnorm_gemm":
+        return rmsnorm_gemm(*tensors)
     raise KeyError(kind)

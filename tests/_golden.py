@@ -71,13 +71,25 @@ def bf16_ulp_diff(a_bits, b_bits):
     return np.abs(a - b)
 
 
-def assert_close(out_f32, ref_f32, dtype, what=""):
+def rounded_operand_bound(a_f32, b_f32, dtype, slope=1.0):
+    """Extra tolerance for a GEMM whose A operand is computed (not a graph
+    input): the tensor cores take A rounded once to ``dtype``, which moves
+    each output by at most u * sum_k |a_k| |b_kn| (u = 2^-8 for bf16, 2^-11
+    for fp16; Higham's first-order bound for perturbing every a_k by a
+    relative u), times ``slope`` >= max |f'| of an elementwise epilogue f."""
+    u = 2.0 ** -8 if dtype == "bfloat16" else 2.0 ** -11
+    return slope * u * (np.abs(a_f32.astype(np.float64)) @ np.abs(b_f32.astype(np.float64)))
+
+
+def assert_close(out_f32, ref_f32, dtype, what="", extra_abs=None):
     """The parity bar of this project.
 
     fp32:        |out - ref| <= 1e-5 |ref| + 1e-6 * max|ref|
     bf16 / fp16: |out - ref| <= 1e-2 |ref| + 1e-3 * rms(ref)
     (ref is the fp32-accumulated reference; the absolute term only covers
     values that cancel to near zero, e.g. y*0.5 + r or GELU at large -v).
+    ``extra_abs`` (same shape as ref) adds a per-element bound, e.g.
+    ``rounded_operand_bound`` for a GEMM fed by a computed operand.
     """
     out_f32 = np.asarray(out_f32, dtype=np.float32)
     ref_f32 = np.asarray(ref_f32, dtype=np.float32)
@@ -92,6 +104,8 @@ def assert_close(out_f32, ref_f32, dtype, what=""):
         tol = 1e-5 * np.abs(r) + 1e-6 * np.abs(r).max()
     else:
         tol = 1e-2 * np.abs(r) + 1e-3 * np.sqrt(np.mean(r * r))
+    if extra_abs is not None:
+        tol = tol + np.broadcast_to(np.asarray(extra_abs, np.float64), ref_f32.shape)[fin]
     err = np.abs(o - r)
     bad = err > tol
     assert not bad.any(), (f"{what}: {int(bad.sum())}/{bad.size} outside tolerance; "

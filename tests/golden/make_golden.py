@@ -275,6 +275,15 @@ def make_fusion(ir, fusion, compiler):
     g.add_output(g.softmax(g.matmul(q, k)))
     cases["transformer_block"] = groups(g)
 
+    # RMSNorm feeding a GEMM with a bias + GELU epilogue
+    g = DG("norm_gemm")
+    x = g.add_input("x", TS([256, 512]))
+    w = g.add_input("w", TS([512]))
+    B = g.add_input("B", TS([512, 384]))
+    bias = g.add_input("bias", TS([384]))
+    g.add_output(g.add_op(OT.GELU, [g.add(g.matmul(g.rms_norm(x, w, "norm"), B), bias)]))
+    cases["norm_gemm"] = groups(g)
+
     # attention scores, ops.py:55-59: softmax(Q @ K^T * scale)
     g = DG("attention_score")
     q = g.add_input("q", TS([256, 128]))

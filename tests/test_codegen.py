@@ -200,7 +200,7 @@ def test_attention_score_plan(tmp_path):
     gemm, row = k.plan.kernels
     assert gemm.family == "gemm" and gemm.config["b_kmajor"] and (gemm.m, gemm.n, gemm.k) == (256, 512, 128)
     assert row.family == "row"
-    assert ", true>(sh, args)" in k.source
+    assert ", true, NoPrologue>(sh, args)" in k.source
     assert build_cubin(k.source, k.name, tmp_path).stat().st_size > 1000
 
 

@@ -122,6 +122,13 @@ def _reference_graphs():
     k = g.add_input("k", TS([512, 4]))
     g.add_output(g.softmax(g.matmul(q, k)))
     out["transformer_block"] = g
+    g = DataflowGraph("norm_gemm")
+    x = g.add_input("x", TS([256, 512]))
+    w = g.add_input("w", TS([512]))
+    B = g.add_input("B", TS([512, 384]))
+    bias = g.add_input("bias", TS([384]))
+    g.add_output(g.add_op(OpType.GELU, [g.add(g.matmul(g.rms_norm(x, w, "norm"), B), bias)]))
+    out["norm_gemm"] = g
     g = DataflowGraph("attention_score")
     q = g.add_input("q", TS([256, 128]))
     k = g.add_input("k", TS([512, 128]))

@@ -20,9 +20,10 @@ torch = pytest.importorskip("torch")
 
 from molten_b200 import graphs, workloads
 from molten_b200.codegen import compile_graph
+from molten_b200.fusion import FusionEngine
 from molten_b200.runtime import MoltenRuntime
 from oracle import graph_oracle as orc
-from tests._golden import CASES, assert_close, graph_for, load
+from tests._golden import CASES, assert_close, graph_for, load, rounded_operand_bound
 
 pytestmark = pytest.mark.gpu
 
@@ -472,6 +473,81 @@ def test_gemm_with_transposed_b(rt):
     assert MoltenRuntime.read_status(0) == 0
     res = orc.evaluate(g, {"A": to_numpy(A), "Bt": to_numpy(Bt), "bias": to_numpy(bb)})
     assert_close(as_f32(out), res[("f32", g.ops[g._outputs[0]].inputs[0])], "bfloat16", "gemm Bt")
+
+
+def _norm_gemm_graph(m, k, n, dt, wdt, norm_out=False):
+    from molten_b200.ir import DataflowGraph, TensorShape as TS
+    g = DataflowGraph("norm_gemm")
+    x = g.add_input("x", TS([m, k]), dtype=dt)
+    w = g.add_input("w", TS([k]), dtype=wdt)
+    B = g.add_input("B", TS([k, n]), dtype=dt)
+    bias = g.add_input("bias", TS([n]), dtype=dt)
+    normed = g.rms_norm(x, w, "norm")
+    g.add_output(g.gelu(g.add(g.matmul(normed, B), bias)))
+    if norm_out:
+        g.add_output(normed)
+    return g
+
+
+def _normed(xs):
+    """fp32 x / sqrt(mean(x^2) + 1e-6) * w, the GEMM's computed A operand
+    (1.13 bounds |GELU'| for the bias + GELU epilogue)."""
+    x, w = as_f32(xs[0]).astype(np.float64), as_f32(xs[1]).astype(np.float64)
+    return (x / np.sqrt(np.mean(x * x, axis=-1, keepdims=True) + 1e-6) * w).astype(np.float32)
+
+
+def _norm_gemm_inputs(m, k, n, dt, wdt, seed):
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(seed)
+    x = torch.randn(m, k, generator=gen, device=DEV).to(TORCH_DT[dt])
+    w = (1 + 0.1 * torch.randn(k, generator=gen, device=DEV)).to(TORCH_DT[wdt])
+    B = (torch.randn(k, n, generator=gen, device=DEV) / k ** 0.5).to(TORCH_DT[dt])
+    bias = (0.02 * torch.randn(n, generator=gen, device=DEV)).to(TORCH_DT[dt])
+    return [x, w, B, bias]
+
+
+@pytest.mark.parametrize("m,k,n,dt,wdt", [(256, 512, 384, "bfloat16", "bfloat16"),
+                                          (300, 520, 136, "bfloat16", "float32"),
+                                          (64, 4096, 1024, "float16", "float16"),
+                                          (1, 3584, 512, "bfloat16", "bfloat16")])
+def test_rmsnorm_gemm_prologue(rt, m, k, n, dt, wdt):
+    """RMSNorm -> GEMM (+ bias + GELU), one fusion group as the reference
+    groups it, run (opt-in) as ONE tcgen05 GEMM that normalises A as it is
+    staged (x * w in shared memory, 1/rms on the accumulator rows)."""
+    g = _norm_gemm_graph(m, k, n, dt, wdt)
+    xs = _norm_gemm_inputs(m, k, n, dt, wdt, seed=m + k + n)
+    rt = MoltenRuntime(tune={"gemm": {"prologue": True}})
+    from molten_b200.codegen import CodeGenerator
+    ck = rt.compile(CodeGenerator(dtype=dt, tune=rt.tune).generate(g, FusionEngine().fuse(g)[0]))
+    out = ck(*xs)
+    torch.cuda.synchronize()
+    assert MoltenRuntime.read_status(0) == 0
+    (sk,) = ck.specialization(*xs).plan.kernels
+    assert sk.family == "gemm" and sk.config["prologue"]["kind"] == "rmsnorm"
+    res = orc.evaluate(g, {"x": to_numpy(xs[0]), "w": to_numpy(xs[1]), "B": to_numpy(xs[2]),
+                           "bias": to_numpy(xs[3])})
+    assert_close(as_f32(out), res[("f32", g.ops[g._outputs[0]].inputs[0])], dt,
+                 f"rmsnorm->gemm {m}x{k}x{n} {dt}/{wdt}",
+                 extra_abs=rounded_operand_bound(_normed(xs), as_f32(xs[2]), dt, slope=1.13))
+
+
+def test_rmsnorm_gemm_unfused_when_the_norm_is_an_output(rt):
+    g = _norm_gemm_graph(128, 512, 256, "bfloat16", "bfloat16", norm_out=True)
+    xs = _norm_gemm_inputs(128, 512, 256, "bfloat16", "bfloat16", seed=5)
+    # the normalised x is also an output: two kernels even with the prologue on
+    from molten_b200.codegen import CodeGenerator
+    kern = CodeGenerator(dtype="bfloat16", tune={"gemm": {"prologue": True}}).generate(
+        g, FusionEngine().fuse(g)[0])
+    assert [sk.family for sk in kern.plan.kernels] == ["row", "gemm"]
+    assert "prologue" not in kern.plan.kernels[1].config
+    outs = dict(zip(kern.plan.outputs, rt.compile(kern)(*xs)))   # by producing op id
+    y, normed = (outs[g.ops[o].inputs[0]] for o in g._outputs)
+    torch.cuda.synchronize()
+    res = orc.evaluate(g, {"x": to_numpy(xs[0]), "w": to_numpy(xs[1]), "B": to_numpy(xs[2]),
+                           "bias": to_numpy(xs[3])})
+    assert_close(as_f32(y), res[("f32", g.ops[g._outputs[0]].inputs[0])], "bfloat16", "gemm",
+                 extra_abs=rounded_operand_bound(_normed(xs), as_f32(xs[2]), "bfloat16", slope=1.13))
+    assert_close(as_f32(normed), res[("f32", g.ops[g._outputs[1]].inputs[0])], "bfloat16", "norm")
 
 
 def test_misaligned_pointers_take_the_scalar_path(rt):
