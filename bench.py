@@ -145,6 +145,9 @@ def cpu_sample(w, fraction_rows=None):
         p["shape"] = (rows, cols)
     elif w.kind in workloads.GEMM_KINDS:
         p["m"] = min(p["m"], fraction_rows or 256)
+    elif w.kind == "attention_score":
+        p["heads"] = 1
+        p["m"] = min(p["m"], fraction_rows or 256)
     elif w.kind == "rope":
         p["batch"] = 1
         p["seq"] = max(1, min(p["seq"], (fraction_rows or 1024) // max(1, p["heads"] // 8)))

@@ -74,10 +74,10 @@ typedef struct molten_gemm_args {
   MOLTEN_ALIGN64 unsigned char tmap_b[128];
   const void* in[MOLTEN_MAX_IO];
   void* out[MOLTEN_MAX_IO];
-  long long m, n, k;
+  long long m, n, k;             /* one problem: C[m, n] = A[m, k] B[k, n] */
   long long row_offset;
   int* status;
-  int pad_;
+  int batch;                     /* stacked independent problems (0 or 1: one) */
 } molten_gemm_args;
 
 /* Version of this ABI (major * 100 + minor). */

@@ -64,7 +64,7 @@ class GemmArgs(ctypes.Structure):
                 ("inp", ctypes.c_void_p * MAX_IO), ("out", ctypes.c_void_p * MAX_IO),
                 ("m", ctypes.c_longlong), ("n", ctypes.c_longlong), ("k", ctypes.c_longlong),
                 ("row_offset", ctypes.c_longlong), ("status", ctypes.c_void_p),
-                ("pad_", ctypes.c_int), ("tail_", ctypes.c_ubyte * 20)]
+                ("batch", ctypes.c_int), ("tail_", ctypes.c_ubyte * 20)]
 
 
 assert ctypes.sizeof(RowArgs) == 160

@@ -31,10 +31,10 @@ struct alignas(64) GemmArgs {
   CUtensorMap tmap_b;              // B [K, N], box {64, BK}; or Bt [N, K], box {64, BN}
   const void* in[8];               // epilogue operands (kernel order)
   void* out[8];                    // outputs
-  long long m, n, k;
+  long long m, n, k;               // one problem: C[m, n] = A[m, k] B[k, n]
   long long row_offset;            // global row of local row 0
   int* status;                     // error bits (may be null)
-  int pad_;
+  int batch;                       // stacked independent problems (0 or 1: one)
 };
 
 enum GemmStatus { kGemmTimeoutFull = 1, kGemmTimeoutEmpty = 2, kGemmTimeoutAcc = 4,
@@ -215,7 +215,10 @@ __device__ __forceinline__ int gemm_tid() { return threadIdx.y * blockDim.x + th
 // stay in L2 instead of being re-read from HBM on every wave.
 template <class L>
 __device__ __forceinline__ void gemm_tile_coords(long long tile, long long MB, long long NB,
-                                                 int& m0, int& n0) {
+                                                 int& m0, int& n0, int& h) {
+  // problem h of a batch: its MB x NB tiles are consecutive
+  h = (int)(tile / (MB * NB));
+  tile -= (long long)h * MB * NB;
   const long long G = L::GROUP_M;
   const long long span = G * NB;                       // tiles of a full group
   const long long g = tile / span;
@@ -271,7 +274,8 @@ __device__ __forceinline__ void gemm_init(const GemmShared& s, const GemmArgs& a
   tc_fence_before();
 }
 
-// The three roles.  Epi::apply(args, row, col0, acc[32]) writes C[row, col0..col0+31].
+// The three roles.  Epi::apply(args, row, col0, acc[32]) writes C[row, col0..col0+31]
+// (row of the stacked C, always a valid row; columns from col0 < n).
 // B_KMAJOR: tmap_b describes Bt [N, K] (inner K) with box {64, BN}; a stage
 // holds BN rows of 128 bytes, the same 128-byte-swizzled K-major layout as A.
 // Pro (ENABLED): C = diag(1/rms(x)) ((x * w) B) for A = rmsnorm(x, w) with
@@ -291,8 +295,13 @@ __device__ __forceinline__ void gemm_roles(const GemmShared& s, const GemmArgs& 
   const Bars<L> bar(s);
   const long long MB = (args.m + L::BM - 1) / L::BM;
   const long long NB = (args.n + L::BN - 1) / L::BN;
-  const long long T = MB * NB;
+  const long long T = (args.batch > 1 ? args.batch : 1) * MB * NB;
   const int KB = (int)((args.k + L::BK - 1) / L::BK);
+  // Batched problems are stacked: A [batch*m, k], B [batch*k, n] (or
+  // Bt [batch*n, k]), C [batch*m, n].  A tile of problem h that runs past its
+  // m rows (or n columns) reads the next problem's rows; those products land
+  // in rows / columns the epilogue never stores.  Past k, A is zero-filled
+  // (its columns end at k), so whatever B rows sit there multiply zeros.
 
   if (warp == 0) {
     // ------------------------------------------------------- TMA producer
@@ -300,22 +309,23 @@ __device__ __forceinline__ void gemm_roles(const GemmShared& s, const GemmArgs& 
       uint32_t st = 0, ph = 0;
       long long issued = 0;
       for (long long tile = blockIdx.x; tile < T && !*s.abort_flag; tile += gridDim.x) {
-        int m0, n0;
-        gemm_tile_coords<L>(tile, MB, NB, m0, n0);
+        int m0, n0, h;
+        gemm_tile_coords<L>(tile, MB, NB, m0, n0, h);
+        const int a_row = (int)(h * args.m) + m0;
         for (int kb = 0; kb < KB; ++kb) {
           if (!mbar_wait(bar.empty(st), ph ^ 1u)) { gemm_fail(s, args, kGemmTimeoutEmpty); break; }
           if (*s.abort_flag) break;
           const uint32_t a_dst = smem_u32(s.tiles + st * L::STAGE_BYTES);
           const uint32_t b_dst = a_dst + L::A_BYTES;
           mbar_expect_tx(bar.full(st), (uint32_t)L::STAGE_BYTES);
-          tma_load_2d(a_dst, &args.tmap_a, bar.full(st), kb * L::BK, m0);
+          tma_load_2d(a_dst, &args.tmap_a, bar.full(st), kb * L::BK, a_row);
           if constexpr (B_KMAJOR) {
-            tma_load_2d(b_dst, &args.tmap_b, bar.full(st), kb * L::BK, n0);
+            tma_load_2d(b_dst, &args.tmap_b, bar.full(st), kb * L::BK, (int)(h * args.n) + n0);
           } else {
 #pragma unroll
             for (int c = 0; c < L::BN / 64; ++c)
               tma_load_2d(b_dst + c * L::B_CHUNK_BYTES, &args.tmap_b, bar.full(st), n0 + 64 * c,
-                          kb * L::BK);
+                          (int)(h * args.k) + kb * L::BK);
           }
           ++issued;
           if (++st == (uint32_t)L::STAGES) { st = 0; ph ^= 1u; }
@@ -445,9 +455,10 @@ __device__ __forceinline__ void gemm_roles(const GemmShared& s, const GemmArgs& 
         break;
       }
       tc_fence_after();
-      int m0, n0;
-      gemm_tile_coords<L>(tile, MB, NB, m0, n0);
-      const long long row = (long long)m0 + quarter * 32 + lane;
+      int m0, n0, h;
+      gemm_tile_coords<L>(tile, MB, NB, m0, n0, h);
+      const long long mrow = (long long)m0 + quarter * 32 + lane;   // row of problem h
+      const long long row = (long long)h * args.m + mrow;           // row of stacked C
       const long long nbase = n0;
       float rinv = 1.0f;
       if constexpr (Pro::ENABLED) {
@@ -469,7 +480,7 @@ __device__ __forceinline__ void gemm_roles(const GemmShared& s, const GemmArgs& 
           for (int q = 0; q < 32; ++q) acc[q] *= rinv;
         }
         const long long col0 = nbase + 32 * c;
-        if (col0 < args.n) Epi::apply(args, row, col0, acc);
+        if (col0 < args.n && mrow < args.m) Epi::apply(args, row, col0, acc);
       }
       tc_fence_before();
       __syncwarp();

@@ -61,7 +61,6 @@ def emit_gemm(sk: SubKernel, name: str) -> str:
     w("  __device__ __forceinline__ static void apply(const GemmArgs& args, long long row,")
     w("                                               long long col0, const float (&acc)[32]) {")
     w(f"    constexpr long long N = {sk.n}LL;")
-    w("    if (row >= args.m) return;")
     w("    const long long grow = args.row_offset + row;")
     w("    (void)grow;")
     # row-level leaves

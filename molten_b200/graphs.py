@@ -104,12 +104,15 @@ def rope(batch=1, seq=4096, heads=32, head_dim=128, dtype="bfloat16", table_dtyp
 BUILDERS["rope"] = rope
 
 
-def attention_score(m=2048, n=2048, d=128, dtype="bfloat16", scale=None) -> DataflowGraph:
-    """softmax(Q @ K^T * scale) with Q [m, d], K [n, d] (``ops.py:55-59``);
-    scale defaults to 1/sqrt(d)."""
+def attention_score(m=2048, n=2048, d=128, dtype="bfloat16", scale=None,
+                    heads=None) -> DataflowGraph:
+    """softmax(Q @ K^T * scale) with Q [m, d], K [n, d] -- or [heads, m, d],
+    [heads, n, d], one problem per head (``ops.py:55-59``); scale defaults
+    to 1/sqrt(d)."""
     g = DataflowGraph("attention_score")
-    q = g.add_input("q", TensorShape([m, d]), dtype=dtype)
-    k = g.add_input("k", TensorShape([n, d]), dtype=dtype)
+    lead = [heads] if heads else []
+    q = g.add_input("q", TensorShape(lead + [m, d]), dtype=dtype)
+    k = g.add_input("k", TensorShape(lead + [n, d]), dtype=dtype)
     s = g.add_constant("scale", float(scale if scale is not None else d ** -0.5))
     g.add_output(g.softmax(g.mul(g.matmul(q, g.transpose(k, "kT"), "scores"), s), -1, "probs"))
     return g

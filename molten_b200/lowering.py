@@ -123,11 +123,13 @@ def infer_shapes(graph: DataflowGraph, op_ids, known: dict) -> dict:
             s = tuple(ins[0][:-2]) + (ins[0][-1], ins[0][-2])
         elif t == OpType.MATMUL:
             a, b = ins
-            if len(b) != 2 or len(a) < 2:
-                raise LoweringError("MATMUL needs A [..., M, K] and a 2-D B [K, N]")
-            if a[-1] != b[0]:
+            if len(b) < 2 or len(a) < 2:
+                raise LoweringError("MATMUL needs A [..., M, K] and B [K, N] or [..., K, N]")
+            if len(b) > 2 and tuple(a[:-2]) != tuple(b[:-2]):
+                raise LoweringError(f"batched MATMUL needs equal batch dims: {a} @ {b}")
+            if a[-1] != b[-2]:
                 raise LoweringError(f"MATMUL inner dims differ: {a} @ {b}")
-            s = tuple(a[:-1]) + (b[1],)
+            s = tuple(a[:-1]) + (b[-1],)
         else:
             raise LoweringError(f"{t.name} has no sm_100a lowering")
         shapes[oid] = tuple(int(d) for d in s)

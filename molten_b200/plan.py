@@ -303,16 +303,20 @@ def _plan_gemm(graph, ops, ext, outs, shapes, dts, tune) -> SubKernel:
         if b_id in outs:
             raise LoweringError("a transposed GEMM operand cannot also be an output")
         b_id = graph.ops[b_id].inputs[0]
-        if len(shapes[b_id]) != 2:
-            raise LoweringError("the transposed GEMM operand must be a matrix [N, K]")
         ops = [o for o in ops if graph.ops[o].op_type != OpType.TRANSPOSE]
     a_shape, b_shape = shapes[a_id], shapes[b_id]
-    K, N = (int(b_shape[1]), int(b_shape[0])) if b_kmajor else (int(b_shape[0]), int(b_shape[1]))
-    M = prod(a_shape[:-1])
+    K, N = (int(b_shape[-1]), int(b_shape[-2])) if b_kmajor else (int(b_shape[-2]), int(b_shape[-1]))
+    # B with leading dims: a batch of independent problems stacked in memory
+    batch = prod(b_shape[:-2]) if len(b_shape) > 2 else 1
+    M = int(a_shape[-2]) if batch > 1 else prod(a_shape[:-1])
+    if batch > 1 and prologue is not None:
+        raise LoweringError("the RMSNorm prologue takes an unbatched B")
+    if max(batch * M, batch * K, batch * N) >= 2 ** 31:
+        raise LoweringError("GEMM rows beyond the 32-bit TMA coordinate range")
     it = shapes[mm]
     for o in ops:
         it = broadcast_shapes(it, shapes[o])
-    if prod(it[:-1]) != M or it[-1] != N:
+    if prod(it[:-1]) != batch * M or it[-1] != N:
         raise LoweringError("the GEMM epilogue broadcasts beyond the product shape")
     operands = []
     a_idx = b_idx = None
@@ -363,8 +367,9 @@ def _plan_gemm(graph, ops, ext, outs, shapes, dts, tune) -> SubKernel:
     if any(values[v].avail for v in needed):
         raise LoweringError("GEMM epilogues are elementwise only")
     from .gemm_config import choose_gemm_config
-    sk.config = choose_gemm_config(sk, tune.get("gemm") or {})
+    sk.config = choose_gemm_config(sk, tune.get("gemm") or {}, batch=batch)
     sk.config["b_kmajor"] = bool(b_kmajor)
+    sk.config["batch"] = int(batch)
     if prologue is not None:
         sk.config["prologue"] = {"kind": "rmsnorm", "eps": prologue["eps"], "w": prologue["w"],
                                  "w_dtype": prologue["w_dtype"]}

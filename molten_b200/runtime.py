@@ -134,7 +134,7 @@ class _Spec:
         else:
             torch = _torch()
             sms = torch.cuda.get_device_properties(device).multi_processor_count
-            tiles = (-(-sk.m // c["bm"])) * (-(-sk.n // c["bn"]))
+            tiles = c.get("batch", 1) * (-(-sk.m // c["bm"])) * (-(-sk.n // c["bn"]))
             cfg.grid[:] = [max(1, min(tiles, sms)), 1, 1]
             cfg.block[:] = [128, c["threads"] // 128, 1]
             cfg.cluster[:] = [1, 1, 1]
@@ -179,14 +179,19 @@ class _Spec:
                 A = env[sk.operands[sk.a_operand].op_id]
                 B = env[sk.operands[sk.b_operand].op_id]
                 dt = sk.operands[sk.a_operand].dtype
+                nb = sk.config.get("batch", 1)
                 A2 = A.reshape(-1, A.shape[-1])
-                ctypes.memmove(a.tmap_a, self.tmap(A2, dt, sk.m, sk.k, 64, 128), 128)
+                ctypes.memmove(a.tmap_a, self.tmap(A2, dt, nb * sk.m, sk.k, 64, 128), 128)
                 if sk.config.get("b_kmajor"):
-                    # B is the transpose of Bt [N, K]: its rows, K-major
-                    ctypes.memmove(a.tmap_b, self.tmap(B, dt, sk.n, sk.k, 64, sk.config["bn"]), 128)
+                    # B is the transpose of Bt [(batch x) N, K]: its rows, K-major
+                    B2 = B.reshape(-1, B.shape[-1])
+                    ctypes.memmove(a.tmap_b, self.tmap(B2, dt, nb * sk.n, sk.k, 64, sk.config["bn"]),
+                                   128)
                 else:
-                    ctypes.memmove(a.tmap_b, self.tmap(B, dt, sk.k, sk.n, 64, 64), 128)
+                    B2 = B.reshape(-1, B.shape[-1])
+                    ctypes.memmove(a.tmap_b, self.tmap(B2, dt, nb * sk.k, sk.n, 64, 64), 128)
                 a.m, a.n, a.k = sk.m, sk.n, sk.k
+                a.batch = nb
                 a.status = _capi.status_word(di)
             else:
                 a = _capi.RowArgs()

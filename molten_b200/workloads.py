@@ -11,6 +11,7 @@ softmax                    logits ~ N(0, 3^2), [32*2048, 2048] (as
                            [32, 2048, 2048]) or [4096, 32768]; fp32 / bf16;
                            optional causal mask
 chain                      x, r bf16 [16384, 8192] ~ N(0,1); a, b, s ~ U(-1,1)
+attention_score            q, k bf16 [32 heads, 2048, 128] ~ N(0,1); scale 1/sqrt(128)
 rmsnorm_gemm               x bf16 [8192, 4096] ~ N(0,1), w = 1 + 0.1 N(0,1), then
                            B and bias as gemm_bias_gelu (GELU(rmsnorm(x, w) @ B + bias))
 gemm_bias_gelu             A bf16 [8192, 4096] ~ N(0,1); B [4096, 14336] ~
@@ -102,6 +103,10 @@ WORKLOADS = {w.name: w for w in [
     Workload("chain_bf16_16384x8192", "chain", {"rows": 16384, "cols": 8192}, "bfloat16",
              3 * 16384 * 8192 * 2 + 3 * 8192 * 2, 0, ["x", "r", "a", "b", "s"]),
     _rope("rope_bf16_4x4096x32x128", 4, 4096, 32, 128, "bfloat16"),
+    Workload("attention_score_bf16_32x2048x2048x128", "attention_score",
+             {"heads": 32, "m": 2048, "n": 2048, "d": 128}, "bfloat16",
+             (2 * 32 * 2048 * 128 + 32 * 2048 * 2048) * 2, 2 * 32 * 2048 * 2048 * 128,
+             ["q", "k"]),
     Workload("rmsnorm_gemm_bf16_64x4096x14336", "rmsnorm_gemm",
              {"m": 64, "k": 4096, "n": 14336}, "bfloat16",
              (64 * 4096 + 4096 + 4096 * 14336 + 14336 + 64 * 14336) * 2,
@@ -133,6 +138,10 @@ def scaled(w: Workload, **params) -> Workload:
                         3 * r * c * 2 + 3 * c * 2, 0, list(w.input_names))
     if w.kind == "rope":
         return _rope(w.name + "_scaled", p["batch"], p["seq"], p["heads"], p["head_dim"], w.dtype)
+    if w.kind == "attention_score":
+        h, m, n, d = p["heads"], p["m"], p["n"], p["d"]
+        return Workload(w.name + "_scaled", "attention_score", dict(p), w.dtype,
+                        (h * m * d + h * n * d + h * m * n) * 2, 2 * h * m * n * d, ["q", "k"])
     m, k, n = p["m"], p["k"], p["n"]
     if w.kind == "rmsnorm_gemm":
         return Workload(w.name + "_scaled", "rmsnorm_gemm", {"m": m, "k": k, "n": n}, w.dtype,
@@ -180,6 +189,8 @@ def make_inputs(w: Workload, seed: int = 0, device="cpu") -> list:
         b = uniform((cols,), -1.0, 1.0)
         s = uniform((cols,), -1.0, 1.0)
         return [x, r, a, b, s]
+    if w.kind == "attention_score":
+        return [normal((p["heads"], p["m"], p["d"])), normal((p["heads"], p["n"], p["d"]))]
     if w.kind == "rope":
         x = normal((p["batch"], p["seq"], p["heads"], p["head_dim"]))
         ang = torch.rand(p["seq"], p["head_dim"] // 2, generator=g, device=dev,
@@ -217,6 +228,8 @@ def input_shapes(w: Workload) -> list:
         return [(p["m"], p["k"]), (p["k"], p["n"]), (p["n"],)]
     if w.kind == "rmsnorm_gemm":
         return [(p["m"], p["k"]), (p["k"],), (p["k"], p["n"]), (p["n"],)]
+    if w.kind == "attention_score":
+        return [(p["heads"], p["m"], p["d"]), (p["heads"], p["n"], p["d"])]
     if w.kind == "rope":
         half = (p["seq"], p["head_dim"] // 2)
         return [(p["batch"], p["seq"], p["heads"], p["head_dim"]), half, half]

@@ -15,6 +15,7 @@ caller's tensors, in their dtype, on the host's cores.
 * gemm_bias_gelu     torch.matmul as benchmarks/ops.py:58, + bias, GELU
 * rope               benchmarks/ops.py:24-35
 * rmsnorm_gemm       rmsnorm, then gemm_bias_gelu
+* attention_score    benchmarks/ops.py:55-59
 """
 
 from __future__ import annotations
@@ -79,6 +80,11 @@ def rmsnorm_gemm(x, w, B, bias, eps=1e-6):
     return gemm_bias_gelu(rmsnorm(x, w, eps), B, bias)
 
 
+def attention_score(q, k, scale):
+    """softmax(q @ k^T * scale) over the last dim (benchmarks/ops.py:55-59)."""
+    return F.softmax(torch.matmul(q, k.transpose(-2, -1)) * scale, dim=-1)
+
+
 def run_workload(kind: str, tensors, params: dict):
     """Evaluate a named workload kind on CPU tensors."""
     if kind == "rmsnorm":
@@ -95,4 +101,6 @@ def run_workload(kind: str, tensors, params: dict):
         return rope(*tensors)
     if kind == "rmsnorm_gemm":
         return rmsnorm_gemm(*tensors)
+    if kind == "attention_score":
+        return attention_score(*tensors, params["d"] ** -0.5)
     raise KeyError(kind)

@@ -98,6 +98,7 @@ FULL = [
     "softmax_bf16_4096x32768_causal",
     "chain_bf16_16384x8192",
     "rope_bf16_4x4096x32x128",
+    "attention_score_bf16_32x2048x2048x128",
 ]
 
 
@@ -141,6 +142,15 @@ def test_full_size_row_workloads(rt, name):
             r = np.arange(full.shape[0]) % cols
             masked = np.arange(cols)[None, :] > r[:, None]
             assert np.all(full[masked] == 0.0), "masked entries must be exactly 0"
+    elif w.kind == "attention_score":
+        # row r of the stacked scores: head r // m, query r % m
+        p = w.params
+        q, k = to_numpy(xs[0]), to_numpy(xs[1])
+        g1 = graphs.attention_score(1, p["n"], p["d"])
+        oid = g1.ops[g1._outputs[0]].inputs[0]
+        ref = np.concatenate([
+            orc.evaluate(g1, {"q": q[r // p["m"], r % p["m"]][None, :], "k": k[r // p["m"]]})[("f32", oid)]
+            for r in pick])
     elif w.kind == "rope":
         # each sampled row at its own position ((row // heads) % seq)
         p = w.params
@@ -450,6 +460,50 @@ def test_attention_score(rt, m, n, d, dtype):
     assert_close(as_f32(out), ref, dtype, f"attention {m}x{n}x{d} {dtype}")
     sums = as_f32(out).astype(np.float64).sum(axis=1)
     assert np.all(np.abs(sums - 1.0) < 2e-2)
+
+
+@pytest.mark.parametrize("h,m,n,d", [(3, 200, 300, 64), (4, 256, 512, 128)])
+def test_multihead_attention_score(rt, h, m, n, d):
+    """One problem per head: the batched GEMM walks heads x row blocks x
+    column blocks; ragged m and n read the next head's rows, which are never
+    stored."""
+    g = graphs.attention_score(m, n, d, heads=h)
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(h * 100 + m)
+    q = torch.randn(h, m, d, generator=gen, device=DEV).to(torch.bfloat16)
+    k = torch.randn(h, n, d, generator=gen, device=DEV).to(torch.bfloat16)
+    (kern,) = compile_graph(g, dtype="bfloat16")
+    assert kern.plan.kernels[0].config["batch"] == h
+    out = rt.compile(kern)(q, k)
+    torch.cuda.synchronize()
+    assert out.shape == (h, m, n) and MoltenRuntime.read_status(0) == 0
+    res = orc.evaluate(g, {"q": to_numpy(q), "k": to_numpy(k)})
+    assert_close(as_f32(out), res[("f32", g.ops[g._outputs[0]].inputs[0])], "bfloat16",
+                 f"attention {h}x{m}x{n}x{d}")
+
+
+def test_batched_gemm_k_tail(rt):
+    """Batched MN-major B with k = 72: the last k block of a problem reaches
+    into the next problem's B rows, which meet A's zero-filled columns."""
+    from molten_b200.ir import DataflowGraph, TensorShape as TS
+    h, m, k, n = 2, 130, 72, 192
+    g = DataflowGraph("bmm")
+    a = g.add_input("A", TS([h, m, k]), dtype="bfloat16")
+    b = g.add_input("B", TS([h, k, n]), dtype="bfloat16")
+    bias = g.add_input("bias", TS([n]), dtype="bfloat16")
+    g.add_output(g.gelu(g.add(g.matmul(a, b), bias)))
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(9)
+    A = torch.randn(h, m, k, generator=gen, device=DEV).to(torch.bfloat16)
+    B = (torch.randn(h, k, n, generator=gen, device=DEV) / k ** 0.5).to(torch.bfloat16)
+    bb = (0.02 * torch.randn(n, generator=gen, device=DEV)).to(torch.bfloat16)
+    (kern,) = compile_graph(g, dtype="bfloat16")
+    assert kern.plan.kernels[0].config["batch"] == h
+    out = rt.compile(kern)(A, B, bb)
+    torch.cuda.synchronize()
+    assert MoltenRuntime.read_status(0) == 0
+    res = orc.evaluate(g, {"A": to_numpy(A), "B": to_numpy(B), "bias": to_numpy(bb)})
+    assert_close(as_f32(out), res[("f32", g.ops[g._outputs[0]].inputs[0])], "bfloat16", "bmm")
 
 
 def test_gemm_with_transposed_b(rt):
