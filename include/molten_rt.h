@@ -80,6 +80,20 @@ typedef struct molten_gemm_args {
   int batch;                     /* stacked independent problems (0 or 1: one) */
 } molten_gemm_args;
 
+/* Parameter block of the generated fused attention-score kernels
+ * (device side: molten::AttnArgs in molten/attn_sm100.cuh):
+ * P[h] = softmax(Q[h] K[h]^T * scale) for h < batch. */
+typedef struct molten_attn_args {
+  MOLTEN_ALIGN64 unsigned char tmap_q[128];  /* Q [batch*m, d], box {64, 128}, 128B swizzle */
+  MOLTEN_ALIGN64 unsigned char tmap_k[128];  /* K [batch*n, d], box {64, BN}, 128B swizzle */
+  MOLTEN_ALIGN64 unsigned char tmap_p[128];  /* P [batch*m, n], box {32, 32}, 64B swizzle */
+  void* out;                     /* P */
+  long long m, n, d;
+  long long row_offset;
+  int* status;
+  int batch;                     /* stacked independent problems (0 or 1: one) */
+} molten_attn_args;
+
 /* Version of this ABI (major * 100 + minor). */
 int molten_version(void);
 
@@ -131,12 +145,13 @@ int molten_launch(void* mod, const char* kernel, const molten_launch_cfg* cfg,
 /* Encode a 2-D TMA descriptor (128 bytes, 64-byte aligned `tmap`) for a
  * row-major matrix of `outer` rows of `inner` elements, rows
  * `row_stride_bytes` apart, copied in boxes of box_inner x box_outer,
- * with 128-byte swizzle when swizzle128 != 0.  Out-of-range box elements
- * read as zero.  base must be 16-byte aligned and row_stride a multiple of
- * 16 bytes. */
+ * swizzled in spans of `swizzle` bytes: 0 none, 32, 64, or 128 (1 also
+ * means 128); a swizzled box row must not exceed the span.  Out-of-range box
+ * elements read as zero and are not written by stores.  base must be
+ * 16-byte aligned and row_stride a multiple of 16 bytes. */
 int molten_encode_tma_2d(void* tmap, int dtype, const void* base,
                          uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
-                         uint32_t box_inner, uint32_t box_outer, int swizzle128);
+                         uint32_t box_inner, uint32_t box_outer, int swizzle);
 
 /* Per-device error word that kernels with bounded waits set bits in
  * (allocated on first use, then reused). */

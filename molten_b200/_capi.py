@@ -67,7 +67,18 @@ class GemmArgs(ctypes.Structure):
                 ("batch", ctypes.c_int), ("tail_", ctypes.c_ubyte * 20)]
 
 
+class AttnArgs(ctypes.Structure):
+    """molten_attn_args / molten::AttnArgs (448 bytes, 64-byte aligned on the
+    device side)."""
+    _fields_ = [("tmap_q", ctypes.c_ubyte * 128), ("tmap_k", ctypes.c_ubyte * 128),
+                ("tmap_p", ctypes.c_ubyte * 128), ("out", ctypes.c_void_p),
+                ("m", ctypes.c_longlong), ("n", ctypes.c_longlong), ("d", ctypes.c_longlong),
+                ("row_offset", ctypes.c_longlong), ("status", ctypes.c_void_p),
+                ("batch", ctypes.c_int), ("tail_", ctypes.c_ubyte * 12)]
+
+
 assert ctypes.sizeof(RowArgs) == 160
+assert ctypes.sizeof(AttnArgs) == 448
 assert ctypes.sizeof(GemmArgs) == 448
 
 
@@ -153,15 +164,16 @@ class Module:
 
 
 def encode_tma_2d(dtype_code: int, base: int, inner: int, outer: int, row_stride_bytes: int,
-                  box_inner: int, box_outer: int, swizzle128: bool = True) -> bytes:
-    """128-byte TMA descriptor for a row-major 2-D matrix."""
+                  box_inner: int, box_outer: int, swizzle: int = 128) -> bytes:
+    """128-byte TMA descriptor for a row-major 2-D matrix; ``swizzle`` is the
+    span in bytes (0 none, 32, 64, 128)."""
     lib = load_library()
     buf = ctypes.create_string_buffer(128 + 64)
     addr = ctypes.addressof(buf)
     aligned = (addr + 63) & ~63
     check(lib.molten_encode_tma_2d(ctypes.c_void_p(aligned), dtype_code, ctypes.c_void_p(base),
                                    inner, outer, row_stride_bytes, box_inner, box_outer,
-                                   1 if swizzle128 else 0),
+                                   int(swizzle)),
           "encoding a TMA descriptor")
     return ctypes.string_at(aligned, 128)
 

@@ -99,6 +99,9 @@ def launch_records(plan: GroupPlan, name: str) -> list:
             rec.update(block=c["block"], rpc=c["rpc"], upt=c["upt"], tiles=c["tiles"], smem=0)
         elif sk.family == "rope":
             rec.update(block=c["block"], vec=c["vec"], slots_per_row=c["spr"], smem=0)
+        elif sk.family == "attn":
+            rec.update(block=c["threads"], bm=128, bn=c["bn"], stages=c["stages"],
+                       smem=c["smem_bytes"], tma_store=c["tma_store"])
         else:
             rec.update(block=c["threads"], bm=c["bm"], bn=c["bn"], bk=c["bk"],
                        stages=c["stages"], smem=c.get("smem_bytes", 0))
@@ -127,6 +130,8 @@ def estimate(plan: GroupPlan):
     for sk in plan.kernels:
         if sk.family == "gemm":
             flops += 2 * sk.m * sk.n * sk.k
+        elif sk.family == "attn":
+            flops += 2 * sk.config["batch"] * sk.m * sk.n * sk.k
         flops += sk.rows * sk.cols * max(1, len(sk.op_ids))
     return flops, nbytes
 
@@ -161,6 +166,7 @@ class CodeGenerator:
         from .emit import emit_ew, emit_row, emit_row_tma
         from .emit_gemm import emit_gemm
         from .emit_rope import emit_rope
+        from .emit_attn import emit_attn
         chunks = []
         ops_txt = " -> ".join(graph.ops[i].op_type.name for i in group.op_ids) if graph else ""
         chunks.append(f"// Molten auto-generated for {ARCH}: {name}")
@@ -186,6 +192,10 @@ class CodeGenerator:
             elif sk.family == "rope":
                 chunks.append(emit_rope(sk, entry))
                 block_x = sk.config["block"]
+            elif sk.family == "attn":
+                chunks.append(emit_attn(sk, entry))
+                block_x, block_y = 128, sk.config["threads"] // 128
+                smem = max(smem, sk.config["smem_bytes"])
             else:
                 chunks.append(emit_gemm(sk, entry))
                 block_x, block_y = 128, sk.config["threads"] // 128

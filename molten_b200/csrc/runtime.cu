@@ -174,7 +174,7 @@ void molten_internal_set_error(const char* msg) { g_last_error = msg ? msg : "";
 
 extern "C" {
 
-int molten_version(void) { return 100; }
+int molten_version(void) { return 101; }
 
 const char* molten_last_error(void) { return g_last_error.c_str(); }
 
@@ -389,7 +389,7 @@ int molten_launch(void* mod, const char* kernel, const molten_launch_cfg* cfg,
 
 int molten_encode_tma_2d(void* tmap, int dtype, const void* base, uint64_t inner, uint64_t outer,
                          uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
-                         int swizzle128) {
+                         int swizzle) {
   if (!tmap || !base) return fail(MOLTEN_ERR_INVALID, "null tensor map or base pointer");
   if (reinterpret_cast<uintptr_t>(tmap) % 64)
     return fail(MOLTEN_ERR_INVALID, "tensor map storage must be 64-byte aligned");
@@ -409,8 +409,18 @@ int molten_encode_tma_2d(void* tmap, int dtype, const void* base, uint64_t inner
   }
   if ((box_inner * esize) % 16)
     return fail(MOLTEN_ERR_INVALID, "TMA box inner extent must be a multiple of 16 bytes");
-  if (swizzle128 && box_inner * esize > 128)
-    return fail(MOLTEN_ERR_INVALID, "128-byte swizzle needs a box row of at most 128 bytes");
+  // swizzle: 0 none; 1 or 128: 128-byte; 64: 64-byte; 32: 32-byte
+  const uint32_t span = swizzle == 1 ? 128u : (uint32_t)swizzle;
+  CUtensorMapSwizzle sw;
+  switch (span) {
+    case 0: sw = CU_TENSOR_MAP_SWIZZLE_NONE; break;
+    case 32: sw = CU_TENSOR_MAP_SWIZZLE_32B; break;
+    case 64: sw = CU_TENSOR_MAP_SWIZZLE_64B; break;
+    case 128: sw = CU_TENSOR_MAP_SWIZZLE_128B; break;
+    default: return fail(MOLTEN_ERR_INVALID, "swizzle must be 0, 32, 64 or 128 bytes");
+  }
+  if (span && box_inner * esize > span)
+    return fail(MOLTEN_ERR_INVALID, "a swizzled box row must not exceed the swizzle span");
   int rc = need_driver();
   if (rc) return rc;
   cuuint64_t dims[2] = {inner, outer};
@@ -420,7 +430,7 @@ int molten_encode_tma_2d(void* tmap, int dtype, const void* base, uint64_t inner
   CUresult r = driver().tensor_map_encode_tiled(
       static_cast<CUtensorMap*>(tmap), t, 2, const_cast<void*>(base), dims, strides, box, estr,
       CU_TENSOR_MAP_INTERLEAVE_NONE,
-      swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+      sw,
       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return drv_fail(r, "cuTensorMapEncodeTiled");
   return MOLTEN_OK;

@@ -310,13 +310,52 @@ def rms_prologue(graph: DataflowGraph, m: int, members: set, outs=()):
     return None
 
 
-def split_group(graph: DataflowGraph, ordered: list, outs=(), fuse_prologue: bool = True) -> list:
+def attention_pattern(graph: DataflowGraph, ordered: list, outs=()):
+    """(transpose, matmul, mul or None, softmax) when the group is exactly
+    softmax(matmul(q, transpose(k)) [* scalar constant]) over the last dim,
+    with only the softmax leaving the group; else None."""
+    if len(ordered) not in (3, 4):
+        return None
+    by = {graph.ops[i].op_type: i for i in ordered}
+    if len(by) != len(ordered) or not {OpType.TRANSPOSE, OpType.MATMUL, OpType.SOFTMAX} <= set(by):
+        return None
+    t, m, sm = by[OpType.TRANSPOSE], by[OpType.MATMUL], by[OpType.SOFTMAX]
+    mul = by.get(OpType.MUL)
+    if len(ordered) == 4 and mul is None:
+        return None
+    if graph.ops[m].inputs[1] != t or graph.ops[m].inputs[0] == t:
+        return None
+    members = set(ordered)
+    if any(o in outs for o in (t, m, mul) if o is not None) or sm not in outs and outs:
+        return None
+    users = lambda o: [u for u in members if o in graph.ops[u].inputs]
+    if users(t) != [m]:
+        return None
+    if mul is not None:
+        others = [i for i in graph.ops[mul].inputs if i != m]
+        if len(others) != 1 or users(m) != [mul] or graph.ops[sm].inputs != [mul]:
+            return None
+        c = graph.ops[others[0]]
+        if c.op_type != OpType.CONSTANT or c.attrs.get("kind") or c.attrs.get("value") is None:
+            return None
+    elif graph.ops[sm].inputs != [m]:
+        return None
+    d = graph.ops[sm].reduction_dim
+    if d not in (None, -1):
+        return None
+    return t, m, mul, sm
+
+
+def split_group(graph: DataflowGraph, ordered: list, outs=(), fuse_prologue: bool = True,
+                fuse_attention: bool = True) -> list:
     """Split a group's live ops into (family, ops) sub-kernels.
 
     ROTATE (RoPE) reads each element's pair partner, so it runs as a
     sub-kernel of its own between what it depends on and what follows (the
     fusion rules put it in any group: it is neither elementwise nor a
     reduction, ``fusion.py:65``)."""
+    if fuse_attention and attention_pattern(graph, ordered, set(outs)):
+        return [("attn", list(ordered))]
     rot = [i for i in ordered if graph.ops[i].op_type == OpType.ROTATE]
     if rot:
         r = rot[0]

@@ -9,12 +9,13 @@ from .lowering import (
     DTYPE_SIZE, GroupPlan, LoweringError, Operand, OutputSpec, SubKernel,
     broadcast_shapes, build_dag, canon_dtype, choose_ew_config,
     choose_row_config, choose_row_tma_config, choose_rope_config, classify_operand,
-    rms_prologue,
+    rms_prologue, attention_pattern,
     group_boundary, infer_shapes,
     is_mask_const, prod, promote, split_group, EXPENSIVE,
 )
 
 DEFAULT_SYMBOLIC_DIM = 1024
+ATTN_SMEM_LIMIT = 232448          # dynamic shared memory one sm_100 CTA may opt into
 
 
 def declared_shape(op, symbols: dict) -> tuple:
@@ -77,8 +78,10 @@ def plan_group(graph: DataflowGraph, group_op_ids, input_shapes: dict,
     # row kernel + GEMM pair (bf16 8192x4096x14336: 1308 vs 892 us; 64 rows:
     # 64 vs 44 us) -- the in-place transform of every A stage competes with
     # the tensor core for the same shared memory and lengthens each stage
+    # {"attn": {"fused": False}} runs attention scores as GEMM + row softmax
     parts = split_group(graph, ordered, outs,
-                        fuse_prologue=(tune.get("gemm") or {}).get("prologue", False))
+                        fuse_prologue=(tune.get("gemm") or {}).get("prologue", False),
+                        fuse_attention=(tune.get("attn") or {}).get("fused", True))
     # intermediates between the sub-kernels of one group are stored in fp32,
     # so a split group still rounds once (at its outputs); a MATMUL operand
     # keeps its 16-bit type because the tensor cores read it
@@ -124,6 +127,8 @@ def plan_group(graph: DataflowGraph, group_op_ids, input_shapes: dict,
 def _plan_sub(graph, family, ops, ext, outs, shapes, dts, tune) -> SubKernel:
     if family == "gemm":
         return _plan_gemm(graph, ops, ext, outs, shapes, dts, tune)
+    if family == "attn":
+        return _plan_attn(graph, ops, outs, shapes, dts, tune)
     if family == "rope":
         return _plan_rope(graph, ops, outs, shapes, dts, tune)
     it = ()
@@ -281,6 +286,59 @@ def _plan_rope(graph, ops, outs, shapes, dts, tune) -> SubKernel:
     sk.precise = True
     sk.config = choose_rope_config(sk, op.attrs.get("style") or "interleaved",
                                    int(x_shape[-3]), int(x_shape[-2]), tune.get("rope") or {})
+    return sk
+
+
+def _plan_attn(graph, ops, outs, shapes, dts, tune) -> SubKernel:
+    """Fused attention scores: P = softmax(q k^T * scale), q [.., m, d],
+    k [.., n, d], leading dims = independent problems (heads)."""
+    t, m, mul, sm = attention_pattern(graph, ops, set(outs))
+    q_id, k_id = graph.ops[m].inputs[0], graph.ops[t].inputs[0]
+    qs, ks = tuple(shapes[q_id]), tuple(shapes[k_id])
+    if len(qs) < 2 or len(ks) < 2 or qs[-1] != ks[-1] or (len(ks) > 2 and qs[:-2] != ks[:-2]):
+        raise LoweringError(f"attention scores need q [.., m, d] and k [.., n, d]: {qs}, {ks}")
+    if dts[q_id] != dts[k_id] or dts[q_id] == "float32":
+        raise LoweringError("attention scores take bf16 or fp16 q and k")
+    batch = prod(ks[:-2]) if len(ks) > 2 else 1
+    M = int(qs[-2]) if batch > 1 else prod(qs[:-1])
+    N, D = int(ks[-2]), int(qs[-1])
+    if D % 8 or D > 256:
+        raise LoweringError("attention head dim must be a multiple of 8, at most 256")
+    if max(batch * M, batch * N) >= 2 ** 31:
+        raise LoweringError("attention rows beyond the 32-bit TMA coordinate range")
+    scale = 1.0
+    if mul is not None:
+        c = [i for i in graph.ops[mul].inputs if i != m][0]
+        scale = float(graph.ops[c].attrs["value"])
+    operands = [Operand(index=i, op_id=j, name=graph.ops[j].name or f"op{j}", dtype=dts[j],
+                        shape=shapes[j], last="vec", row_map="full")
+                for i, j in enumerate((q_id, k_id))]
+    outputs = [OutputSpec(index=0, op_id=sm, dtype=dts[sm], shape=shapes[sm], kind="full")]
+    sk = SubKernel(family="attn", op_ids=list(ops), operands=operands, outputs=outputs,
+                   rows=batch * M, cols=N, m=M, n=N, k=D, a_operand=0, b_operand=1)
+    if DTYPE_SIZE[dts[sm]] != 2:
+        raise LoweringError("attention scores are stored as bf16 or fp16")
+    if M < 1 or N < 1:
+        raise LoweringError("attention scores need at least one row and one column")
+    o = dict(tune.get("attn") or {})
+    bn = int(o.get("bn") or min(256, 64 * -(-N // 64)))
+    if bn % 64 or not 64 <= bn <= 256:
+        raise LoweringError(f"attention column block {bn} must be 64..256, a multiple of 64")
+    dch = -(-D // 64)
+    # resident Q tile + K ring + 4 warps x 2 staging tiles of 32 x 32 outputs
+    q_bytes, stage, out_bytes = dch * 128 * 128, bn * 128, 4 * 2 * 32 * 64
+    fit = (ATTN_SMEM_LIMIT - 2048 - out_bytes - q_bytes) // stage
+    stages = int(o.get("stages") or max(2, min(8, fit)))
+    smem = q_bytes + stages * stage + out_bytes + (2 * stages + 7) * 8 + 16 + 1024
+    if smem > ATTN_SMEM_LIMIT:
+        raise LoweringError(f"attention tile needs {smem} bytes of shared memory")
+    rows_aligned = (N * 2) % 16 == 0
+    # a TMA store box of 32 rows stays inside its head when m % 32 == 0; with
+    # one head the rows past m lie outside the tensor and are dropped
+    tma_store = bool(o.get("tma_store", True)) and rows_aligned and (M % 32 == 0 or batch == 1)
+    sk.config = {"bn": bn, "dch": dch, "stages": stages, "smem_bytes": smem, "threads": 256,
+                 "scale": scale, "batch": int(batch), "rows_aligned": rows_aligned,
+                 "tma_store": tma_store}
     return sk
 
 

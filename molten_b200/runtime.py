@@ -131,6 +131,15 @@ class _Spec:
             cfg.block[:] = [c["block"], 1, 1]
             cfg.cluster[:] = [1, 1, 1]
             cfg.smem_bytes = 0
+        elif sk.family == "attn":
+            # persistent: one CTA per SM (the tile's shared memory allows one)
+            torch = _torch()
+            sms = torch.cuda.get_device_properties(device).multi_processor_count
+            items = c["batch"] * (-(-sk.m // 128))
+            cfg.grid[:] = [max(1, min(items, sms)), 1, 1]
+            cfg.block[:] = [128, c["threads"] // 128, 1]
+            cfg.cluster[:] = [1, 1, 1]
+            cfg.smem_bytes = c["smem_bytes"]
         else:
             torch = _torch()
             sms = torch.cuda.get_device_properties(device).multi_processor_count
@@ -143,19 +152,40 @@ class _Spec:
         self._cfgs[key] = cfg
         return cfg
 
-    def tmap(self, t, dtype: str, rows: int, cols: int, box_inner: int, box_outer: int) -> bytes:
-        key = (t.data_ptr(), rows, cols, t.stride(0), box_inner, box_outer)
+    def tmap(self, t, dtype: str, rows: int, cols: int, box_inner: int, box_outer: int,
+             swizzle: int = 128) -> bytes:
+        key = (t.data_ptr(), rows, cols, t.stride(0), box_inner, box_outer, swizzle)
         v = self._tmaps.get(key)
         if v is None:
             esz = DTYPE_SIZE[dtype]
             v = _capi.encode_tma_2d(_TMA_CODE[dtype], t.data_ptr(), cols, rows,
-                                    t.stride(0) * esz, box_inner, box_outer, True)
+                                    t.stride(0) * esz, box_inner, box_outer, swizzle)
             self._tmaps[key] = v
             if len(self._tmaps) > 64:
                 self._tmaps.popitem(last=False)
         else:
             self._tmaps.move_to_end(key)
         return v
+
+    def _attn_args(self, sk, env, device: int):
+        """molten_attn_args for the fused attention-score kernel."""
+        c = sk.config
+        a = _capi.AttnArgs()
+        dt = sk.operands[0].dtype
+        nb = c["batch"]
+        Q = _attn_tensor_2d(env[sk.operands[0].op_id])
+        K = _attn_tensor_2d(env[sk.operands[1].op_id])
+        P = _attn_tensor_2d(env[sk.outputs[0].op_id])
+        ctypes.memmove(a.tmap_q, self.tmap(Q, dt, nb * sk.m, sk.k, 64, 128), 128)
+        ctypes.memmove(a.tmap_k, self.tmap(K, dt, nb * sk.n, sk.k, 64, c["bn"]), 128)
+        if c["tma_store"]:
+            ctypes.memmove(a.tmap_p, self.tmap(P, sk.outputs[0].dtype, nb * sk.m, sk.n, 32, 32, 64),
+                           128)
+        a.out = P.data_ptr()
+        a.m, a.n, a.d = sk.m, sk.n, sk.k
+        a.batch = nb
+        a.status = _capi.status_word(device)
+        return a
 
     def run(self, tensors, outs, stream: Optional[int], row_offset: int):
         torch = _torch()
@@ -174,7 +204,9 @@ class _Spec:
         mod = self.module(di)
         for i, sk in enumerate(plan.kernels):
             cfg = self.launch_cfg(i, di)
-            if sk.family == "gemm":
+            if sk.family == "attn":
+                a = self._attn_args(sk, env, di)
+            elif sk.family == "gemm":
                 a = _capi.GemmArgs()
                 A = env[sk.operands[sk.a_operand].op_id]
                 B = env[sk.operands[sk.b_operand].op_id]
@@ -201,6 +233,17 @@ class _Spec:
                     a.status = _capi.status_word(di)
             a.row_offset = row_offset
             ins_al, outs_al = self.align[i]
+            if sk.family == "attn":
+                # pointers travel inside the tensor maps; check their alignment
+                for opd, al in zip(sk.operands, ins_al):
+                    if env[opd.op_id].data_ptr() % al:
+                        raise _capi.MoltenError(f"input {opd.name!r} is not {al}-byte aligned as "
+                                                f"kernel {self.entries[i].decode()} requires")
+                if a.out % outs_al[0]:
+                    raise _capi.MoltenError(f"output is not {outs_al[0]}-byte aligned as kernel "
+                                            f"{self.entries[i].decode()} requires")
+                mod.launch(self.entries[i], cfg, a, stream)
+                continue
             for opd, al in zip(sk.operands, ins_al):
                 p = env[opd.op_id].data_ptr()
                 if p % al:
@@ -217,11 +260,19 @@ class _Spec:
         return outs
 
 
+def _attn_tensor_2d(t):
+    """[.., rows, cols] contiguous-row tensor as a 2-D [rows, cols] view."""
+    return t.reshape(-1, t.shape[-1])
+
+
 def _alignment_rules(sk):
     """Byte alignment each input / output pointer of a sub-kernel needs:
     16 for TMA sources and for 16-byte vector slots, the slot size for
     narrower slots, the element size for per-row scalars."""
     c = sk.config
+    if sk.family == "attn":
+        # TMA sources; P is written by TMA (16) or element by element (2)
+        return [16, 16], [16 if c["rows_aligned"] else 2]
     if sk.family == "gemm":
         ins = [16 if o.last == "vec" else DTYPE_SIZE[o.dtype] for o in sk.operands]
         return ins, [16 for _ in sk.outputs]

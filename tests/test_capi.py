@@ -33,7 +33,7 @@ def test_library_loads_and_exports_every_declared_symbol():
 
 def test_version_and_last_error():
     lib = _capi.load_library()
-    assert lib.molten_version() == 100
+    assert lib.molten_version() == 101
     assert isinstance(lib.molten_last_error(), bytes)
 
 
@@ -67,6 +67,11 @@ def test_null_and_bad_arguments_are_rejected():
                                     64, 64, 120, 64, 64, 1) == 1          # stride
     assert lib.molten_encode_tma_2d(ctypes.c_void_p(aligned), 2, ctypes.c_void_p(4096),
                                     64, 64, 256, 64, 64, 1) == 1          # 256 B box row
+    assert lib.molten_encode_tma_2d(ctypes.c_void_p(aligned), 0, ctypes.c_void_p(4096),
+                                    64, 64, 128, 64, 64, 64) == 1         # row over a 64 B span
+    assert lib.molten_encode_tma_2d(ctypes.c_void_p(aligned), 0, ctypes.c_void_p(4096),
+                                    64, 64, 128, 32, 32, 48) == 1         # no such swizzle
+    assert b"swizzle" in lib.molten_last_error()
     assert lib.molten_read_status(0, None, 0) == 1
 
 

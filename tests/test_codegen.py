@@ -193,15 +193,66 @@ def test_rope_kernels(tmp_path, style, packed):
 
 def test_attention_score_plan(tmp_path):
     """[TRANSPOSE, MATMUL, MUL, SOFTMAX] (one group, as the reference fuses
-    it): a K-major-B GEMM with the scale in its epilogue, then a row
-    softmax; the TRANSPOSE is no kernel."""
+    it) runs as one fused kernel: K read K-major, scale * log2(e) baked in,
+    two tensor-core passes, TMA stores of the probabilities."""
     (k,) = compile_graph(graphs.attention_score(256, 512, 128), dtype="bfloat16")
     assert k.name == "molten_fused_transpose_matmul_mul_softmax"
+    (sk,) = k.plan.kernels
+    assert sk.family == "attn" and (sk.m, sk.n, sk.k) == (256, 512, 128)
+    c = sk.config
+    assert c["bn"] == 256 and c["dch"] == 2 and c["tma_store"] and c["batch"] == 1
+    assert c["smem_bytes"] <= 232448 and abs(c["scale"] - 128 ** -0.5) < 1e-12
+    assert "attn_roles<" in k.source and ", bf16, true, true>(sh, args," in k.source
+    rec = k.config.launches[0]
+    assert rec["family"] == "attn" and rec["smem"] == c["smem_bytes"]
+    assert build_cubin(k.source, k.name, tmp_path).stat().st_size > 1000
+
+
+def test_attention_score_store_paths():
+    """TMA stores need 16-byte rows (n % 8 == 0) and store boxes that stay in
+    one head (m % 32 == 0, or a single head); otherwise direct stores."""
+    def cfg(**kw):
+        (k,) = compile_graph(graphs.attention_score(**kw), dtype="bfloat16")
+        return k.plan.kernels[0].config
+    assert cfg(m=96, n=136, d=128, heads=5)["tma_store"]
+    assert not cfg(m=200, n=300, d=64, heads=3)["tma_store"]          # m % 32
+    assert cfg(m=200, n=304, d=64)["tma_store"]                        # one head: clipped
+    c = cfg(m=100, n=77, d=72)
+    assert not c["tma_store"] and not c["rows_aligned"]
+    assert c["bn"] == 128 and c["dch"] == 2
+    assert cfg(m=64, n=1000, d=256, heads=2)["stages"] == 4
+
+
+def test_attention_score_unfused_plan(tmp_path):
+    """With {"attn": {"fused": False}}: a K-major-B GEMM with the scale in
+    its epilogue, then a row softmax; the TRANSPOSE is no kernel."""
+    g = graphs.attention_score(256, 512, 128)
+    k = CodeGenerator(dtype="bfloat16", tune={"attn": {"fused": False}}).generate(
+        g, FusionEngine().fuse(g)[0])
     gemm, row = k.plan.kernels
     assert gemm.family == "gemm" and gemm.config["b_kmajor"] and (gemm.m, gemm.n, gemm.k) == (256, 512, 128)
     assert row.family == "row"
     assert ", true, NoPrologue>(sh, args)" in k.source
     assert build_cubin(k.source, k.name, tmp_path).stat().st_size > 1000
+
+
+def test_attention_pattern_needs_the_exact_group():
+    """Only softmax(matmul(q, transpose(k)) [* constant]) fuses; a tensor
+    scale or an extra output keeps the two-kernel form."""
+    g = DataflowGraph("s")
+    q = g.add_input("q", TS([128, 64]), dtype="bfloat16")
+    kk = g.add_input("k", TS([256, 64]), dtype="bfloat16")
+    sc = g.add_input("sc", TS([256]), dtype="bfloat16")
+    g.add_output(g.softmax(g.mul(g.matmul(q, g.transpose(kk)), sc)))
+    (k,) = compile_graph(g, dtype="bfloat16")
+    assert [sk.family for sk in k.plan.kernels] == ["gemm", "row"]
+    g = DataflowGraph("s2")
+    q = g.add_input("q", TS([128, 64]), dtype="bfloat16")
+    kk = g.add_input("k", TS([256, 64]), dtype="bfloat16")
+    g.add_output(g.softmax(g.matmul(q, g.transpose(kk))))
+    (k,) = compile_graph(g, dtype="bfloat16")
+    assert [sk.family for sk in k.plan.kernels] == ["attn"]
+    assert k.plan.kernels[0].config["scale"] == 1.0
 
 
 def test_transpose_elsewhere_is_rejected():

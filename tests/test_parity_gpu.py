@@ -438,20 +438,37 @@ def test_rmsnorm_then_rope_group(rt):
     assert_close(as_f32(out), res[("f32", g.ops[g._outputs[0]].inputs[0])], "bfloat16", "norm+rope")
 
 
+def _attention_kernel(g, dtype, fused):
+    from molten_b200.codegen import CodeGenerator
+    gen = CodeGenerator(dtype=dtype, tune=None if fused else {"attn": {"fused": False}})
+    (grp,) = FusionEngine().fuse(g)
+    kern = gen.generate(g, grp)
+    fams = [sk.family for sk in kern.plan.kernels]
+    if fused:
+        assert fams == ["attn"]
+    else:
+        assert fams == ["gemm", "row"] and kern.plan.kernels[0].config["b_kmajor"]
+    return kern
+
+
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "gemm+softmax"])
 @pytest.mark.parametrize("m,n,d,dtype", [(256, 512, 128, "bfloat16"), (200, 300, 64, "bfloat16"),
-                                         (130, 1000, 256, "float16"), (64, 4096, 128, "bfloat16")])
-def test_attention_score(rt, m, n, d, dtype):
-    """softmax(Q @ K^T * scale) (ops.py:55-59): the GEMM reads K's rows
-    K-major (the TRANSPOSE costs nothing), scale in its epilogue, fp32
-    scores, row softmax."""
+                                         (130, 1000, 256, "float16"), (64, 4096, 128, "bfloat16"),
+                                         (100, 77, 72, "bfloat16"), (33, 40, 16, "float16"),
+                                         (512, 2048, 128, "bfloat16")])
+def test_attention_score(rt, m, n, d, dtype, fused):
+    """softmax(Q @ K^T * scale) (ops.py:55-59).  Fused: one kernel, two
+    tensor-core passes over K (row statistics, then probabilities), no score
+    matrix in HBM.  Unfused: the GEMM reads K's rows K-major (the TRANSPOSE
+    costs nothing), scale in its epilogue, fp32 scores, row softmax.  Ragged
+    m, n and d: rows past m and columns past n are computed from zero-filled
+    or neighbouring data and never stored."""
     g = graphs.attention_score(m, n, d, dtype=dtype)
     gen = torch.Generator(device=DEV)
     gen.manual_seed(m + n + d)
     q = torch.randn(m, d, generator=gen, device=DEV).to(TORCH_DT[dtype])
     k = torch.randn(n, d, generator=gen, device=DEV).to(TORCH_DT[dtype])
-    (kern,) = compile_graph(g, dtype=dtype)
-    assert [sk.family for sk in kern.plan.kernels] == ["gemm", "row"]
-    assert kern.plan.kernels[0].config["b_kmajor"]
+    kern = _attention_kernel(g, dtype, fused)
     out = rt.compile(kern)(q, k)
     torch.cuda.synchronize()
     assert MoltenRuntime.read_status(0) == 0
@@ -462,17 +479,19 @@ def test_attention_score(rt, m, n, d, dtype):
     assert np.all(np.abs(sums - 1.0) < 2e-2)
 
 
-@pytest.mark.parametrize("h,m,n,d", [(3, 200, 300, 64), (4, 256, 512, 128)])
-def test_multihead_attention_score(rt, h, m, n, d):
-    """One problem per head: the batched GEMM walks heads x row blocks x
-    column blocks; ragged m and n read the next head's rows, which are never
-    stored."""
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "gemm+softmax"])
+@pytest.mark.parametrize("h,m,n,d", [(3, 200, 300, 64), (4, 256, 512, 128), (5, 96, 136, 128),
+                                     (2, 129, 64, 128), (6, 64, 1000, 32)])
+def test_multihead_attention_score(rt, h, m, n, d, fused):
+    """One problem per head, heads stacked along the rows: a row block past
+    m reads the next head's rows, which are never stored (TMA stores only
+    when m is a multiple of 32, so that no 32-row store box crosses a head)."""
     g = graphs.attention_score(m, n, d, heads=h)
     gen = torch.Generator(device=DEV)
     gen.manual_seed(h * 100 + m)
     q = torch.randn(h, m, d, generator=gen, device=DEV).to(torch.bfloat16)
     k = torch.randn(h, n, d, generator=gen, device=DEV).to(torch.bfloat16)
-    (kern,) = compile_graph(g, dtype="bfloat16")
+    kern = _attention_kernel(g, "bfloat16", fused)
     assert kern.plan.kernels[0].config["batch"] == h
     out = rt.compile(kern)(q, k)
     torch.cuda.synchronize()
@@ -480,6 +499,27 @@ def test_multihead_attention_score(rt, h, m, n, d):
     res = orc.evaluate(g, {"q": to_numpy(q), "k": to_numpy(k)})
     assert_close(as_f32(out), res[("f32", g.ops[g._outputs[0]].inputs[0])], "bfloat16",
                  f"attention {h}x{m}x{n}x{d}")
+
+
+def test_fused_attention_large_logits(rt):
+    """Scores far from zero (scale 1, |s| up to ~100): the row maximum is
+    subtracted before exponentiation, so nothing overflows and each row's
+    largest entry is the one the oracle picks."""
+    m, n, d = 128, 384, 64
+    g = graphs.attention_score(m, n, d, scale=1.0)
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(7)
+    q = (torch.randn(m, d, generator=gen, device=DEV) * 1.5).to(torch.bfloat16)
+    k = (torch.randn(n, d, generator=gen, device=DEV) * 1.5).to(torch.bfloat16)
+    kern = _attention_kernel(g, "bfloat16", True)
+    out = rt.compile(kern)(q, k)
+    torch.cuda.synchronize()
+    assert MoltenRuntime.read_status(0) == 0
+    got = as_f32(out)
+    assert np.all(np.isfinite(got))
+    res = orc.evaluate(g, {"q": to_numpy(q), "k": to_numpy(k)})
+    ref = res[("f32", g.ops[g._outputs[0]].inputs[0])]
+    assert_close(got, ref, "bfloat16", "attention large logits")
 
 
 def test_batched_gemm_k_tail(rt):
