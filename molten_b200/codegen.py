@@ -194,7 +194,7 @@ class CodeGenerator:
                 block_x = sk.config["block"]
             elif sk.family == "attn":
                 chunks.append(emit_attn(sk, entry))
-                block_x, block_y = 128, sk.config["threads"] // 128
+                block_x, block_y = sk.config["threads"], 1
                 smem = max(smem, sk.config["smem_bytes"])
             else:
                 chunks.append(emit_gemm(sk, entry))

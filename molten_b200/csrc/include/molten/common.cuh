@@ -151,6 +151,26 @@ __device__ __forceinline__ float fast_exp2(float x) {
 }
 #define MOLTEN_LOG2E 1.4426950408889634f
 
+// 2^x on the FMA pipe, for kernels whose EX2 unit is the bottleneck: Cody-
+// Waite range reduction x = j + f, j = round(x) (adding 1.5 * 2^23 leaves
+// round(x) in the low mantissa bits), f in [-1/2, 1/2]; 2^f by the cubic of
+// least maximum relative error on that interval (Remez exchange, relative
+// error 7.5e-5 -- enough for 16-bit results); 2^j added to the exponent
+// field as an integer.  x is clamped at -126 so the exponent never wraps:
+// results below 2^-126 come out as tiny values instead of 0.  x <= 1 here.
+#define MOLTEN_EXP2_C0 0.9999280571937561f
+#define MOLTEN_EXP2_C1 0.6932609677314758f
+#define MOLTEN_EXP2_C2 0.2426111251115799f
+#define MOLTEN_EXP2_C3 0.0551716685295105f
+__device__ __forceinline__ float exp2_poly3(float x) {
+  x = fmaxf(x, -126.0f);
+  const float r = __fadd_rn(x, 12582912.0f);
+  const float f = __fsub_rn(x, __fsub_rn(r, 12582912.0f));
+  const float p = fmaf(fmaf(fmaf(MOLTEN_EXP2_C3, f, MOLTEN_EXP2_C2), f, MOLTEN_EXP2_C1), f,
+                       MOLTEN_EXP2_C0);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(r) << 23));
+}
+
 // 1/x with the MUFU.RCP instruction (rcp.approx.ftz: about 1 ulp); 1/inf = 0
 __device__ __forceinline__ float fast_rcp(float x) {
   float y;

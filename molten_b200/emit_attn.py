@@ -30,7 +30,11 @@ def emit_attn(sk: SubKernel, name: str) -> str:
     w("")
     w("using namespace molten;")
     w("")
-    w(f"typedef AttnLayout<{c['bn']}, {c['dch']}, {c['stages']}> Layout_{name};")
+    w(f"typedef AttnLayout<{c['bn']}, {c['dch']}, {c['stages']}, {c['epi_warps']}, {c['groups']}> "
+      f"Layout_{name};")
+    w(f"static_assert(Layout_{name}::SMEM_BYTES <= {c['smem_bytes']}, "
+      f"\"the launch's dynamic shared memory holds the layout\");")
+    w(f"static_assert(Layout_{name}::THREADS == {c['threads']}, \"block size\");")
     w("")
     w(f"extern \"C\" __global__ void __launch_bounds__({c['threads']}, 1) "
       f"{name}(const __grid_constant__ AttnArgs args) {{")
@@ -40,7 +44,9 @@ def emit_attn(sk: SubKernel, name: str) -> str:
     w("  pdl_enter();                            // no global access before this")
     w("  __syncthreads();")
     w(f"  attn_roles<Layout_{name}, {f16in}, {ot}, {'true' if c['tma_store'] else 'false'}, "
-      f"{'true' if c['rows_aligned'] else 'false'}>(sh, args, {c_float(c2)});")
+      f"{'true' if c['rows_aligned'] else 'false'}, {c['poly'][0]}, {c['poly'][1]}, "
+      f"{'true' if c['sum16'] else 'false'}>"
+      f"(sh, args, {c_float(c2)});")
     w("  __syncthreads();")
     w(f"  attn_teardown<Layout_{name}>(sh);       // TMEM release")
     w("}")

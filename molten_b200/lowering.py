@@ -338,6 +338,9 @@ def attention_pattern(graph: DataflowGraph, ordered: list, outs=()):
         c = graph.ops[others[0]]
         if c.op_type != OpType.CONSTANT or c.attrs.get("kind") or c.attrs.get("value") is None:
             return None
+        v = float(c.attrs["value"])
+        if not (v > 0.0 and v < float("inf")):       # the row max is taken on raw scores
+            return None
     elif graph.ops[sm].inputs != [m]:
         return None
     d = graph.ops[sm].reduction_dim

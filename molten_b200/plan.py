@@ -16,6 +16,8 @@ from .lowering import (
 
 DEFAULT_SYMBOLIC_DIM = 1024
 ATTN_SMEM_LIMIT = 232448          # dynamic shared memory one sm_100 CTA may opt into
+ATTN_POLY = (0, 0)                # exponentials per 32 on the FMA pipe (pass 0, pass 1)
+ATTN_SUM16 = False                # pass-0 row sums from f16 exponential pairs
 
 
 def declared_shape(op, symbols: dict) -> tuple:
@@ -325,20 +327,43 @@ def _plan_attn(graph, ops, outs, shapes, dts, tune) -> SubKernel:
     if bn % 64 or not 64 <= bn <= 256:
         raise LoweringError(f"attention column block {bn} must be 64..256, a multiple of 64")
     dch = -(-D // 64)
-    # resident Q tile + K ring + 4 warps x 2 staging tiles of 32 x 32 outputs
-    q_bytes, stage, out_bytes = dch * 128 * 128, bn * 128, 4 * 2 * 32 * 64
-    fit = (ATTN_SMEM_LIMIT - 2048 - out_bytes - q_bytes) // stage
+    # epilogue warps: 4 per TMEM lane quarter when a tile has 4 column parts
+    # of whole 32-column chunks, else 2
+    # epilogue warps: 4 per TMEM lane quarter, each a quarter of every
+    # tile's columns ("groups": 2 splits them into two groups taking
+    # alternate tiles -- measured slower: each group then owns one of the two
+    # accumulator buffers and waits for its next tile's MMA serially)
+    groups = int(o.get("groups") or 1)
+    epi = int(o.get("epi_warps") or (16 if (bn // 32) % (4 // groups) == 0 else 8))
+    if epi not in (4, 8, 12, 16) or groups not in (1, 2) or (epi // 4) % groups:
+        raise LoweringError(f"{epi} epilogue warps cannot form {groups} groups")
+    parts = epi // 4 // groups
+    if (bn // 32) % parts:
+        raise LoweringError(f"{parts} column parts cannot split a {bn}-column block")
+    # resident Q tile + K ring + per-warp staging tiles of 32 rows x (up to
+    # 64) columns (two per warp up to 8 warps) + the (max, sum) exchange
+    scols = 64 if (bn // parts) % 64 == 0 else 32
+    out_bytes = epi * (2 if epi <= 8 else 1) * 32 * scols * 2
+    q_bytes, stage, stat_bytes = dch * 128 * 128, bn * 128, 2 * epi * 32 * 8
+    fit = (ATTN_SMEM_LIMIT - 2048 - out_bytes - stat_bytes - q_bytes) // stage
     stages = int(o.get("stages") or max(2, min(8, fit)))
-    smem = q_bytes + stages * stage + out_bytes + (2 * stages + 7) * 8 + 16 + 1024
+    smem = q_bytes + stages * stage + out_bytes + stat_bytes + (2 * stages + 11) * 8 + 16 + 1024
     if smem > ATTN_SMEM_LIMIT:
         raise LoweringError(f"attention tile needs {smem} bytes of shared memory")
     rows_aligned = (N * 2) % 16 == 0
     # a TMA store box of 32 rows stays inside its head when m % 32 == 0; with
     # one head the rows past m lie outside the tensor and are dropped
     tma_store = bool(o.get("tma_store", True)) and rows_aligned and (M % 32 == 0 or batch == 1)
-    sk.config = {"bn": bn, "dch": dch, "stages": stages, "smem_bytes": smem, "threads": 256,
+    # of each 32 exponentials per pass, how many run on the FMA pipe
+    poly = o.get("poly", ATTN_POLY)
+    poly = [int(poly), int(poly)] if isinstance(poly, (int, float)) else [int(x) for x in poly]
+    if len(poly) != 2 or not all(0 <= x <= 32 for x in poly):
+        raise LoweringError(f"attention poly split {poly} must be two counts in 0..32")
+    sk.config = {"bn": bn, "dch": dch, "stages": stages, "smem_bytes": smem,
+                 "threads": 32 * (4 + epi), "epi_warps": epi, "groups": groups,
                  "scale": scale, "batch": int(batch), "rows_aligned": rows_aligned,
-                 "tma_store": tma_store}
+                 "tma_store": tma_store, "poly": poly, "store_cols": scols,
+                 "sum16": bool(o.get("sum16", ATTN_SUM16))}
     return sk
 
 

@@ -137,7 +137,7 @@ class _Spec:
             sms = torch.cuda.get_device_properties(device).multi_processor_count
             items = c["batch"] * (-(-sk.m // 128))
             cfg.grid[:] = [max(1, min(items, sms)), 1, 1]
-            cfg.block[:] = [128, c["threads"] // 128, 1]
+            cfg.block[:] = [c["threads"], 1, 1]
             cfg.cluster[:] = [1, 1, 1]
             cfg.smem_bytes = c["smem_bytes"]
         else:
@@ -179,8 +179,9 @@ class _Spec:
         ctypes.memmove(a.tmap_q, self.tmap(Q, dt, nb * sk.m, sk.k, 64, 128), 128)
         ctypes.memmove(a.tmap_k, self.tmap(K, dt, nb * sk.n, sk.k, 64, c["bn"]), 128)
         if c["tma_store"]:
-            ctypes.memmove(a.tmap_p, self.tmap(P, sk.outputs[0].dtype, nb * sk.m, sk.n, 32, 32, 64),
-                           128)
+            sc = c["store_cols"]          # 32 or 64 columns: a 64- or 128-byte swizzled row
+            ctypes.memmove(a.tmap_p, self.tmap(P, sk.outputs[0].dtype, nb * sk.m, sk.n, sc, 32,
+                                               2 * sc), 128)
         a.out = P.data_ptr()
         a.m, a.n, a.d = sk.m, sk.n, sk.k
         a.batch = nb

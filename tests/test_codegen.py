@@ -202,7 +202,7 @@ def test_attention_score_plan(tmp_path):
     c = sk.config
     assert c["bn"] == 256 and c["dch"] == 2 and c["tma_store"] and c["batch"] == 1
     assert c["smem_bytes"] <= 232448 and abs(c["scale"] - 128 ** -0.5) < 1e-12
-    assert "attn_roles<" in k.source and ", bf16, true, true>(sh, args," in k.source
+    assert "attn_roles<" in k.source and ", bf16, true, true, 0, 0, false>(sh, args," in k.source
     rec = k.config.launches[0]
     assert rec["family"] == "attn" and rec["smem"] == c["smem_bytes"]
     assert build_cubin(k.source, k.name, tmp_path).stat().st_size > 1000
@@ -220,7 +220,8 @@ def test_attention_score_store_paths():
     c = cfg(m=100, n=77, d=72)
     assert not c["tma_store"] and not c["rows_aligned"]
     assert c["bn"] == 128 and c["dch"] == 2
-    assert cfg(m=64, n=1000, d=256, heads=2)["stages"] == 4
+    assert cfg(m=64, n=1000, d=256, heads=2)["stages"] == 2
+    assert cfg(m=64, n=1000, d=128)["stages"] == 3
 
 
 def test_attention_score_unfused_plan(tmp_path):
@@ -253,6 +254,8 @@ def test_attention_pattern_needs_the_exact_group():
     (k,) = compile_graph(g, dtype="bfloat16")
     assert [sk.family for sk in k.plan.kernels] == ["attn"]
     assert k.plan.kernels[0].config["scale"] == 1.0
+    (k,) = compile_graph(graphs.attention_score(64, 64, 64, scale=-0.5), dtype="bfloat16")
+    assert [sk.family for sk in k.plan.kernels] == ["gemm", "row"]     # max of raw scores needs scale > 0
 
 
 def test_transpose_elsewhere_is_rejected():
@@ -324,3 +327,34 @@ def test_alignment_rules():
     sk = CodeGenerator(tune={"row": {"engine": "tma"}}).generate(g, grp, shapes, dts)
     assert sk.plan.kernels[0].config["engine"] == "tma"
     assert _alignment_rules(sk.plan.kernels[0])[0] == [16, 16, 16]
+
+
+def test_exp2_poly3_error_bound():
+    """The FMA-pipe 2^x of molten/common.cuh, evaluated step by step in fp32
+    exactly as the device does (round-to-nearest adds, fused multiply-adds,
+    exponent added as an integer): relative error below 1e-4 on [-126, 1],
+    and the clamp keeps results positive and tiny below -126."""
+    import numpy as np
+    from molten_b200.build import ENGINE_INCLUDE
+    src = (ENGINE_INCLUDE / "molten" / "common.cuh").read_text()
+    c = [np.float32(float(re.search(rf"#define MOLTEN_EXP2_C{i} ([0-9.e+-]+)f", src).group(1)))
+         for i in range(4)]
+
+    def fma(a, b, d):        # one rounding, as the device's FFMA
+        return np.float32(a.astype(np.float64) * b.astype(np.float64) + d.astype(np.float64))
+
+    x = np.concatenate([np.linspace(-126, 1, 2_000_001, dtype=np.float32),
+                        np.float32(-126) - np.arange(1, 100, dtype=np.float32)])
+    xc = np.maximum(x, np.float32(-126))
+    magic = np.float32(12582912.0)
+    r = (xc + magic).astype(np.float32)
+    f = (xc - (r - magic)).astype(np.float32)
+    p = fma(fma(fma(np.full_like(f, c[3]), f, np.full_like(f, c[2])), f, np.full_like(f, c[1])),
+            f, np.full_like(f, c[0]))
+    bits = (p.view(np.int32).astype(np.int64) + (r.view(np.int32).astype(np.int64) << 23)) % (1 << 32)
+    y = bits.astype(np.uint32).view(np.float32).astype(np.float64)
+    assert np.all(np.abs(f) <= 0.5)
+    ok = x >= -125
+    rel = np.abs(y[ok] / np.exp2(x[ok].astype(np.float64)) - 1)
+    assert rel.max() < 1e-4, rel.max()
+    assert np.all(y[x < -126] >= 0) and np.all(y[x < -126] < 2.0 ** -125)

@@ -501,6 +501,35 @@ def test_multihead_attention_score(rt, h, m, n, d, fused):
                  f"attention {h}x{m}x{n}x{d}")
 
 
+@pytest.mark.parametrize("tune", [{"poly": [12, 12]}, {"poly": [32, 32]}, {"poly": [0, 16]},
+                                  {"sum16": True}, {"sum16": True, "poly": [0, 8]},
+                                  {"sum16": False}],
+                         ids=["poly12", "poly32", "poly0-16", "sum16", "sum16-poly8", "sum32"])
+@pytest.mark.parametrize("h,m,n,d,dtype", [(2, 256, 512, 128, "bfloat16"), (1, 100, 77, 72, "float16"),
+                                           (1, 64, 2000, 64, "float16")])
+def test_fused_attention_exp2_variants(rt, tune, h, m, n, d, dtype):
+    """Exponentials on the FMA pipe (Cody-Waite + a minimax cubic, relative
+    error < 1e-4) and pass-0 row sums from f16 exponential pairs: the same
+    parity bar as the fp32 EX2 path."""
+    from molten_b200.codegen import CodeGenerator
+    g = graphs.attention_score(m, n, d, dtype=dtype, heads=h if h > 1 else None)
+    kern = CodeGenerator(dtype=dtype, tune={"attn": dict(tune)}).generate(
+        g, FusionEngine().fuse(g)[0])
+    c = kern.plan.kernels[0].config
+    assert all(c[k] == v for k, v in tune.items())
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(m * 7 + n)
+    lead = (h,) if h > 1 else ()
+    q = torch.randn(*lead, m, d, generator=gen, device=DEV).to(TORCH_DT[dtype])
+    k = torch.randn(*lead, n, d, generator=gen, device=DEV).to(TORCH_DT[dtype])
+    out = rt.compile(kern)(q, k)
+    torch.cuda.synchronize()
+    assert MoltenRuntime.read_status(0) == 0
+    res = orc.evaluate(g, {"q": to_numpy(q), "k": to_numpy(k)})
+    assert_close(as_f32(out), res[("f32", g.ops[g._outputs[0]].inputs[0])], dtype,
+                 f"attention {tune}")
+
+
 def test_fused_attention_large_logits(rt):
     """Scores far from zero (scale 1, |s| up to ~100): the row maximum is
     subtracted before exponentiation, so nothing overflows and each row's
