@@ -101,7 +101,8 @@ def launch_records(plan: GroupPlan, name: str) -> list:
             rec.update(block=c["block"], vec=c["vec"], slots_per_row=c["spr"], smem=0)
         elif sk.family == "attn":
             rec.update(block=c["threads"], bm=128, bn=c["bn"], stages=c["stages"],
-                       smem=c["smem_bytes"], tma_store=c["tma_store"])
+                       smem=c["smem_bytes"], tma_store=c["tma_store"],
+                       store_cols=c["store_cols"], batch=c["batch"])
         else:
             rec.update(block=c["threads"], bm=c["bm"], bn=c["bn"], bk=c["bk"],
                        stages=c["stages"], smem=c.get("smem_bytes", 0))
