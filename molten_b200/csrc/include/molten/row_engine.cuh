@@ -304,15 +304,29 @@ struct RowTeam {
     s = a + b;
   }
 
+  // Butterfly all-reduce of (max, sum of 2^((x - max) log2e)) pairs over
+  // aligned groups of W lanes, in two phases: the max first, then each lane
+  // rescales its own sum once to the common max and the sums are added --
+  // one EX2 per lane instead of two per butterfly step (merging pairs step by
+  // step, as softmax_combine does, costs 2 log2(W) EX2).  Every lane of a
+  // group ends with the same bits (xor pairing: the same additions, only
+  // commuted).
+  template <int W>
+  __device__ __forceinline__ static void softmax_butterfly(float& m, float& s) {
+    float M = m;
+#pragma unroll
+    for (int off = W / 2; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    float S = (m == -INFINITY) ? 0.0f : s * fast_exp2((m - M) * MOLTEN_LOG2E);
+#pragma unroll
+    for (int off = W / 2; off > 0; off >>= 1) S += __shfl_xor_sync(0xffffffffu, S, off);
+    m = M;
+    s = S;
+  }
+
   // Levels 1-2 of the softmax pair reduction (2 floats per warp of `smem`).
   __device__ __forceinline__ void softmax_cta(float& m, float& s, float* smem) const {
     constexpr int W = TPC < 32 ? TPC : 32;
-#pragma unroll
-    for (int off = W / 2; off > 0; off >>= 1) {
-      const float m2 = __shfl_xor_sync(0xffffffffu, m, off);
-      const float s2 = __shfl_xor_sync(0xffffffffu, s, off);
-      softmax_combine(m, s, m2, s2);
-    }
+    softmax_butterfly<W>(m, s);
     if constexpr (WPR > 1) {
       const int warp = t / 32, lane = t % 32;
       float* red = smem + team * WPR * 2;
@@ -327,12 +341,7 @@ struct RowTeam {
       const int src = lane % P;
       float M = src < WPR ? red[src * 2] : -INFINITY;
       float S = src < WPR ? red[src * 2 + 1] : 0.0f;
-#pragma unroll
-      for (int off = P / 2; off > 0; off >>= 1) {
-        const float m2 = __shfl_xor_sync(0xffffffffu, M, off);
-        const float s2 = __shfl_xor_sync(0xffffffffu, S, off);
-        softmax_combine(M, S, m2, s2);
-      }
+      softmax_butterfly<P>(M, S);
       m = M;
       s = S;
       __syncthreads();
