@@ -22,18 +22,25 @@ def emit_gemm(sk: SubKernel, name: str) -> str:
     needed = set(cfg["needed"])
     L = []
     w = L.append
+    pair = bool(cfg.get("pair"))
     w(f"// Molten sm_100a tcgen05 GEMM + epilogue: {name}")
     w(f"// C[{sk.m}, {sk.n}] = epilogue(A[{sk.m}, {sk.k}] @ B[{sk.k}, {sk.n}]); "
-      f"tile {BM}x{BN}x{BK}, {ST} stages")
-    w("#include \"molten/gemm_sm100.cuh\"")
+      f"tile {BM}x{BN}x{BK}, {ST} stages" + ("; SM pair (cta_group::2)" if pair else ""))
+    w("#include \"molten/gemm2_sm100.cuh\"" if pair else "#include \"molten/gemm_sm100.cuh\"")
     w("")
     w("using namespace molten;")
     w("")
     w("namespace {")
     w(f"constexpr int TILE_M = {BM}, TILE_N = {BN}, TILE_K = {BK}, STAGES = {ST};")
     pro = cfg.get("prologue")
-    w(f"typedef GemmLayout<TILE_M, TILE_N, TILE_K, STAGES, {cfg.get('group_m', 16)}, "
-      f"{'true' if pro else 'false'}> Layout_{name};")
+    if pair:
+        if pro:
+            raise LoweringError("the SM-pair GEMM has no RMSNorm prologue")
+        w(f"typedef Gemm2Layout<TILE_N, STAGES, {cfg.get('group_m', 16)}> Layout_{name};")
+        w(f"static_assert(Layout_{name}::SMEM_BYTES <= {cfg['smem_bytes']}, \"shared memory\");")
+    else:
+        w(f"typedef GemmLayout<TILE_M, TILE_N, TILE_K, STAGES, {cfg.get('group_m', 16)}, "
+          f"{'true' if pro else 'false'}> Layout_{name};")
     if pro:
         wt = DTYPE_CTYPE[pro["w_dtype"]]
         w(f"// RMSNorm prologue: A = x / sqrt(mean(x^2) + eps) * w, normalised as it is staged")
@@ -142,6 +149,16 @@ def emit_gemm(sk: SubKernel, name: str) -> str:
     w(f"extern \"C\" __global__ void __launch_bounds__({cfg['threads']}, 1) "
       f"{name}(const __grid_constant__ GemmArgs args) {{")
     w("  extern __shared__ __align__(1024) uint8_t smem_raw[];")
+    if pair:
+        kmaj = "true" if cfg.get("b_kmajor") else "false"
+        w(f"  const GemmShared sh = gemm2_carve<Layout_{name}>(smem_raw);")
+        w(f"  gemm2_init<Layout_{name}>(sh, args);    // mbarriers, pair TMEM allocation, pair barrier")
+        w("  pdl_enter();                            // no global access before this")
+        w(f"  gemm2_roles<Layout_{name}, {f16in}, Epilogue_{name}, {kmaj}>(sh, args);")
+        w("  __syncthreads();")
+        w(f"  gemm2_teardown<Layout_{name}>(sh);      // pair barrier, pair TMEM release")
+        w("}")
+        return "\n".join(L) + "\n"
     w(f"  const GemmShared sh = gemm_carve<Layout_{name}>(smem_raw);")
     w(f"  gemm_init<Layout_{name}>(sh, args);     // mbarriers + TMEM allocation")
     w("  pdl_enter();                            // no global access before this")

@@ -144,10 +144,20 @@ class _Spec:
             torch = _torch()
             sms = torch.cuda.get_device_properties(device).multi_processor_count
             tiles = c.get("batch", 1) * (-(-sk.m // c["bm"])) * (-(-sk.n // c["bn"]))
-            cfg.grid[:] = [max(1, min(tiles, sms)), 1, 1]
             cfg.block[:] = [128, c["threads"] // 128, 1]
-            cfg.cluster[:] = [1, 1, 1]
             cfg.smem_bytes = c["smem_bytes"]
+            if c.get("pair"):
+                # clusters of 2 CTAs (an SM pair per 256-row tile), persistent
+                cfg.cluster[:] = [2, 1, 1]
+                cfg.grid[:] = [2 * max(1, min(tiles, sms // 2)), 1, 1]
+                _, clusters = self.module(device).max_resident(self.entries[i], cfg)
+                if clusters < 1:
+                    raise _capi.MoltenError(f"kernel {self.entries[i].decode()} cannot be resident "
+                                            f"as a 2-CTA cluster")
+                cfg.grid[:] = [2 * max(1, min(tiles, clusters)), 1, 1]
+            else:
+                cfg.grid[:] = [max(1, min(tiles, sms)), 1, 1]
+                cfg.cluster[:] = [1, 1, 1]
         cfg.flags = _capi.LAUNCH_PDL if PDL else 0
         self._cfgs[key] = cfg
         return cfg
@@ -217,9 +227,10 @@ class _Spec:
                 ctypes.memmove(a.tmap_a, self.tmap(A2, dt, nb * sk.m, sk.k, 64, 128), 128)
                 if sk.config.get("b_kmajor"):
                     # B is the transpose of Bt [(batch x) N, K]: its rows, K-major
+                    # (an SM pair's CTA stages BN/2 of them)
                     B2 = B.reshape(-1, B.shape[-1])
-                    ctypes.memmove(a.tmap_b, self.tmap(B2, dt, nb * sk.n, sk.k, 64, sk.config["bn"]),
-                                   128)
+                    rows_b = sk.config["bn"] // (2 if sk.config.get("pair") else 1)
+                    ctypes.memmove(a.tmap_b, self.tmap(B2, dt, nb * sk.n, sk.k, 64, rows_b), 128)
                 else:
                     B2 = B.reshape(-1, B.shape[-1])
                     ctypes.memmove(a.tmap_b, self.tmap(B2, dt, nb * sk.k, sk.n, 64, 64), 128)

@@ -358,3 +358,21 @@ def test_exp2_poly3_error_bound():
     rel = np.abs(y[ok] / np.exp2(x[ok].astype(np.float64)) - 1)
     assert rel.max() < 1e-4, rel.max()
     assert np.all(y[x < -126] >= 0) and np.all(y[x < -126] < 2.0 ** -125)
+
+
+def test_gemm_sm_pair_plan(tmp_path):
+    """From 1024 stacked rows the GEMM runs on SM pairs (clusters of 2 CTAs,
+    tcgen05.mma.cta_group::2, 256-row tiles); decode-size GEMMs and the
+    RMSNorm prologue keep the one-SM engine."""
+    (k,) = compile_graph(graphs.gemm_bias_gelu(8192, 4096, 14336), dtype="bfloat16")
+    c = k.plan.kernels[0].config
+    assert c["pair"] and c["bm"] == 256 and c["bn"] == 256 and c["smem_bytes"] <= 232448
+    assert "gemm2_roles<" in k.source and "molten/gemm2_sm100.cuh" in k.source
+    assert build_cubin(k.source, k.name, tmp_path).stat().st_size > 1000
+    (k,) = compile_graph(graphs.gemm_bias_gelu(64, 4096, 14336), dtype="bfloat16")
+    assert not k.plan.kernels[0].config["pair"]
+    g = graphs.rmsnorm_gemm(2048, 1024, 1024)
+    k = CodeGenerator(dtype="bfloat16", tune={"gemm": {"prologue": True}}).generate(
+        g, FusionEngine().fuse(g)[0])
+    (sk,) = k.plan.kernels
+    assert sk.config.get("prologue") and not sk.config["pair"]

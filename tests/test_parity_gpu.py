@@ -205,6 +205,48 @@ def test_gemm_shapes(rt, m, k, n):
                  f"gemm {m}x{k}x{n}")
 
 
+@pytest.mark.parametrize("m,k,n,bn,kmajor,batch", [
+    (256, 64, 256, 256, False, 1), (300, 200, 504, 256, False, 1), (1000, 72, 136, 128, False, 1),
+    (513, 1024, 768, 256, False, 1), (2048, 512, 1024, None, False, 1),
+    (300, 512, 384, 256, True, 1), (200, 128, 300, 128, True, 3), (256, 136, 520, 256, False, 2)])
+def test_gemm_sm_pair(rt, m, k, n, bn, kmajor, batch):
+    """The SM-pair engine (cluster of 2 CTAs, tcgen05.mma.cta_group::2, a
+    256-row tile per pair, each CTA staging half of A's rows and half of B's
+    columns): ragged m, n, k, both B majors, stacked problems."""
+    from molten_b200.codegen import CodeGenerator
+    from molten_b200.ir import DataflowGraph, TensorShape as TS
+    lead = [batch] if batch > 1 else []
+    g = DataflowGraph("gemm_pair")
+    a = g.add_input("A", TS(lead + [m, k]), dtype="bfloat16")
+    if kmajor:
+        bt = g.add_input("Bt", TS(lead + [n, k]), dtype="bfloat16")
+        bmat = g.transpose(bt)
+    else:
+        bmat = g.add_input("B", TS(lead + [k, n]), dtype="bfloat16")
+    bias = g.add_input("bias", TS([n]), dtype="bfloat16")
+    g.add_output(g.gelu(g.add(g.matmul(a, bmat), bias)))
+    tune = {"gemm": {"pair": True, **({"bn": bn} if bn else {})}}
+    kern = CodeGenerator(dtype="bfloat16", tune=tune).generate(g, FusionEngine().fuse(g)[0])
+    (sk,) = kern.plan.kernels
+    assert sk.family == "gemm" and sk.config["pair"] and sk.config["b_kmajor"] == kmajor
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(m + 3 * n + k)
+    A = torch.randn(*lead, m, k, generator=gen, device=DEV).to(torch.bfloat16)
+    bshape = (*lead, n, k) if kmajor else (*lead, k, n)
+    B = (torch.randn(*bshape, generator=gen, device=DEV) / k ** 0.5).to(torch.bfloat16)
+    bb = (0.02 * torch.randn(n, generator=gen, device=DEV)).to(torch.bfloat16)
+    ck = rt.compile(kern)
+    out = ck(A, B, bb)
+    out2 = ck(A, B, bb)
+    torch.cuda.synchronize()
+    assert MoltenRuntime.read_status(0) == 0
+    assert torch.equal(out.view(torch.int16), out2.view(torch.int16)), "repeated runs differ"
+    names = ["A", "Bt" if kmajor else "B", "bias"]
+    res = orc.evaluate(g, dict(zip(names, [to_numpy(A), to_numpy(B), to_numpy(bb)])))
+    assert_close(as_f32(out), res[("f32", g.ops[g._outputs[0]].inputs[0])], "bfloat16",
+                 f"pair gemm {batch}x{m}x{k}x{n} bn {bn} kmajor {kmajor}")
+
+
 def test_gemm_plain_matmul_fp16(rt):
     g = graphs.gemm_bias_gelu(256, 256, 256, dtype="float16")
     gen = torch.Generator(device=DEV)
