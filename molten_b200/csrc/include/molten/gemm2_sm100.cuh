@@ -7,15 +7,16 @@
 // whose GemmArgs, epilogue functors and primitives this engine reuses.
 //
 //   warp 0  (both CTAs)  TMA producer: its CTA's A and B halves of each k
-//                        block, completing bytes on the even CTA's `full`
-//                        barrier (cp.async.bulk.tensor .cta_group::2; no
-//                        multicast); the even CTA alone arms `full` for both
+//                        block into its own shared memory, completing bytes
+//                        on the even CTA's `full` barrier (tensor copies with
+//                        .cta_group::2); the even CTA alone arms `full` for both
 //                        CTAs' bytes with a local arrive.expect_tx (a remote,
 //                        cluster-release arrive per stage measured 1.7x
 //                        slower: its fence starved the MMA);
 //   warp 1  (even CTA)   MMA issuer: waits on `full`, issues the pair's
 //                        MMAs, commits `empty` stages and `acc_full`
-//                        buffers to both CTAs (commit .multicast::cluster);
+//                        buffers to both CTAs (one tcgen05.commit with a
+//                        2-CTA mask);
 //   warp 1  (both)       TMEM allocation and release, done collectively by
 //                        the pair (tcgen05.alloc/dealloc .cta_group::2);
 //   warps 4..7 (both)    epilogue of the CTA's 128 rows, releasing an
