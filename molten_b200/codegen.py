@@ -105,7 +105,8 @@ def launch_records(plan: GroupPlan, name: str) -> list:
                        store_cols=c["store_cols"], batch=c["batch"])
         else:
             rec.update(block=c["threads"], bm=c["bm"], bn=c["bn"], bk=c["bk"],
-                       stages=c["stages"], smem=c.get("smem_bytes", 0))
+                       stages=c["stages"], smem=c.get("smem_bytes", 0),
+                       cluster=2 if c.get("pair") else 1)
         recs.append(rec)
     return recs
 
@@ -212,7 +213,8 @@ class CodeGenerator:
                            vectorize=plan.kernels[0].config.get("vec", 8),
                            shared_mem_bytes=smem, dtype=self.dtype,
                            family=fam,
-                           cluster_x=max(sk.config.get("cl", 1) for sk in plan.kernels),
+                           cluster_x=max(sk.config.get("cl", 2 if sk.config.get("pair") else 1)
+                                         for sk in plan.kernels),
                            launches=launch_records(plan, name))
         return GeneratedKernel(name=name, source=source, config=cfg,
                                num_args=len(plan.inputs) + len(plan.outputs) + 1,
