@@ -403,8 +403,11 @@ def run_molten(args, w):
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "ncu_traffic.json")
     try:
-        with open(tpath) as f:
-            traffic = json.load(f).get(w_local.name if not is_gemm else w.name)
+        # captured on the whole single-GPU workload: a column shard's launch
+        # moves a different byte count, so N > 1 GEMM lines carry none
+        if not (is_gemm and world > 1):
+            with open(tpath) as f:
+                traffic = json.load(f).get(w_local.name if not is_gemm else w.name)
     except (OSError, ValueError):
         traffic = None
     roof.update({"achieved": achieved, "peak": peak, "frac": achieved / peak,

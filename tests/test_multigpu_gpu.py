@@ -48,12 +48,14 @@ def _gemm_worker(rank, world, q):
     torch.cuda.set_device(rank)
     dev = f"cuda:{rank}"
     gen = torch.Generator().manual_seed(5)
-    A = torch.randn(512, 256, generator=gen).to(torch.bfloat16)
+    A = torch.randn(1100, 256, generator=gen).to(torch.bfloat16)
     B = (torch.randn(256, 1024, generator=gen) / 16).to(torch.bfloat16)
     bias = (0.02 * torch.randn(1024, generator=gen)).to(torch.bfloat16)
     n0, n1 = col_shards(1024, world)[rank]
-    g = graphs.gemm_bias_gelu(512, 256, n1 - n0)
-    ck = MoltenRuntime().compile(compile_graph(g, dtype="bfloat16")[0])
+    g = graphs.gemm_bias_gelu(1100, 256, n1 - n0)
+    (kern,) = compile_graph(g, dtype="bfloat16")
+    assert kern.plan.kernels[0].config["pair"]          # SM-pair clusters on every rank
+    ck = MoltenRuntime().compile(kern)
     out = ck(A.to(dev), B[:, n0:n1].contiguous().to(dev), bias[n0:n1].contiguous().to(dev))
     torch.cuda.synchronize()
     assert MoltenRuntime.read_status(rank) == 0
@@ -105,10 +107,10 @@ def test_gemm_column_shards_on_two_gpus_match_one_launch(world):
     from molten_b200.runtime import MoltenRuntime
     parts = _run(_gemm_worker, world)
     gen = torch.Generator().manual_seed(5)
-    A = torch.randn(512, 256, generator=gen).to(torch.bfloat16)
+    A = torch.randn(1100, 256, generator=gen).to(torch.bfloat16)
     B = (torch.randn(256, 1024, generator=gen) / 16).to(torch.bfloat16)
     bias = (0.02 * torch.randn(1024, generator=gen)).to(torch.bfloat16)
-    ck = MoltenRuntime().compile(compile_graph(graphs.gemm_bias_gelu(512, 256, 1024),
+    ck = MoltenRuntime().compile(compile_graph(graphs.gemm_bias_gelu(1100, 256, 1024),
                                                dtype="bfloat16")[0])
     whole = ck(A.cuda(), B.cuda(), bias.cuda())
     torch.cuda.synchronize()
