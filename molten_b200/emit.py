@@ -545,6 +545,7 @@ def _emit_row_body(e: _Emitter, closures, reds, smx, materialize, prefetch, mask
         e.w(f"  float m{vid}[NV][VEC];")
     mat_ready = set()
     call = 0
+    early_zero, skip_lim = (), None        # outputs stored early in their masked slots
     for p in range(sk.passes):
         rs = reds[p]
         e.w(f"  // ---- pass {p}: " + ", ".join(f"{values[r].op}(v{values[r].args[0]})"
@@ -557,7 +558,17 @@ def _emit_row_body(e: _Emitter, closures, reds, smx, materialize, prefetch, mask
         if len(smx[p]) == 1 and not rs and not to_mat:
             causal = _causal_softmax_parts(values, smx[p][0], targets)
         if causal is not None:
-            _emit_causal_softmax_pass(e, sk, smx[p][0], causal, targets, prefetch, mat_ready)
+            full = [o for o in sk.outputs if o.kind == "full"]
+            # only where the row's reduction crosses warps (shared memory /
+            # cluster rounds that the zero stores can overlap); a one-warp
+            # row measured slower with them (bf16 x2048 causal 70.9 -> 75.4 us)
+            team = sk.config["tpc"] * sk.config.get("cl", 1)
+            if (p == sk.passes - 1 and full and team > 32
+                    and all(sk.out_values[o.index] == smx[p][0] for o in full)):
+                early_zero = full
+                skip_lim = f"mlim{causal[1]}"
+            _emit_causal_softmax_pass(e, sk, smx[p][0], causal, targets, prefetch, mat_ready,
+                                      early_zero)
         else:
             if smx[p]:
                 _emit_softmax_local_max(e, sk, smx[p], targets, prefetch, mat_ready)
@@ -622,6 +633,8 @@ def _emit_row_body(e: _Emitter, closures, reds, smx, materialize, prefetch, mask
         e.w(f"{ind}for (int k = 0; k < NV; ++k) {{")
         e.w(f"{ind}  const int j = tm.slot(k);")
         e.w(f"{ind}  if (!(rok && j < NVEC)) continue;")
+        if skip_lim:
+            e.w(f"{ind}  if (j * VEC > {skip_lim}) continue;         // stored before the reductions")
         _emit_nonprefetched_loads(e, fin, prefetch, ind + "  ")
         for o in full_outs:
             e.w(f"{ind}  float f{o.index}[VEC];")
@@ -1137,11 +1150,14 @@ def _causal_softmax_parts(values, v: int, targets):
 
 
 def _emit_causal_softmax_pass(e: _Emitter, sk: SubKernel, v: int, parts, targets, prefetch,
-                              mat_ready):
+                              mat_ready, early_zero=()):
     """Softmax of a + causal mask, classifying each slot once: columns
     c0 .. c0+VEC-1 all above the row's limit (exponentials are 0, nothing is
     computed), all at or below it (no mask arithmetic), or straddling it (the
-    one boundary slot of the row, checked per element)."""
+    one boundary slot of the row, checked per element).  ``early_zero``:
+    outputs that are this softmax itself -- their fully masked slots are 0
+    whatever the row's statistics, so they are stored here, before the
+    row's reductions, and the output pass skips them."""
     values = sk.values
     VEC = sk.config["vec"]
     a, mk = parts
@@ -1192,6 +1208,10 @@ def _emit_causal_softmax_pass(e: _Emitter, sk: SubKernel, v: int, parts, targets
     e.w(f"    if (c0 > {lim}) {{")
     e.w("#pragma unroll")
     e.w(f"      for (int e = 0; e < VEC; ++e) m{v}[k][e] = 0.0f;")
+    for o in early_zero:
+        ct = _ctype(o.dtype)
+        e.w(f"      {{ Slot<{ct}, VEC> z; const float zf[VEC] = {{}}; pack_slot<{ct}, VEC>(z, zf);")
+        e.w(f"        store_slot<kStoreDefault, {ct}, VEC>(out{o.index} + j * VEC, z); }}")
     e.w("      continue;")
     e.w("    }")
     _emit_nonprefetched_loads(e, a_targets, prefetch, "    ")
