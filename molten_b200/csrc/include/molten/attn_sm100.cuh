@@ -16,7 +16,7 @@
 //               a resident area, then per pass and column block the K tiles
 //               ({64, BN} boxes of K's rows) through a STAGES-deep ring;
 //   warp 1      TMEM owner + MMA issuer (tcgen05.mma.cta_group::1.kind::f16,
-//               fp32 accumulators double-buffered in TMEM);
+//               fp32 accumulators in 2 or 4 TMEM buffers of BN columns);
 //   warps 4..   epilogue: EPI_WARPS / 4 warps per TMEM lane quarter
 //               (warp % 4), in GROUPS groups that take alternate tiles (so
 //               group g always reads accumulator buffer g: one group's TMEM
@@ -76,9 +76,13 @@ struct AttnLayout {
   static constexpr int OUT_BUFS = EPI_WARPS <= 8 ? 2 : 1;   // staging tiles per warp
   static constexpr int OUT_BYTES = EPI_WARPS * OUT_BUFS * OUT_TILE;
   static constexpr int STAT_BYTES = 2 * EPI_WARPS * 32 * 8;  // (max, sum) per row and slot, x2
-  static constexpr int TMEM_COLS = (2 * BN <= 128) ? 128 : ((2 * BN <= 256) ? 256 : 512);
-  // barriers: full[S], empty[S], acc_full[2], acc_empty[2], q_full, q_empty, done, stat[4]
-  static constexpr int NUM_BARS = 2 * STAGES + 11;
+  // accumulator buffers: as many BN-column tiles as TMEM holds (at most 4),
+  // so the MMA can run up to ACC_BUFS - 1 tiles ahead of the epilogue
+  static constexpr int ACC_BUFS = (4 * BN <= 512) ? 4 : 2;
+  static constexpr int TMEM_COLS = (ACC_BUFS * BN <= 256) ? 256 : 512;
+  static_assert(ACC_BUFS * BN <= 512, "accumulators fit TMEM");
+  // barriers: full[S], empty[S], acc_full[B], acc_empty[B], q_full, q_empty, done, stat[4]
+  static constexpr int NUM_BARS = 2 * STAGES + 2 * ACC_BUFS + 7;
   static constexpr int OUT_OFFSET = Q_BYTES + STAGES * STAGE_BYTES;
   static constexpr int STAT_OFFSET = OUT_OFFSET + OUT_BYTES;
   static constexpr int BAR_OFFSET = STAT_OFFSET + STAT_BYTES;
@@ -91,12 +95,13 @@ template <class L> struct AttnBars {
   __device__ __forceinline__ explicit AttnBars(uint32_t b) : base(b) {}
   __device__ __forceinline__ uint32_t full(int i) const { return base + 8u * i; }
   __device__ __forceinline__ uint32_t empty(int i) const { return base + 8u * (L::STAGES + i); }
-  __device__ __forceinline__ uint32_t acc_full(int b) const { return base + 8u * (2 * L::STAGES + b); }
-  __device__ __forceinline__ uint32_t acc_empty(int b) const { return base + 8u * (2 * L::STAGES + 2 + b); }
-  __device__ __forceinline__ uint32_t q_full() const { return base + 8u * (2 * L::STAGES + 4); }
-  __device__ __forceinline__ uint32_t q_empty() const { return base + 8u * (2 * L::STAGES + 5); }
-  __device__ __forceinline__ uint32_t done() const { return base + 8u * (2 * L::STAGES + 6); }
-  __device__ __forceinline__ uint32_t stat(int quarter) const { return base + 8u * (2 * L::STAGES + 7 + quarter); }
+  static constexpr int A0 = 2 * L::STAGES, B2 = 2 * L::ACC_BUFS;
+  __device__ __forceinline__ uint32_t acc_full(int b) const { return base + 8u * (A0 + b); }
+  __device__ __forceinline__ uint32_t acc_empty(int b) const { return base + 8u * (A0 + L::ACC_BUFS + b); }
+  __device__ __forceinline__ uint32_t q_full() const { return base + 8u * (A0 + B2); }
+  __device__ __forceinline__ uint32_t q_empty() const { return base + 8u * (A0 + B2 + 1); }
+  __device__ __forceinline__ uint32_t done() const { return base + 8u * (A0 + B2 + 2); }
+  __device__ __forceinline__ uint32_t stat(int quarter) const { return base + 8u * (A0 + B2 + 3 + quarter); }
 };
 
 struct AttnShared {
@@ -134,7 +139,7 @@ __device__ __forceinline__ void attn_init(const AttnShared& s, const AttnArgs& a
   if (tid == 0) {
     const AttnBars<L> b(s.bars);
     for (int i = 0; i < L::STAGES; ++i) { mbar_init(b.full(i), 1); mbar_init(b.empty(i), 1); }
-    for (int i = 0; i < 2; ++i) { mbar_init(b.acc_full(i), 1); mbar_init(b.acc_empty(i), L::RELEASERS); }
+    for (int i = 0; i < L::ACC_BUFS; ++i) { mbar_init(b.acc_full(i), 1); mbar_init(b.acc_empty(i), L::RELEASERS); }
     mbar_init(b.q_full(), 1);
     mbar_init(b.q_empty(), 1);
     mbar_init(b.done(), 1);
@@ -233,6 +238,24 @@ __device__ __forceinline__ float attn_exp2(int i, float x) {
   return (i % 32) >= 32 - POLY ? exp2_poly3(x) : fast_exp2(x);
 }
 
+// Packed fp32 pairs (one FFMA2 / FADD2 instruction for two lanes of work).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
 // Two f16 exponentials per EX2 instruction: x rounded to f16, 2^x in f16
 // (ex2.approx.f16x2), the pair summed as f16x2.
 __device__ __forceinline__ uint32_t f16x2_pack(float lo, float hi) {
@@ -263,7 +286,7 @@ __device__ __forceinline__ float f16x2_sum_f32(uint32_t x) {
 // partial sums within 2^-9, the rest in fp32) -- the sum only scales the
 // row, so its error reaches every output of the row as one factor of about
 // 1 + 1e-3 at worst.
-template <int N, int POLY, bool MASK, bool SUM16 = false>
+template <int N, int POLY, bool MASK, bool SUM16 = false, bool X2 = false>
 __device__ __forceinline__ void attn_stats(float (&a)[N], int valid, float C2, float& mx, float& sum) {
   constexpr int K = 8;                             // independent chains
   if constexpr (MASK) {
@@ -304,10 +327,25 @@ __device__ __forceinline__ void attn_stats(float (&a)[N], int valid, float C2, f
     return;
   }
   float t[K];
+  if constexpr (X2) {
+    // arguments and sums in packed pairs: K/2 chains of (even, odd) columns
+    float2 t2[K / 2];
 #pragma unroll
-  for (int j = 0; j < K; ++j) t[j] = 0.0f;
+    for (int j = 0; j < K / 2; ++j) t2[j] = make_float2(0.0f, 0.0f);
 #pragma unroll
-  for (int i = 0; i < N; ++i) t[i % K] += attn_exp2<POLY>(i, fmaf(a[i], C2, off));   // 2^-inf = 0
+    for (int i = 0; i < N; i += 2) {
+      const float2 x = ffma2(make_float2(a[i], a[i + 1]), make_float2(C2, C2), make_float2(off, off));
+      t2[(i / 2) % (K / 2)] = fadd2(t2[(i / 2) % (K / 2)],
+                                    make_float2(attn_exp2<POLY>(i, x.x), attn_exp2<POLY>(i + 1, x.y)));
+    }
+#pragma unroll
+    for (int j = 0; j < K / 2; ++j) { t[2 * j] = t2[j].x; t[2 * j + 1] = t2[j].y; }
+  } else {
+#pragma unroll
+    for (int j = 0; j < K; ++j) t[j] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < N; ++i) t[i % K] += attn_exp2<POLY>(i, fmaf(a[i], C2, off));   // 2^-inf = 0
+  }
 #pragma unroll
   for (int w = K / 2; w >= 1; w /= 2) {
 #pragma unroll
@@ -324,9 +362,10 @@ __device__ __forceinline__ void attn_stats(float (&a)[N], int valid, float C2, f
 // (n * 2 % 16 == 0), element by element otherwise.  C2 = scale * log2(e).
 // POLY0 / POLY1: of every 32 exponentials, how many pass 0 / pass 1
 // computes on the FMA pipe.  SUM16: pass-0 sums from f16 exponential pairs.
+// X2: exponent arguments and pass-0 sums as packed fp32 pairs (FFMA2/FADD2).
 // batch * m and batch * n are below 2^31.
 template <class L, bool F16IN, typename OT, bool TMA_STORE, bool ROWS_ALIGNED, int POLY0 = 0,
-          int POLY1 = 0, bool SUM16 = false>
+          int POLY1 = 0, bool SUM16 = false, bool X2 = false>
 __device__ __forceinline__ void attn_roles(const AttnShared& s, const AttnArgs& args, float C2) {
   tc_fence_after();
   const int tid = gemm_tid(), warp = tid / 32, lane = tid % 32;
@@ -395,8 +434,8 @@ __device__ __forceinline__ void attn_roles(const AttnShared& s, const AttnArgs& 
         tc_fence_after();
         for (int pass = 0; pass < 2 && ok; ++pass) {
           for (int nb = 0; nb < NB && ok; ++nb, ++tile) {
-            const int b = (int)(tile & 1u);
-            const uint32_t acc_ph = (tile >> 1) & 1u;
+            const int b = (int)(tile % (uint32_t)L::ACC_BUFS);
+            const uint32_t acc_ph = (tile / (uint32_t)L::ACC_BUFS) & 1u;
             if (!attn_wait(bar.acc_empty(b), acc_ph ^ 1u)) { attn_fail(s, args); ok = false; break; }
             tc_fence_after();
             const uint32_t d = tmem + (uint32_t)(b * L::BN);
@@ -440,9 +479,9 @@ __device__ __forceinline__ void attn_roles(const AttnShared& s, const AttnArgs& 
       // ---- pass 0: row statistics
       float mx = -INFINITY, sum = 0.0f;            // raw-score max; sum of 2^((s - mx) * C2)
       for (int nb = 0; nb < NB; ++nb, ++tile) {
-        const int b = (int)(tile & 1u);
-        if (L::GROUPS == 2 && b != group) continue;              // the other group's tile
-        const bool got = attn_wait(bar.acc_full(b), (tile >> 1) & 1u);
+        const int b = (int)(tile % (uint32_t)L::ACC_BUFS);
+        if (L::GROUPS == 2 && (b % 2) != group) continue;        // the other group's tile
+        const bool got = attn_wait(bar.acc_full(b), (tile / (uint32_t)L::ACC_BUFS) & 1u);
         if (!__all_sync(0xffffffffu, got ? 1 : 0)) {
           if (lane == 0) attn_fail(s, args);
           ok = false;
@@ -456,8 +495,8 @@ __device__ __forceinline__ void attn_roles(const AttnShared& s, const AttnArgs& 
           if (col0 >= N) break;                                  // warp-uniform
           float a[LC];
           tmem_ld_cols<LC>(lane_tmem + (uint32_t)(b * L::BN + u * LC), a);
-          if (nb < nb_full) attn_stats<LC, POLY0, false, SUM16>(a, LC, C2, mx, sum);
-          else attn_stats<LC, POLY0, true, SUM16>(a, N - col0, C2, mx, sum);
+          if (nb < nb_full) attn_stats<LC, POLY0, false, SUM16, X2>(a, LC, C2, mx, sum);
+          else attn_stats<LC, POLY0, true, SUM16, X2>(a, N - col0, C2, mx, sum);
         }
         tc_fence_before();
         __syncwarp();
@@ -493,9 +532,9 @@ __device__ __forceinline__ void attn_roles(const AttnShared& s, const AttnArgs& 
       }
       // ---- pass 1: probabilities
       for (int nb = 0; nb < NB; ++nb, ++tile) {
-        const int b = (int)(tile & 1u);
-        if (L::GROUPS == 2 && b != group) continue;              // the other group's tile
-        const bool got = attn_wait(bar.acc_full(b), (tile >> 1) & 1u);
+        const int b = (int)(tile % (uint32_t)L::ACC_BUFS);
+        if (L::GROUPS == 2 && (b % 2) != group) continue;        // the other group's tile
+        const bool got = attn_wait(bar.acc_full(b), (tile / (uint32_t)L::ACC_BUFS) & 1u);
         if (!__all_sync(0xffffffffu, got ? 1 : 0)) {
           if (lane == 0) attn_fail(s, args);
           ok = false;
@@ -509,8 +548,18 @@ __device__ __forceinline__ void attn_roles(const AttnShared& s, const AttnArgs& 
           if (col0 >= N) break;                                  // warp-uniform
           float a[LC];
           tmem_ld_cols<LC>(lane_tmem + (uint32_t)(b * L::BN + u * LC), a);
+          if constexpr (X2) {
 #pragma unroll
-          for (int i = 0; i < LC; ++i) a[i] = attn_exp2<POLY1>(i, fmaf(a[i], C2, -lse));
+            for (int i = 0; i < LC; i += 2) {
+              const float2 x = ffma2(make_float2(a[i], a[i + 1]), make_float2(C2, C2),
+                                     make_float2(-lse, -lse));
+              a[i] = attn_exp2<POLY1>(i, x.x);
+              a[i + 1] = attn_exp2<POLY1>(i + 1, x.y);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < LC; ++i) a[i] = attn_exp2<POLY1>(i, fmaf(a[i], C2, -lse));
+          }
           if constexpr (TMA_STORE) {
             if (qrow0 >= M) continue;                            // warp-uniform
             const uint32_t tile_addr = stage0 + (uint32_t)(sbuf * L::OUT_TILE);

@@ -18,6 +18,7 @@ DEFAULT_SYMBOLIC_DIM = 1024
 ATTN_SMEM_LIMIT = 232448          # dynamic shared memory one sm_100 CTA may opt into
 ATTN_POLY = (0, 0)                # exponentials per 32 on the FMA pipe (pass 0, pass 1)
 ATTN_SUM16 = False                # pass-0 row sums from f16 exponential pairs
+ATTN_X2 = False                   # packed fp32 pairs for exponent arguments and sums
 
 
 def declared_shape(op, symbols: dict) -> tuple:
@@ -345,9 +346,11 @@ def _plan_attn(graph, ops, outs, shapes, dts, tune) -> SubKernel:
     scols = 64 if (bn // parts) % 64 == 0 else 32
     out_bytes = epi * (2 if epi <= 8 else 1) * 32 * scols * 2
     q_bytes, stage, stat_bytes = dch * 128 * 128, bn * 128, 2 * epi * 32 * 8
+    acc_bufs = 4 if 4 * bn <= 512 else 2                  # TMEM accumulator buffers
     fit = (ATTN_SMEM_LIMIT - 2048 - out_bytes - stat_bytes - q_bytes) // stage
     stages = int(o.get("stages") or max(2, min(8, fit)))
-    smem = q_bytes + stages * stage + out_bytes + stat_bytes + (2 * stages + 11) * 8 + 16 + 1024
+    smem = (q_bytes + stages * stage + out_bytes + stat_bytes + (2 * stages + 2 * acc_bufs + 7) * 8
+            + 16 + 1024)
     if smem > ATTN_SMEM_LIMIT:
         raise LoweringError(f"attention tile needs {smem} bytes of shared memory")
     rows_aligned = (N * 2) % 16 == 0
@@ -363,7 +366,7 @@ def _plan_attn(graph, ops, outs, shapes, dts, tune) -> SubKernel:
                  "threads": 32 * (4 + epi), "epi_warps": epi, "groups": groups,
                  "scale": scale, "batch": int(batch), "rows_aligned": rows_aligned,
                  "tma_store": tma_store, "poly": poly, "store_cols": scols,
-                 "sum16": bool(o.get("sum16", ATTN_SUM16))}
+                 "sum16": bool(o.get("sum16", ATTN_SUM16)), "x2": bool(o.get("x2", ATTN_X2))}
     return sk
 
 

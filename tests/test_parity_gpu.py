@@ -545,8 +545,10 @@ def test_multihead_attention_score(rt, h, m, n, d, fused):
 
 @pytest.mark.parametrize("tune", [{"poly": [12, 12]}, {"poly": [32, 32]}, {"poly": [0, 16]},
                                   {"sum16": True}, {"sum16": True, "poly": [0, 8]},
-                                  {"sum16": False}],
-                         ids=["poly12", "poly32", "poly0-16", "sum16", "sum16-poly8", "sum32"])
+                                  {"sum16": False}, {"x2": True}, {"x2": True, "poly": [4, 8]},
+                                  {"bn": 128}, {"bn": 128, "groups": 2}, {"bn": 64}],
+                         ids=["poly12", "poly32", "poly0-16", "sum16", "sum16-poly8", "sum32",
+                              "x2", "x2-poly", "bn128-4buf", "bn128-groups", "bn64-4buf"])
 @pytest.mark.parametrize("h,m,n,d,dtype", [(2, 256, 512, 128, "bfloat16"), (1, 100, 77, 72, "float16"),
                                            (1, 64, 2000, 64, "float16")])
 def test_fused_attention_exp2_variants(rt, tune, h, m, n, d, dtype):
