@@ -417,6 +417,122 @@ class CompiledKernel:
         """The GeneratedKernel that a call with these tensors runs."""
         return self._spec_for(list(tensors)).gk
 
+    # -- host buffers ---------------------------------------------------
+    def row_chunkable(self, tensors) -> Optional[list]:
+        """Which of these (host) inputs are split by rows in ``run_host``:
+        a list of flags when every output is 2-D [R, C] and every input is
+        either 2-D [R, C'] (one row per output row) or has no row dimension
+        (1-D, or all leading dims 1), and every sub-kernel is a row,
+        elementwise or GEMM kernel (rows of the GEMM = rows of A); else None."""
+        plan = self.kernel.plan
+        if any(sk.family not in ("row", "ew", "gemm") for sk in plan.kernels):
+            return None
+        if any(len(s) != 2 for s in plan.output_shapes):
+            return None
+        rows = plan.output_shapes[0][0]
+        # a GEMM's B goes up whole (its rows are K, not the output's rows)
+        gemm_b = {sk.operands[sk.b_operand].op_id for sk in plan.kernels if sk.family == "gemm"}
+        flags = []
+        for op_id, t in zip(plan.inputs, tensors):
+            s = tuple(t.shape)
+            if op_id in gemm_b:
+                flags.append(False)
+            elif len(s) == 2 and s[0] == rows and rows > 1:
+                flags.append(True)
+            elif all(d == 1 for d in s[:-1]) or len(s) <= 1:
+                flags.append(False)
+            else:
+                return None
+        return flags if any(flags) else None
+
+    def run_host(self, *tensors, out=None, chunks: int = 8, row_offset: int = 0, device=None):
+        """Host tensors in, host outputs back.  Row-indexed inputs are split
+        into ``chunks`` blocks of rows; each block's upload, kernel and
+        download run on three streams of ``device`` so that block i+1's
+        upload, block i's kernel and block i-1's download overlap (PCIe is
+        full duplex), through two device slots per tensor.  Inputs without a
+        row dimension go up once per call.  Pinned host memory makes the
+        copies asynchronous.  Returns the host output(s); the current stream
+        of ``device`` waits for all of it, so events recorded on it around
+        the call time the whole transfer.  Graphs that do not split by rows
+        (see ``row_chunkable``) run as one block."""
+        torch = _torch()
+        dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+        plan = self.kernel.plan
+        flags = self.row_chunkable(tensors) if chunks > 1 else None
+        if flags is None:
+            # one block: upload everything, run, download (any output shape)
+            cur = torch.cuda.current_stream(dev)
+            dev_in = [t.to(dev, non_blocking=True) for t in tensors]
+            res = self(*dev_in, stream=cur.cuda_stream, row_offset=row_offset)
+            res = list(res) if isinstance(res, tuple) else [res]
+            if out is None:
+                out = [torch.empty(tuple(r.shape), dtype=r.dtype, pin_memory=True) for r in res]
+            outs = list(out) if isinstance(out, (list, tuple)) else [out]
+            for o, r in zip(outs, res):
+                o.copy_(r, non_blocking=True)
+            return outs[0] if len(outs) == 1 else tuple(outs)
+        rows = plan.output_shapes[0][0]
+        chunks = max(1, min(int(chunks), rows))
+        bounds = [(rows * i // chunks, rows * (i + 1) // chunks) for i in range(chunks)]
+        bounds = [b for b in bounds if b[1] > b[0]]
+        rmax = max(b1 - b0 for b0, b1 in bounds)
+        if out is None:
+            out = [torch.empty(tuple(s), dtype=d, pin_memory=True)
+                   for s, d in zip(plan.output_shapes, [_torch_dtype(x) for x in plan.output_dtypes])]
+        outs = list(out) if isinstance(out, (list, tuple)) else [out]
+        one = len(bounds) == 1
+        # device slots: two per row-split tensor, one per whole input
+        dev_whole = [None if f else torch.empty(tuple(t.shape), dtype=t.dtype, device=dev)
+                     for t, f in zip(tensors, flags)]
+        nslot = 1 if one else 2
+        dev_split = [[torch.empty((rmax, t.shape[1]), dtype=t.dtype, device=dev)
+                      for _ in range(nslot)] if f else None for t, f in zip(tensors, flags)]
+        dev_out = [[torch.empty((rmax, o.shape[1]), dtype=o.dtype, device=dev)
+                    for _ in range(nslot)] for o in outs]
+        cur = torch.cuda.current_stream(dev)
+        s_up, s_run, s_down = (torch.cuda.Stream(dev) for _ in range(3))
+        for s in (s_up, s_run, s_down):
+            s.wait_stream(cur)
+        with torch.cuda.stream(s_up):
+            for t, d in zip(tensors, dev_whole):
+                if d is not None:
+                    d.copy_(t, non_blocking=True)
+        ev_up, ev_run, ev_down = [], [], []
+        for i, (r0, r1) in enumerate(bounds):
+            slot, n = i % nslot, r1 - r0
+            with torch.cuda.stream(s_up):
+                if i >= nslot:
+                    s_up.wait_event(ev_run[i - nslot])        # the slot's inputs were consumed
+                for t, d in zip(tensors, dev_split):
+                    if d is not None:
+                        d[slot][:n].copy_(t[r0:r1], non_blocking=True)
+                ev_up.append(torch.cuda.Event())
+                ev_up[-1].record(s_up)
+            with torch.cuda.stream(s_run):
+                s_run.wait_event(ev_up[i])
+                if i >= nslot:
+                    s_run.wait_event(ev_down[i - nslot])      # the slot's outputs were read back
+                args = [w if w is not None else d[slot][:n] for w, d in zip(dev_whole, dev_split)]
+                self(*args, out=[o[slot][:n] for o in dev_out], stream=s_run.cuda_stream,
+                     row_offset=row_offset + r0)
+                ev_run.append(torch.cuda.Event())
+                ev_run[-1].record(s_run)
+            with torch.cuda.stream(s_down):
+                s_down.wait_event(ev_run[i])
+                for o, d in zip(outs, dev_out):
+                    o[r0:r1].copy_(d[slot][:n], non_blocking=True)
+                ev_down.append(torch.cuda.Event())
+                ev_down[-1].record(s_down)
+        cur.wait_stream(s_down)
+        # the device buffers are freed when the last stream using them is done
+        for t in [*dev_whole, *[x for d in dev_split if d for x in d], *[x for d in dev_out for x in d]]:
+            if t is not None:
+                t.record_stream(s_up)
+                t.record_stream(s_run)
+                t.record_stream(s_down)
+        return outs[0] if len(outs) == 1 else tuple(outs)
+
 
 class MoltenRuntime:
     """Builds generated kernels into cubins and hands out callables."""

@@ -202,7 +202,7 @@ def test_attention_score_plan(tmp_path):
     c = sk.config
     assert c["bn"] == 256 and c["dch"] == 2 and c["tma_store"] and c["batch"] == 1
     assert c["smem_bytes"] <= 232448 and abs(c["scale"] - 128 ** -0.5) < 1e-12
-    assert "attn_roles<" in k.source and ", bf16, true, true, 0, 0, false>(sh, args," in k.source
+    assert "attn_roles<" in k.source and ", bf16, true, true, 0, 0, false, false>(sh, args," in k.source
     rec = k.config.launches[0]
     assert rec["family"] == "attn" and rec["smem"] == c["smem_bytes"]
     assert build_cubin(k.source, k.name, tmp_path).stat().st_size > 1000
@@ -376,3 +376,21 @@ def test_gemm_sm_pair_plan(tmp_path):
         g, FusionEngine().fuse(g)[0])
     (sk,) = k.plan.kernels
     assert sk.config.get("prologue") and not sk.config["pair"]
+
+
+def test_run_host_row_split_rules():
+    """run_host splits 2-D row-indexed inputs by rows; row-invariant inputs
+    (weights, GEMM B) go up whole; attention and 4-D RoPE run as one block."""
+    import torch
+    from molten_b200.runtime import CompiledKernel
+
+    def flags(g, tensors, dtype="bfloat16"):
+        (k,) = compile_graph(g, dtype=dtype)
+        return CompiledKernel(name=k.name, source=k.source, config=k.config, kernel=k).row_chunkable(tensors)
+
+    e = lambda *s: torch.empty(*s)
+    assert flags(graphs.rmsnorm_silu_gate(64, 256), [e(64, 256), e(256), e(64, 256)]) == [True, False, True]
+    assert flags(graphs.softmax((96, 256), causal=True), [e(96, 256)], "float32") == [True]
+    assert flags(graphs.gemm_bias_gelu(128, 64, 64), [e(128, 64), e(64, 64), e(64)]) == [True, False, False]
+    assert flags(graphs.attention_score(64, 64, 64), [e(64, 64), e(64, 64)]) is None
+    assert flags(graphs.rope(1, 16, 4, 128), [e(1, 16, 4, 128), e(16, 64), e(16, 64)]) is None

@@ -793,6 +793,42 @@ def test_multi_kernel_group_gemm_then_softmax(rt):
     assert_close(as_f32(out), res[("f32", g.ops[g._outputs[0]].inputs[0])], "bfloat16", "scores")
 
 
+@pytest.mark.parametrize("case", ["rms_silu", "softmax_causal", "gemm", "attention"])
+def test_run_host_matches_one_device_call(rt, case):
+    """Host buffers in and out, rows split into chunks whose uploads,
+    kernels and downloads overlap on three streams (each chunk launched with
+    its global row offset): bit-identical to one call on device tensors."""
+    gen = torch.Generator().manual_seed(21)
+    bf = torch.bfloat16
+    if case == "rms_silu":
+        g = graphs.rmsnorm_silu_gate(1000, 3584)
+        xs = [torch.randn(1000, 3584, generator=gen).to(bf), (1 + 0.1 * torch.randn(3584, generator=gen)).to(bf),
+              torch.randn(1000, 3584, generator=gen).to(bf)]
+        dt = "bfloat16"
+    elif case == "softmax_causal":
+        g = graphs.softmax((999, 2048), causal=True)
+        xs = [3 * torch.randn(999, 2048, generator=gen)]
+        dt = "float32"
+    elif case == "gemm":
+        g = graphs.gemm_bias_gelu(1100, 256, 512)
+        xs = [torch.randn(1100, 256, generator=gen).to(bf), (torch.randn(256, 512, generator=gen) / 16).to(bf),
+              (0.02 * torch.randn(512, generator=gen)).to(bf)]
+        dt = "bfloat16"
+    else:
+        g = graphs.attention_score(256, 512, 128, heads=2)
+        xs = [torch.randn(2, 256, 128, generator=gen).to(bf), torch.randn(2, 512, 128, generator=gen).to(bf)]
+        dt = "bfloat16"
+    ck = rt.compile(compile_graph(g, dtype=dt)[0])
+    whole = ck(*[t.to(DEV) for t in xs])
+    host = [t.pin_memory() for t in xs]
+    got = ck.run_host(*host, chunks=4, device=0)
+    torch.cuda.synchronize()
+    assert not got.is_cuda and got.shape == whole.shape
+    w = whole.cpu()
+    assert torch.equal(got.view(torch.int16) if got.dtype == bf else got, w.view(torch.int16) if w.dtype == bf else w)
+    assert MoltenRuntime.read_status(0) == 0
+
+
 def test_wrong_inputs_raise(rt):
     g = graphs.rmsnorm(4, 64)
     ck = rt.compile(compile_graph(g)[0])
