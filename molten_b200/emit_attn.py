@@ -45,7 +45,7 @@ def emit_attn(sk: SubKernel, name: str) -> str:
     w("  __syncthreads();")
     w(f"  attn_roles<Layout_{name}, {f16in}, {ot}, {'true' if c['tma_store'] else 'false'}, "
       f"{'true' if c['rows_aligned'] else 'false'}, {c['poly'][0]}, {c['poly'][1]}, "
-      f"{'true' if c['sum16'] else 'false'}>"
+      f"{'true' if c['sum16'] else 'false'}, {'true' if c['x2'] else 'false'}>"
       f"(sh, args, {c_float(c2)});")
     w("  __syncthreads();")
     w(f"  attn_teardown<Layout_{name}>(sh);       // TMEM release")
