@@ -167,18 +167,26 @@ def time_cpu(w, budget_s: float, threads: int):
     sw = cpu_sample(w)
     xs = workloads.make_inputs(sw, seed=0, device="cpu")
     params = dict(sw.params)
+    # memory-bound kinds: rotate over distinct copies of the sample, ~1 GB in
+    # all, so that calls stream from host DRAM as the full workload would
+    # instead of re-reading a sample that sits in the last-level cache
+    sets = [xs]
+    if w.kind not in workloads.GEMM_KINDS:
+        nbytes = max(1, sum(t.numel() * t.element_size() for t in xs))
+        sets += [[t.clone() for t in xs] for _ in range(min(47, -(-(1 << 30) // nbytes)) - 1)]
     torch_cpu.run_workload(sw.kind, xs, params)          # warm-up
     times = []
     t_end = time.perf_counter() + budget_s
     while time.perf_counter() < t_end or len(times) < 3:
         t0 = time.perf_counter()
-        torch_cpu.run_workload(sw.kind, xs, params)
+        torch_cpu.run_workload(sw.kind, sets[len(times) % len(sets)], params)
         times.append(time.perf_counter() - t0)
         if len(times) >= 200:
             break
     t = statistics.median(times)
     work = sw.flops_per_call if w.kind in workloads.GEMM_KINDS else sw.bytes_per_call
-    desc = f"{sw.kind} {sw.params} {sw.dtype}, median of {len(times)} calls"
+    desc = (f"{sw.kind} {sw.params} {sw.dtype}, median of {len(times)} calls"
+            + (f" over {len(sets)} rotating input copies" if len(sets) > 1 else ""))
     return work / t, desc, t
 
 
