@@ -314,6 +314,10 @@ def _alignment_rules(sk):
     return ins, outs
 
 
+class _HostPlan:
+    """State ``CompiledKernel.run_host`` keeps per device and shapes."""
+
+
 @dataclass
 class CompiledKernel:
     """A generated kernel bound to its cubin; call it with CUDA tensors."""
@@ -324,6 +328,7 @@ class CompiledKernel:
     kernel: Optional[GeneratedKernel] = None
     runtime: Optional["MoltenRuntime"] = None
     _specs: dict = field(default_factory=dict)
+    _hosts: dict = field(default_factory=dict)
 
     def __call__(self, *tensors, out=None, stream=None, row_offset: int = 0):
         if self.kernel is None or self.runtime is None:
@@ -445,6 +450,38 @@ class CompiledKernel:
                 return None
         return flags if any(flags) else None
 
+    def _host_plan(self, dev, tensors, flags, outs, chunks):
+        """Streams, device slots and events of ``run_host`` for one device and
+        one set of shapes, kept across calls (each call's work waits for the
+        previous call's downloads before reusing the slots)."""
+        torch = _torch()
+        key = (dev.index, tuple((tuple(t.shape), t.dtype) for t in tensors),
+               tuple((tuple(o.shape), o.dtype) for o in outs), chunks)
+        hp = self._hosts.get(key)
+        if hp is not None:
+            return hp
+        rows = outs[0].shape[0]
+        bounds = [(rows * i // chunks, rows * (i + 1) // chunks) for i in range(chunks)]
+        bounds = [b for b in bounds if b[1] > b[0]]
+        rmax = max(b1 - b0 for b0, b1 in bounds)
+        nslot = 1 if len(bounds) == 1 else 2
+        hp = _HostPlan()
+        hp.bounds, hp.nslot, hp.last = bounds, nslot, None
+        hp.dev_whole = [None if f else torch.empty(tuple(t.shape), dtype=t.dtype, device=dev)
+                        for t, f in zip(tensors, flags)]
+        hp.dev_split = [[torch.empty((rmax, t.shape[1]), dtype=t.dtype, device=dev)
+                         for _ in range(nslot)] if f else None for t, f in zip(tensors, flags)]
+        hp.dev_out = [[torch.empty((rmax, o.shape[1]), dtype=o.dtype, device=dev)
+                       for _ in range(nslot)] for o in outs]
+        hp.streams = tuple(torch.cuda.Stream(dev) for _ in range(3))
+        hp.ev_up = [torch.cuda.Event() for _ in bounds]
+        hp.ev_run = [torch.cuda.Event() for _ in bounds]
+        hp.ev_down = [torch.cuda.Event() for _ in bounds]
+        if len(self._hosts) > 8:
+            self._hosts.clear()
+        self._hosts[key] = hp
+        return hp
+
     def run_host(self, *tensors, out=None, chunks: int = 8, row_offset: int = 0, device=None):
         """Host tensors in, host outputs back.  Row-indexed inputs are split
         into ``chunks`` blocks of rows; each block's upload, kernel and
@@ -474,63 +511,48 @@ class CompiledKernel:
             return outs[0] if len(outs) == 1 else tuple(outs)
         rows = plan.output_shapes[0][0]
         chunks = max(1, min(int(chunks), rows))
-        bounds = [(rows * i // chunks, rows * (i + 1) // chunks) for i in range(chunks)]
-        bounds = [b for b in bounds if b[1] > b[0]]
-        rmax = max(b1 - b0 for b0, b1 in bounds)
         if out is None:
             out = [torch.empty(tuple(s), dtype=d, pin_memory=True)
                    for s, d in zip(plan.output_shapes, [_torch_dtype(x) for x in plan.output_dtypes])]
         outs = list(out) if isinstance(out, (list, tuple)) else [out]
-        one = len(bounds) == 1
-        # device slots: two per row-split tensor, one per whole input
-        dev_whole = [None if f else torch.empty(tuple(t.shape), dtype=t.dtype, device=dev)
-                     for t, f in zip(tensors, flags)]
-        nslot = 1 if one else 2
-        dev_split = [[torch.empty((rmax, t.shape[1]), dtype=t.dtype, device=dev)
-                      for _ in range(nslot)] if f else None for t, f in zip(tensors, flags)]
-        dev_out = [[torch.empty((rmax, o.shape[1]), dtype=o.dtype, device=dev)
-                    for _ in range(nslot)] for o in outs]
+        hp = self._host_plan(dev, tensors, flags, outs, chunks)
         cur = torch.cuda.current_stream(dev)
-        s_up, s_run, s_down = (torch.cuda.Stream(dev) for _ in range(3))
-        for s in (s_up, s_run, s_down):
+        # this call's work follows the caller's stream and the previous call
+        # (whose slots it reuses)
+        for s in hp.streams:
             s.wait_stream(cur)
+            if hp.last is not None:
+                s.wait_event(hp.last)
+        s_up, s_run, s_down = hp.streams
         with torch.cuda.stream(s_up):
-            for t, d in zip(tensors, dev_whole):
+            for t, d in zip(tensors, hp.dev_whole):
                 if d is not None:
                     d.copy_(t, non_blocking=True)
-        ev_up, ev_run, ev_down = [], [], []
-        for i, (r0, r1) in enumerate(bounds):
+        nslot = hp.nslot
+        for i, (r0, r1) in enumerate(hp.bounds):
             slot, n = i % nslot, r1 - r0
             with torch.cuda.stream(s_up):
                 if i >= nslot:
-                    s_up.wait_event(ev_run[i - nslot])        # the slot's inputs were consumed
-                for t, d in zip(tensors, dev_split):
+                    s_up.wait_event(hp.ev_run[i - nslot])      # the slot's inputs were consumed
+                for t, d in zip(tensors, hp.dev_split):
                     if d is not None:
                         d[slot][:n].copy_(t[r0:r1], non_blocking=True)
-                ev_up.append(torch.cuda.Event())
-                ev_up[-1].record(s_up)
+                hp.ev_up[i].record(s_up)
             with torch.cuda.stream(s_run):
-                s_run.wait_event(ev_up[i])
+                s_run.wait_event(hp.ev_up[i])
                 if i >= nslot:
-                    s_run.wait_event(ev_down[i - nslot])      # the slot's outputs were read back
-                args = [w if w is not None else d[slot][:n] for w, d in zip(dev_whole, dev_split)]
-                self(*args, out=[o[slot][:n] for o in dev_out], stream=s_run.cuda_stream,
+                    s_run.wait_event(hp.ev_down[i - nslot])    # the slot's outputs were read back
+                args = [w if w is not None else d[slot][:n] for w, d in zip(hp.dev_whole, hp.dev_split)]
+                self(*args, out=[o[slot][:n] for o in hp.dev_out], stream=s_run.cuda_stream,
                      row_offset=row_offset + r0)
-                ev_run.append(torch.cuda.Event())
-                ev_run[-1].record(s_run)
+                hp.ev_run[i].record(s_run)
             with torch.cuda.stream(s_down):
-                s_down.wait_event(ev_run[i])
-                for o, d in zip(outs, dev_out):
+                s_down.wait_event(hp.ev_run[i])
+                for o, d in zip(outs, hp.dev_out):
                     o[r0:r1].copy_(d[slot][:n], non_blocking=True)
-                ev_down.append(torch.cuda.Event())
-                ev_down[-1].record(s_down)
+                hp.ev_down[i].record(s_down)
+        hp.last = hp.ev_down[len(hp.bounds) - 1]
         cur.wait_stream(s_down)
-        # the device buffers are freed when the last stream using them is done
-        for t in [*dev_whole, *[x for d in dev_split if d for x in d], *[x for d in dev_out for x in d]]:
-            if t is not None:
-                t.record_stream(s_up)
-                t.record_stream(s_run)
-                t.record_stream(s_down)
         return outs[0] if len(outs) == 1 else tuple(outs)
 
 
