@@ -78,6 +78,8 @@ typedef struct molten_gemm_args {
   long long row_offset;
   int* status;
   int batch;                     /* stacked independent problems (0 or 1: one) */
+  float* work;                   /* stream-K kernels: partial-tile workspace */
+  int* tile_count;               /* stream-K kernels: per-tile counters, zero between calls */
 } molten_gemm_args;
 
 /* Parameter block of the generated fused attention-score kernels

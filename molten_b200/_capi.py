@@ -64,7 +64,8 @@ class GemmArgs(ctypes.Structure):
                 ("inp", ctypes.c_void_p * MAX_IO), ("out", ctypes.c_void_p * MAX_IO),
                 ("m", ctypes.c_longlong), ("n", ctypes.c_longlong), ("k", ctypes.c_longlong),
                 ("row_offset", ctypes.c_longlong), ("status", ctypes.c_void_p),
-                ("batch", ctypes.c_int), ("tail_", ctypes.c_ubyte * 20)]
+                ("batch", ctypes.c_int), ("pad_", ctypes.c_int), ("work", ctypes.c_void_p),
+                ("tile_count", ctypes.c_void_p)]
 
 
 class AttnArgs(ctypes.Structure):

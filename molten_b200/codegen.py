@@ -107,6 +107,10 @@ def launch_records(plan: GroupPlan, name: str) -> list:
             rec.update(block=c["threads"], bm=c["bm"], bn=c["bn"], bk=c["bk"],
                        stages=c["stages"], smem=c.get("smem_bytes", 0),
                        cluster=2 if c.get("pair") else 1)
+            if c.get("streamk"):
+                rec.update(streamk=True, grid=c["sk_ctas"],
+                           work_floats=c["sk_tiles"] * c["sk_maxseg"] * c["bm"] * c["bn"],
+                           tile_counters=c["sk_tiles"])
         recs.append(rec)
     return recs
 

@@ -35,6 +35,8 @@ struct alignas(64) GemmArgs {
   long long row_offset;            // global row of local row 0
   int* status;                     // error bits (may be null)
   int batch;                       // stacked independent problems (0 or 1: one)
+  float* work;                     // stream-K partial tiles (stream-K kernels only)
+  int* tile_count;                 // stream-K per-tile arrival counters, kept at 0 between calls
 };
 
 enum GemmStatus { kGemmTimeoutFull = 1, kGemmTimeoutEmpty = 2, kGemmTimeoutAcc = 4,

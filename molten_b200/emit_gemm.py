@@ -26,7 +26,9 @@ def emit_gemm(sk: SubKernel, name: str) -> str:
     w(f"// Molten sm_100a tcgen05 GEMM + epilogue: {name}")
     w(f"// C[{sk.m}, {sk.n}] = epilogue(A[{sk.m}, {sk.k}] @ B[{sk.k}, {sk.n}]); "
       f"tile {BM}x{BN}x{BK}, {ST} stages" + ("; SM pair (cta_group::2)" if pair else ""))
-    w("#include \"molten/gemm2_sm100.cuh\"" if pair else "#include \"molten/gemm_sm100.cuh\"")
+    streamk = bool(cfg.get("streamk"))
+    w("#include \"molten/gemm2_sm100.cuh\"" if pair else
+      ("#include \"molten/gemm_sk_sm100.cuh\"" if streamk else "#include \"molten/gemm_sm100.cuh\""))
     w("")
     w("using namespace molten;")
     w("")
@@ -160,6 +162,17 @@ def emit_gemm(sk: SubKernel, name: str) -> str:
         w("}")
         return "\n".join(L) + "\n"
     w(f"  const GemmShared sh = gemm_carve<Layout_{name}>(smem_raw);")
+    if streamk:
+        kmaj = "true" if cfg.get("b_kmajor") else "false"
+        w(f"  gemm_sk_init<Layout_{name}>(sh, args);  // mbarriers + TMEM allocation")
+        w("  pdl_enter();                            // no global access before this")
+        w("  __syncthreads();")
+        w(f"  gemm_sk_roles<Layout_{name}, {f16in}, Epilogue_{name}, {kmaj}, {cfg['sk_maxseg']}, "
+          f"{cfg.get('sk_splits', 0)}>(sh, args);")
+        w("  __syncthreads();")
+        w(f"  gemm_teardown<Layout_{name}>(sh);       // TMEM release")
+        w("}")
+        return "\n".join(L) + "\n"
     w(f"  gemm_init<Layout_{name}>(sh, args);     // mbarriers + TMEM allocation")
     w("  pdl_enter();                            // no global access before this")
     w("  __syncthreads();")

@@ -6,9 +6,11 @@ NUM_SMS_B200 = 148
 
 
 PAIR_MIN_ROWS = 1024      # stacked rows from which an SM pair owns 256-row tiles
+SK_MAX_PIECES = 10        # most stream-K CTAs that share one output tile
 
 
-def choose_gemm_config(sk, override: dict, batch: int = 1, allow_pair: bool = True) -> dict:
+def choose_gemm_config(sk, override: dict, batch: int = 1, allow_pair: bool = True,
+                       allow_streamk: bool = True) -> dict:
     """Pick the CTA tile for C[M, N] = A[M, K] @ B[K, N] (+ epilogue).
 
     One CTA owns a BM x BN output tile with its fp32 accumulator in TMEM;
@@ -50,8 +52,46 @@ def choose_gemm_config(sk, override: dict, batch: int = 1, allow_pair: bool = Tr
     if smem > 232448:
         raise ValueError(f"GEMM tile needs {smem} bytes of shared memory")
     group_m = o.get("group_m", 16)
-    return {"bm": bm, "bn": bn, "bk": bk, "stages": stages, "group_m": group_m,
-            "epi_warps": 4, "threads": 256, "smem_bytes": smem, "pair": False}
+    cfg = {"bm": bm, "bn": bn, "bk": bk, "stages": stages, "group_m": group_m,
+           "epi_warps": 4, "threads": 256, "smem_bytes": smem, "pair": False, "streamk": False}
+    # few tiles and long K (decode-size M): stream-K spreads the k-blocks of
+    # all tiles evenly over the SMs (molten/gemm_sk_sm100.cuh).  Measured
+    # (CUDA-graph replay, bf16): 16x8192x1024 (16 tiles) 40.5 -> 20.0 us,
+    # 64x14336x4096 (64 tiles) 67.8 -> 42.2 us, 64x4096x4096 (64 tiles)
+    # 23.7 -> 23.6 us; with 112-128 tiles it loses (64x4096x14336 27.9 ->
+    # 41.1 us: the partial-tile traffic outweighs the SMs it adds), so only
+    # up to half the SMs' worth of tiles.  A tile cut into many pieces pays
+    # for summing them in one CTA (1x4096x256 over 148 CTAs, 37 pieces:
+    # 22.0 -> 26.0 us), so at most SK_MAX_PIECES CTAs per tile (the same
+    # shape over 40 CTAs, 10 pieces a tile: 22.1 -> 14.2 us).
+    tiles = batch * -(-M // bm) * -(-N // bn)
+    kb = -(-K // bk)
+    ctas = int(o.get("sk_ctas", min(NUM_SMS_B200, tiles * SK_MAX_PIECES, tiles * kb)))
+    auto = tiles <= NUM_SMS_B200 // 2 and tiles * kb >= 2 * ctas and batch * M <= 512
+    if o.get("streamk", auto) and allow_streamk:
+        # "sk_splits": S > 0 walks split-K units (split-major, so the CTAs
+        # running together read the same k-regions of B); 0 walks stream-K
+        # ranges (one equal range per CTA)
+        splits = min(int(o.get("sk_splits", 0)), kb)         # no empty units
+        maxseg = splits if splits > 0 else stream_k_max_segments(tiles, kb, ctas)
+        cfg.update(streamk=True, sk_ctas=ctas, sk_maxseg=maxseg, sk_splits=splits,
+                   sk_tiles=tiles, smem_bytes=smem + 64)
+    return cfg
+
+
+def stream_k_max_segments(tiles: int, kb: int, ctas: int) -> int:
+    """The most CTAs whose stream-K ranges share one tile (the device's
+    sk_lo / sk_owner arithmetic: CTA c owns iterations [c*I/G, (c+1)*I/G))."""
+    total = tiles * kb
+
+    def owner(x):
+        c = x * ctas // total
+        while c + 1 < ctas and (c + 1) * total // ctas <= x:
+            c += 1
+        while c > 0 and c * total // ctas > x:
+            c -= 1
+        return c
+    return max(owner((t + 1) * kb - 1) - owner(t * kb) + 1 for t in range(tiles))
 
 
 def _pair_config(M: int, N: int, batch: int, o: dict) -> dict:
@@ -78,4 +118,4 @@ def _pair_config(M: int, N: int, batch: int, o: dict) -> dict:
     if smem > 232448:
         raise ValueError(f"GEMM tile needs {smem} bytes of shared memory")
     return {"bm": 256, "bn": bn, "bk": 64, "stages": stages, "group_m": o.get("group_m", 16),
-            "epi_warps": 4, "threads": 256, "smem_bytes": smem, "pair": True}
+            "epi_warps": 4, "threads": 256, "smem_bytes": smem, "pair": True, "streamk": False}

@@ -454,7 +454,7 @@ def _plan_gemm(graph, ops, ext, outs, shapes, dts, tune) -> SubKernel:
         raise LoweringError("GEMM epilogues are elementwise only")
     from .gemm_config import choose_gemm_config
     sk.config = choose_gemm_config(sk, tune.get("gemm") or {}, batch=batch,
-                                   allow_pair=prologue is None)
+                                   allow_pair=prologue is None, allow_streamk=prologue is None)
     sk.config["b_kmajor"] = bool(b_kmajor)
     sk.config["batch"] = int(batch)
     if prologue is not None:

@@ -146,7 +146,12 @@ class _Spec:
             tiles = c.get("batch", 1) * (-(-sk.m // c["bm"])) * (-(-sk.n // c["bn"]))
             cfg.block[:] = [128, c["threads"] // 128, 1]
             cfg.smem_bytes = c["smem_bytes"]
-            if c.get("pair"):
+            if c.get("streamk"):
+                # stream-K: one range of the tiles x k-blocks per CTA over a
+                # fixed CTA count (the kernel's workspace slots assume it)
+                cfg.grid[:] = [c["sk_ctas"], 1, 1]
+                cfg.cluster[:] = [1, 1, 1]
+            elif c.get("pair"):
                 # clusters of 2 CTAs (an SM pair per 256-row tile), persistent
                 cfg.cluster[:] = [2, 1, 1]
                 cfg.grid[:] = [2 * max(1, min(tiles, sms // 2)), 1, 1]
@@ -161,6 +166,22 @@ class _Spec:
         cfg.flags = _capi.LAUNCH_PDL if PDL else 0
         self._cfgs[key] = cfg
         return cfg
+
+    def stream_k_workspace(self, i: int, device: int):
+        """(fp32 partial tiles, int32 per-tile counters) of stream-K kernel i
+        on ``device``, allocated once; the kernel leaves the counters at 0.
+        Calls of one specialisation must not overlap on the GPU (they share
+        this workspace)."""
+        key = ("sk", i, device)
+        ws = self._cfgs.get(key)
+        if ws is None:
+            torch = _torch()
+            c = self.plan.kernels[i].config
+            n = c["sk_tiles"] * c["sk_maxseg"] * c["bm"] * c["bn"]
+            ws = (torch.empty(n, dtype=torch.float32, device=f"cuda:{device}"),
+                  torch.zeros(c["sk_tiles"], dtype=torch.int32, device=f"cuda:{device}"))
+            self._cfgs[key] = ws
+        return ws
 
     def tmap(self, t, dtype: str, rows: int, cols: int, box_inner: int, box_outer: int,
              swizzle: int = 128) -> bytes:
@@ -237,6 +258,9 @@ class _Spec:
                 a.m, a.n, a.k = sk.m, sk.n, sk.k
                 a.batch = nb
                 a.status = _capi.status_word(di)
+                if sk.config.get("streamk"):
+                    work, count = self.stream_k_workspace(i, di)
+                    a.work, a.tile_count = work.data_ptr(), count.data_ptr()
             else:
                 a = _capi.RowArgs()
                 a.rows, a.cols = sk.rows, sk.cols

@@ -394,3 +394,29 @@ def test_run_host_row_split_rules():
     assert flags(graphs.gemm_bias_gelu(128, 64, 64), [e(128, 64), e(64, 64), e(64)]) == [True, False, False]
     assert flags(graphs.attention_score(64, 64, 64), [e(64, 64), e(64, 64)]) is None
     assert flags(graphs.rope(1, 16, 4, 128), [e(1, 16, 4, 128), e(16, 64), e(16, 64)]) is None
+
+
+def test_stream_k_plan():
+    """Stream-K for GEMMs with at most half the SMs' worth of tiles, a long
+    K and few rows, with at most SK_MAX_PIECES CTAs per tile; the workspace
+    slot count follows the device's range arithmetic."""
+    from molten_b200.gemm_config import SK_MAX_PIECES, stream_k_max_segments
+    (k,) = compile_graph(graphs.gemm_bias_gelu(16, 8192, 1024), dtype="bfloat16")
+    c = k.plan.kernels[0].config
+    assert c["streamk"] and c["sk_ctas"] == 148 and c["sk_tiles"] == 16
+    assert c["sk_maxseg"] == stream_k_max_segments(16, 128, 148) <= SK_MAX_PIECES + 1
+    assert "gemm_sk_roles<" in k.source and "molten/gemm_sk_sm100.cuh" in k.source
+    assert k.config.launches[0]["family"] == "gemm"
+    assert k.config.launches[0]["grid"] == 148
+    (k,) = compile_graph(graphs.gemm_bias_gelu(1, 4096, 256), dtype="bfloat16")
+    c = k.plan.kernels[0].config
+    assert c["streamk"] and c["sk_tiles"] == 4 and c["sk_ctas"] == 4 * SK_MAX_PIECES
+    # decode 64 x 4096 x 14336 has 112 tiles: the plain persistent kernel
+    for big in [(64, 4096, 14336), (64, 4096, 8192), (8192, 4096, 14336), (256, 512, 384),
+                (1024, 256, 512)]:
+        (k,) = compile_graph(graphs.gemm_bias_gelu(*big), dtype="bfloat16")
+        assert not k.plan.kernels[0].config["streamk"], big
+    # every tile is covered by owner(last) - owner(first) + 1 CTAs, at most 2
+    # when each CTA has at least one tile's worth of k-blocks
+    assert stream_k_max_segments(100, 64, 148) <= 3
+    assert stream_k_max_segments(148, 10, 148) == 1

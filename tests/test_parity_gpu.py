@@ -247,6 +247,49 @@ def test_gemm_sm_pair(rt, m, k, n, bn, kmajor, batch):
                  f"pair gemm {batch}x{m}x{k}x{n} bn {bn} kmajor {kmajor}")
 
 
+@pytest.mark.parametrize("m,k,n,batch,dtype,kmajor", [
+    (64, 4096, 2048, 1, "bfloat16", False), (1, 4096, 256, 1, "bfloat16", False),
+    (37, 4000, 384, 1, "bfloat16", False), (50, 1024, 320, 3, "bfloat16", False),
+    (64, 2048, 1024, 1, "float16", False), (64, 4096, 1024, 1, "bfloat16", True)])
+def test_gemm_stream_k(rt, m, k, n, batch, dtype, kmajor):
+    """Fewer tiles than SMs: the tiles x k-blocks iteration space is spread
+    over every SM; CTAs sharing a tile write fp32 partials and the last to
+    arrive sums them in slot order -- deterministic, and the per-tile
+    counters are back at 0 after every call (the repeat must match bit for
+    bit)."""
+    from molten_b200.codegen import CodeGenerator
+    from molten_b200.ir import DataflowGraph, TensorShape as TS
+    lead = [batch] if batch > 1 else []
+    g = DataflowGraph("gemm_sk")
+    a = g.add_input("A", TS(lead + [m, k]), dtype=dtype)
+    if kmajor:
+        bmat = g.transpose(g.add_input("Bt", TS(lead + [n, k]), dtype=dtype))
+    else:
+        bmat = g.add_input("B", TS(lead + [k, n]), dtype=dtype)
+    bias = g.add_input("bias", TS([n]), dtype=dtype)
+    g.add_output(g.gelu(g.add(g.matmul(a, bmat), bias)))
+    kern = CodeGenerator(dtype=dtype, tune={"gemm": {"streamk": True}}).generate(g, FusionEngine().fuse(g)[0])
+    (sk,) = kern.plan.kernels
+    assert sk.config["streamk"] and sk.config["sk_maxseg"] >= 2
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(m * 17 + n + k)
+    T = TORCH_DT[dtype]
+    A = torch.randn(*lead, m, k, generator=gen, device=DEV).to(T)
+    bshape = (*lead, n, k) if kmajor else (*lead, k, n)
+    B = (torch.randn(*bshape, generator=gen, device=DEV) / k ** 0.5).to(T)
+    bb = (0.02 * torch.randn(n, generator=gen, device=DEV)).to(T)
+    ck = rt.compile(kern)
+    out = ck(A, B, bb)
+    out2 = ck(A, B, bb)
+    torch.cuda.synchronize()
+    assert MoltenRuntime.read_status(0) == 0
+    assert torch.equal(out.view(torch.int16), out2.view(torch.int16)), "repeated runs differ"
+    names = ["A", "Bt" if kmajor else "B", "bias"]
+    res = orc.evaluate(g, dict(zip(names, [to_numpy(A), to_numpy(B), to_numpy(bb)])))
+    assert_close(as_f32(out), res[("f32", g.ops[g._outputs[0]].inputs[0])], dtype,
+                 f"stream-K gemm {batch}x{m}x{k}x{n}")
+
+
 def test_gemm_plain_matmul_fp16(rt):
     g = graphs.gemm_bias_gelu(256, 256, 256, dtype="float16")
     gen = torch.Generator(device=DEV)
