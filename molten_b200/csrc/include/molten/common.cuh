@@ -112,6 +112,25 @@ __device__ __forceinline__ void store_slot(T* p, const Slot<T, VEC>& s) {
   }
 }
 
+// Store a slot of VEC zeros: all-zero bits, +0.0 in every float format, so
+// nothing is converted (masked-out softmax outputs).
+template <int HINT, typename T, int VEC>
+__device__ __forceinline__ void store_zero_slot(T* p) {
+  constexpr int BYTES = sizeof(T) * VEC;
+  if constexpr (BYTES % 16 == 0) {
+#pragma unroll
+    for (int i = 0; i < BYTES / 16; ++i)
+      st16<HINT>(reinterpret_cast<char*>(p) + 16 * i, make_uint4(0u, 0u, 0u, 0u));
+  } else if constexpr (BYTES == 8) {
+    *reinterpret_cast<uint2*>(p) = make_uint2(0u, 0u);
+  } else if constexpr (BYTES == 4) {
+    *reinterpret_cast<uint32_t*>(p) = 0u;
+  } else {
+    static_assert(BYTES == 2, "unsupported slot size");
+    *reinterpret_cast<uint16_t*>(p) = 0;
+  }
+}
+
 // Write VEC fp32 values into a slot of T, rounding to nearest even once.
 template <typename T, int VEC>
 __device__ __forceinline__ void pack_slot(Slot<T, VEC>& s, const float (&f)[VEC]) {

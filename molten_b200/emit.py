@@ -1209,9 +1209,7 @@ def _emit_causal_softmax_pass(e: _Emitter, sk: SubKernel, v: int, parts, targets
     e.w("#pragma unroll")
     e.w(f"      for (int e = 0; e < VEC; ++e) m{v}[k][e] = 0.0f;")
     for o in early_zero:
-        ct = _ctype(o.dtype)
-        e.w(f"      {{ Slot<{ct}, VEC> z; const float zf[VEC] = {{}}; pack_slot<{ct}, VEC>(z, zf);")
-        e.w(f"        store_slot<kStoreDefault, {ct}, VEC>(out{o.index} + j * VEC, z); }}")
+        e.w(f"      store_zero_slot<kStoreDefault, {_ctype(o.dtype)}, VEC>(out{o.index} + j * VEC);")
     e.w("      continue;")
     e.w("    }")
     _emit_nonprefetched_loads(e, a_targets, prefetch, "    ")

@@ -105,21 +105,29 @@ def test_specialised_dtypes_and_promotion():
 
 
 def test_long_rows_use_a_cluster():
-    g = graphs.softmax((4096, 32768))
+    """Rows needing more than 1024 threads run on a cluster; fp32 rows of
+    513..1024 threads on one 1024-thread CTA."""
+    g = graphs.softmax((64, 65536))
     k = compile_graph(g)[0]
     sk = k.plan.kernels[0]
     assert sk.config["cl"] > 1 and k.config.cluster_x == sk.config["cl"]
+    for causal in (False, True):
+        k = compile_graph(graphs.softmax((4096, 32768), causal=causal))[0]
+        sk = k.plan.kernels[0]
+        assert (sk.config["tpc"], sk.config["cl"], sk.config["block"]) == (1024, 1, 1024)
+        assert k.config.cluster_x == 1 and not sk.config.get("stream")
 
 
 def test_long_16bit_rows_take_the_stream_form():
     """bf16 rows long enough for a cluster run as one 1024-thread CTA per
-    row in the persistent stream form; fp32 rows keep the cluster."""
+    row in the persistent stream form; fp32 rows as one 1024-thread CTA in
+    the register form."""
     sk = compile_graph(graphs.softmax((4096, 32768), dtype="bfloat16"), dtype="bfloat16")[0] \
         .plan.kernels[0]
     assert (sk.config["tpc"], sk.config["cl"], sk.config["stream"]) == (1024, 1, 3)
     assert sk.config["bulk"] and sk.config["smem"] == 3 * 32768 * 2
     sk = compile_graph(graphs.softmax((4096, 32768)))[0].plan.kernels[0]
-    assert sk.config["cl"] > 1 and not sk.config.get("stream")
+    assert sk.config["cl"] == 1 and not sk.config.get("stream")
 
 
 def test_stream_forms_compile_for_sm100a(tmp_path):

@@ -95,6 +95,7 @@ FULL = [
     "softmax_f32_65536x2048_causal",
     "softmax_bf16_65536x2048_causal",
     "softmax_f32_4096x32768",
+    "softmax_f32_4096x32768_causal",
     "softmax_bf16_4096x32768_causal",
     "chain_bf16_16384x8192",
     "rope_bf16_4x4096x32x128",
