@@ -97,6 +97,34 @@ __device__ __forceinline__ void bulk_row_g2s(uint32_t dst, const void* src, uint
 }
 enum RowStageStatus { kRowTimeoutStage = 256 };
 
+// Zero tail of a masked row: `bytes` zero bytes at global `dst` (both
+// 16-byte multiples), written by the TMA engine from a zero-filled shared
+// buffer of `zbytes` at `zsrc` (bulk stores of up to zbytes each, one bulk
+// group).  The issuing thread goes on at once; bulk_zero_drain() before it
+// exits waits for all of them.
+__device__ __forceinline__ void bulk_zero_tail(void* dst, long long bytes, uint32_t zsrc,
+                                               uint32_t zbytes) {
+  char* p = static_cast<char*>(dst);
+  while (bytes > 0) {
+    const uint32_t n = bytes < (long long)zbytes ? (uint32_t)bytes : zbytes;
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
+                 :: "l"(p), "r"(zsrc), "r"(n) : "memory");
+    p += n;
+    bytes -= n;
+  }
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_zero_drain() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+// Fill `bytes` (a multiple of 16 * blockDim.x) of shared memory at `zbuf`
+// with zeros and make them visible to the TMA engine; every thread calls
+// it, followed by a barrier.
+__device__ __forceinline__ void zero_shared_for_bulk(uint4* zbuf, int bytes) {
+  for (int i = threadIdx.x; i < bytes / 16; i += blockDim.x) zbuf[i] = make_uint4(0u, 0u, 0u, 0u);
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 template <typename T, int VEC>
 __device__ __forceinline__ Slot<T, VEC> lds_slot16(uint32_t addr) {
   static_assert(sizeof(T) * VEC == 16, "staged slots are 16 bytes");

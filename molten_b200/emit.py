@@ -262,6 +262,11 @@ def emit_row(sk: SubKernel, name: str) -> str:
     e.w(f"  __shared__ float red_smem[Team::smem_floats({max_nr}, {n_areas}) > 0 ? "
         f"Team::smem_floats({max_nr}, {n_areas}) : 1];")
     e.w("  const Team tm(args.rows, 0);")
+    # the causal pass may hand masked row tails to the TMA engine (bulk zero
+    # stores): its shared zero buffer goes here, its drain before the end
+    zmark = len(e.lines)
+    e.zero_tail = bool(cfg.get("zero_tail")) and CL == 1 and RPC == 1 and TPC >= 256
+    e.zero_tail_used = False
     body = dict(closures=closures, reds=reds, smx=smx, materialize=materialize,
                 prefetch=prefetch, masked_only=masked_only)
     if not stream:
@@ -279,6 +284,7 @@ def emit_row(sk: SubKernel, name: str) -> str:
             _emit_exchange_teardown(e)
         else:
             e.w("  tm.cluster_done_wait();")
+        _finish_zero_tail(e, zmark)
         e.w("}")
         return "\n".join(e.lines) + "\n"
 
@@ -366,8 +372,28 @@ def emit_row(sk: SubKernel, name: str) -> str:
         e.w("  cp_async_wait<0>();")
     if push:
         _emit_exchange_teardown(e)
+    _finish_zero_tail(e, zmark)
     e.w("}")
     return "\n".join(e.lines) + "\n"
+
+
+ZERO_TAIL_BYTES = 16384      # shared zero buffer the bulk zero stores read
+
+
+def _finish_zero_tail(e: "_Emitter", zmark: int):
+    """When the causal pass used bulk zero stores: the zero buffer (filled
+    and fenced for the TMA engine before any row) at ``zmark``, and the
+    issuing thread's drain of its bulk groups before the kernel ends."""
+    if not e.zero_tail_used:
+        return
+    e.lines[zmark:zmark] = [
+        f"  constexpr uint32_t ZBYTES = {ZERO_TAIL_BYTES}u;",
+        "  __shared__ __align__(128) uint4 zbuf[ZBYTES / 16];",
+        "  zero_shared_for_bulk(zbuf, ZBYTES);     // zeros the bulk zero-tail stores read",
+        "  __syncthreads();",
+        "  const uint32_t zsrc = shared_addr(zbuf);",
+    ]
+    e.w("  if (threadIdx.x == 0) bulk_zero_drain();   // this thread's bulk zero stores are done")
 
 
 def _emit_exchange_setup(e: _Emitter, n_areas: int, max_nr: int):
@@ -1163,6 +1189,24 @@ def _emit_causal_softmax_pass(e: _Emitter, sk: SubKernel, v: int, parts, targets
     a, mk = parts
     a_targets = _closure_within(values, a, targets)
     lim = f"mlim{mk}"
+    # bulk zero tail: the row's fully masked slots (columns from the first
+    # slot above the limit to the end) are written by the TMA engine from a
+    # shared zero buffer, issued by the row's one team leader; threads skip
+    # them.  Needs 16-byte slots covering the row exactly and a 16-byte
+    # aligned output row (checked per row; otherwise the threads store them)
+    zt = None
+    if (early_zero and getattr(e, "zero_tail", False) and sk.cols % VEC == 0
+            and all(DTYPE_SIZE_OF[o.dtype] * VEC == 16 for o in early_zero)):
+        zt = f"zt{v}"
+        align = " | ".join(f"reinterpret_cast<uintptr_t>(out{o.index})" for o in early_zero)
+        e.w(f"  const bool {zt} = rok && ((({align}) & 15u) == 0);")
+        e.w(f"  if ({zt} && threadIdx.x == 0) {{")
+        e.w(f"    const long long z0 = ({lim} < 0) ? 0LL : ((long long)({lim} / VEC) + 1) * VEC;")
+        for o in early_zero:
+            e.w(f"    if (z0 < COLS) bulk_zero_tail(out{o.index} + z0, (COLS - z0) * "
+                f"(long long)sizeof(*out{o.index}), zsrc, ZBYTES);")
+        e.w("  }")
+        e.zero_tail_used = True
     _emit_softmax_thread_max_decl(e, sk, [v])
     packed = _packed_max_operand(sk, values[a], prefetch, VEC)
 
@@ -1209,7 +1253,8 @@ def _emit_causal_softmax_pass(e: _Emitter, sk: SubKernel, v: int, parts, targets
     e.w("#pragma unroll")
     e.w(f"      for (int e = 0; e < VEC; ++e) m{v}[k][e] = 0.0f;")
     for o in early_zero:
-        e.w(f"      store_zero_slot<kStoreDefault, {_ctype(o.dtype)}, VEC>(out{o.index} + j * VEC);")
+        store = f"store_zero_slot<kStoreDefault, {_ctype(o.dtype)}, VEC>(out{o.index} + j * VEC);"
+        e.w(f"      if (!{zt}) {store}" if zt else f"      {store}")
     e.w("      continue;")
     e.w("    }")
     _emit_nonprefetched_loads(e, a_targets, prefetch, "    ")

@@ -118,6 +118,21 @@ def test_long_rows_use_a_cluster():
         assert k.config.cluster_x == 1 and not sk.config.get("stream")
 
 
+def test_causal_zero_tail_selection():
+    """Bulk zero stores for the masked row tails of a causal softmax: in the
+    register form with one team of >= 256 threads per CTA, not in the
+    bulk-staged stream form, not for short rows (several rows per CTA)."""
+    src = compile_graph(graphs.softmax((4096, 32768), causal=True))[0].source
+    assert "bulk_zero_tail" in src and "bulk_zero_drain" in src and "zero_shared_for_bulk" in src
+    src = compile_graph(graphs.softmax((4096, 32768), dtype="bfloat16", causal=True),
+                        dtype="bfloat16")[0].source
+    assert "bulk_zero_tail" not in src and "store_zero_slot" in src
+    src = compile_graph(graphs.softmax((65536, 2048), causal=True))[0].source
+    assert "bulk_zero_tail" not in src
+    src = compile_graph(graphs.softmax((4096, 32768)))[0].source       # no mask, no tail
+    assert "bulk_zero_tail" not in src and "zbuf" not in src
+
+
 def test_long_16bit_rows_take_the_stream_form():
     """bf16 rows long enough for a cluster run as one 1024-thread CTA per
     row in the persistent stream form; fp32 rows as one 1024-thread CTA in

@@ -361,6 +361,9 @@ STREAM_CASES = [
     # bulk staging: one bulk copy per row and staged operand, mbarrier per stage
     ("softmax", 300, 32768, "bfloat16", {"stream": 3, "tpc": 1024, "cl": 1, "bulk": True}),
     ("softmax_causal", 700, 8192, "bfloat16", {"stream": 3, "tpc": 1024, "cl": 1, "bulk": True}),
+    # masked row tails written by bulk zero stores from shared memory
+    ("softmax_causal", 700, 8192, "bfloat16", {"stream": 3, "tpc": 1024, "cl": 1, "bulk": True,
+                                               "zero_tail": True}),
     ("rmsnorm_silu", 1000, 3584, "bfloat16", {"stream": 4, "engine": "regs", "bulk": True}),
 ]
 
@@ -410,6 +413,52 @@ def test_stream_row_engine(kind, rows, cols, dtype, tune):
     for a, b in ((0, half), (half, rows)):
         part = [t if t.dim() == 1 else t[a:b] for t in xs]
         outs.append(ck(*part, row_offset=a))
+    torch.cuda.synchronize()
+    bits = (lambda t: t.view(torch.int16)) if out.dtype != torch.float32 else \
+        (lambda t: t.view(torch.int32))
+    assert torch.equal(bits(torch.cat(outs)), bits(out))
+
+
+@pytest.mark.parametrize("rows,cols,dtype,tune", [
+    (333, 8192, "float32", {}),
+    (4100, 32768, "float32", {}),
+    (300, 32768, "bfloat16", {"tpc": 1024, "cl": 1, "zero_tail": True}),
+])
+def test_causal_zero_tail(rows, cols, dtype, tune):
+    """Causal softmax in the register form with the masked tail of each row
+    written by bulk zero stores (TMA engine, shared zero buffer) instead of
+    the threads: matches the oracle, every fully masked column is exactly
+    0, and two row-offset halves give the same bits (the tail starts where
+    each row's global limit puts it)."""
+    from molten_b200.codegen import CodeGenerator
+    from molten_b200.fusion import FusionEngine
+    rt = MoltenRuntime(tune={"row": dict(tune)})
+    g = graphs.softmax((rows, cols), dtype=dtype, causal=True)
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(rows + cols)
+    x = (3.0 * torch.randn(rows, cols, generator=gen, device=DEV)).to(TORCH_DT[dtype])
+    gk = CodeGenerator(tune=rt.tune).generate(g, FusionEngine().fuse(g)[0], {0: (rows, cols)},
+                                              {0: dtype})
+    assert "bulk_zero_tail" in gk.source and not gk.plan.kernels[0].config.get("stream")
+    ck = rt.compile(gk)
+    out = ck(x)
+    torch.cuda.synchronize()
+    assert MoltenRuntime.read_status(0) == 0
+    # the mask: column c of row r is visible iff c <= r mod cols
+    cidx = torch.arange(cols, device=DEV)[None, :]
+    ridx = (torch.arange(rows, device=DEV) % cols)[:, None]
+    assert torch.all(out.float()[cidx > ridx] == 0)
+    # the oracle on sampled rows, each at its global row (the mask follows it)
+    pick = _sample_rows(rows, 24)
+    g1 = graphs.softmax((1, cols), dtype=dtype, causal=True)
+    oid = g1.ops[g1._outputs[0]].inputs[0]
+    xn = to_numpy(x)
+    ref = np.concatenate([orc.evaluate(g1, {"logits": xn[r:r + 1]}, row_offset=int(r))[("f32", oid)]
+                          for r in pick])
+    got = as_f32(out[torch.as_tensor(pick, device=DEV)])
+    assert_close(got, ref, dtype, f"zero tail {rows}x{cols} {dtype}")
+    half = rows // 2 + 1
+    outs = [ck(x[a:b], row_offset=a) for a, b in ((0, half), (half, rows))]
     torch.cuda.synchronize()
     bits = (lambda t: t.view(torch.int16)) if out.dtype != torch.float32 else \
         (lambda t: t.view(torch.int32))
