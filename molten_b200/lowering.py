@@ -682,8 +682,9 @@ def choose_row_config(sk: SubKernel, prefetch: set, materialize: set,
         # 16-bit rows long enough to need a cluster: one 1024-thread CTA per
         # row in the persistent stream form, 3 rows staged (measured: softmax
         # bf16 x 32768 77% of HBM peak vs 63% with a 2-CTA cluster per row,
-        # causal 79 us vs 117 us; fp32 rows keep the cluster form, which
-        # measured best for them)
+        # causal 79 us vs 117 us; 4-byte rows of up to 1024 threads take one
+        # 1024-thread CTA in the register form instead, chosen above, whose
+        # 32 KB-per-thread-row stages would not fit twice in shared memory)
         tpc, cl, team = tpc * cl, 1, tpc * cl
         stream_auto = 3
     if o.get("rpc"):
