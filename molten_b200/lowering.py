@@ -683,8 +683,9 @@ def choose_row_config(sk: SubKernel, prefetch: set, materialize: set,
         # row in the persistent stream form, 3 rows staged (measured: softmax
         # bf16 x 32768 77% of HBM peak vs 63% with a 2-CTA cluster per row,
         # causal 79 us vs 117 us; 4-byte rows of up to 1024 threads take one
-        # 1024-thread CTA in the register form instead, chosen above, whose
-        # 32 KB-per-thread-row stages would not fit twice in shared memory)
+        # 1024-thread CTA in the register form instead, chosen above: an fp32
+        # row of that length is a 128 KB stage, which would not fit twice in
+        # shared memory)
         tpc, cl, team = tpc * cl, 1, tpc * cl
         stream_auto = 3
     if o.get("rpc"):
