@@ -231,6 +231,10 @@ def pass_closures(values, sk: SubKernel, needed: set, materialized: dict):
         if val.op in ("rsum", "rmax", "rmin", "softmax"):
             roots[val.avail - 1].append(val.args[0])
     roots[sk.passes] += [v for v in sk.out_values if values[v].kind == "elem"]
+    # a value materialized at pass p is computed there, needed there or not
+    for v, pm in materialized.items():
+        if values[v].kind == "elem" and pm <= sk.passes:
+            roots[pm].append(v)
     closures = {}
     for p, rs in roots.items():
         seen, stack = set(), list(rs)
@@ -244,6 +248,9 @@ def pass_closures(values, sk: SubKernel, needed: set, materialized: dict):
             stack.extend(values[v].args)
         closures[p] = seen
     return closures
+
+
+EARLY_OPS = {"exp", "log", "tanh", "sigmoid", "gelu", "silu"}
 
 
 def _row_storage(sk: SubKernel, needed: set):
@@ -262,6 +269,16 @@ def _row_storage(sk: SubKernel, needed: set):
         val = values[v]
         if val.op in EXPENSIVE and max(ps) > first[v] and v not in materialize:
             materialize[v] = first[v]
+    # transcendental terms of the row's own elements that only a later pass
+    # uses (silu(gate) in RMSNorm * SiLU(gate)): computed in the reduction
+    # pass and kept in registers, so their XU work overlaps the row's
+    # reduction instead of queueing behind it at the end (measured:
+    # RMSNorm * SiLU bf16 2048 x 3584, register engine, 9.32 -> 8.72-8.81 us,
+    # bit-identical); at most two, for the register budget
+    early = [v for v in sorted(uses) if values[v].op in EARLY_OPS and values[v].kind == "elem"
+             and values[v].avail == 0 and first[v] > 0 and v not in materialize]
+    for v in early[:2]:
+        materialize[v] = 0
     prefetch = set()
     for opd in sk.operands:
         if opd.last == "vec" and opd.row_map != "zero":

@@ -118,6 +118,20 @@ def test_long_rows_use_a_cluster():
         assert k.config.cluster_x == 1 and not sk.config.get("stream")
 
 
+def test_silu_of_the_gate_is_computed_in_the_reduction_pass():
+    """RMSNorm * SiLU(gate) in the register engine: silu(gate) depends only on
+    the row's own elements, so it is computed next to the sum of squares and
+    kept in registers for the output pass."""
+    (k,) = compile_graph(graphs.rmsnorm_silu_gate(2048, 3584), dtype="bfloat16")
+    c = k.plan.kernels[0].config
+    assert c["engine"] == "regs" and len(c["materialize"]) == 1 and c["materialize"][0][1] == 0
+    body = k.source.split("// ---- pass 0")[1].split("// ---- final pass")[0]
+    assert "m_silu<" in body and "m_silu<" not in k.source.split("// ---- final pass")[1]
+    # a plain RMSNorm has nothing to compute early
+    (k,) = compile_graph(graphs.rmsnorm(2048, 5120))
+    assert k.plan.kernels[0].config["materialize"] == []
+
+
 def test_causal_zero_tail_selection():
     """Bulk zero stores for the masked row tails of a causal softmax: in the
     register form with one team of >= 256 threads per CTA, not in the
