@@ -93,9 +93,11 @@ FULL = [
     "rmsnorm_silu_bf16_8192x3584",
     "softmax_f32_65536x2048",
     "softmax_f32_65536x2048_causal",
+    "softmax_bf16_65536x2048",
     "softmax_bf16_65536x2048_causal",
     "softmax_f32_4096x32768",
     "softmax_f32_4096x32768_causal",
+    "softmax_bf16_4096x32768",
     "softmax_bf16_4096x32768_causal",
     "chain_bf16_16384x8192",
     "rope_bf16_4x4096x32x128",
@@ -204,6 +206,66 @@ def test_gemm_shapes(rt, m, k, n):
     res = orc.evaluate(g, {"A": to_numpy(A), "B": to_numpy(B), "bias": to_numpy(bias)})
     assert_close(as_f32(out), res[("f32", g.ops[g._outputs[0]].inputs[0])], "bfloat16",
                  f"gemm {m}x{k}x{n}")
+
+
+@pytest.mark.parametrize("m,k,n,kmajor,batch,bdt,epi", [
+    (64, 128, 64, False, 1, "float32", False),      # the reference's test_matmul_kernel
+    (256, 512, 384, False, 1, "float32", True),
+    (300, 200, 504, False, 1, "float32", True),
+    (1024, 256, 512, False, 1, "float32", True),
+    (513, 1024, 768, False, 1, "float32", True),
+    (300, 512, 384, True, 1, "float32", True),      # B given as transpose(Bt)
+    (200, 128, 300, True, 3, "float32", True),      # 3 stacked problems, K-major B
+    (256, 136, 520, False, 2, "float32", True),
+    (256, 512, 384, False, 1, "bfloat16", True),    # fp32 A x bf16 B
+    (512, 4096, 1024, False, 1, "float32", True),   # long K
+    (128, 16384, 256, False, 1, "float32", True),   # longer K
+])
+def test_gemm_float32(rt, m, k, n, kmajor, batch, bdt, epi):
+    """fp32 MATMUL (+ bias + GELU): each fp32 operand is split into three
+    bf16 planes, the tensor cores sum the six plane products in chunks of
+    four k-blocks and the epilogue adds the chunks in fp32 registers; held
+    to the fp32 bar against the oracle (fp64 accumulation, one rounding)."""
+    from molten_b200.codegen import CodeGenerator
+    from molten_b200.ir import DataflowGraph, TensorShape as TS
+    lead = [batch] if batch > 1 else []
+    g = DataflowGraph("gemm_f32")
+    a = g.add_input("A", TS(lead + [m, k]), dtype="float32")
+    if kmajor:
+        bmat = g.transpose(g.add_input("Bt", TS(lead + [n, k]), dtype=bdt))
+    else:
+        bmat = g.add_input("B", TS(lead + [k, n]), dtype=bdt)
+    mm = g.matmul(a, bmat)
+    if epi:
+        bias = g.add_input("bias", TS([n]), dtype="float32")
+        mm = g.gelu(g.add(mm, bias))
+    g.add_output(mm)
+    kern = CodeGenerator(dtype="float32").generate(g, FusionEngine().fuse(g)[0])
+    fams = [sk.family for sk in kern.plan.kernels]
+    assert fams == ["split3", "split3", "gemm"] and kern.plan.kernels[-1].config["split3"]
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(m + 5 * n + 3 * k)
+    A = torch.randn(*lead, m, k, generator=gen, device=DEV)
+    bshape = (*lead, n, k) if kmajor else (*lead, k, n)
+    B = (torch.randn(*bshape, generator=gen, device=DEV) / k ** 0.5).to(TORCH_DT[bdt])
+    ins = [A, B]
+    names = ["A", "Bt" if kmajor else "B"]
+    if epi:
+        ins.append(0.02 * torch.randn(n, generator=gen, device=DEV))
+        names.append("bias")
+    ck = rt.compile(kern)
+    out = ck(*ins)
+    out2 = ck(*ins)
+    torch.cuda.synchronize()
+    assert MoltenRuntime.read_status(0) == 0
+    assert out.dtype == torch.float32
+    assert torch.equal(out.view(torch.int32), out2.view(torch.int32)), "repeated runs differ"
+    res = orc.evaluate(g, dict(zip(names, [to_numpy(t) for t in ins])))
+    ref = res[("f32", g.ops[g._outputs[0]].inputs[0])]
+    got = as_f32(out)
+    rel = np.abs(got - ref).max() / np.abs(ref).max()
+    print(f"fp32 gemm {batch}x{m}x{k}x{n}: max |err| / max |ref| = {rel:.2e}")
+    assert_close(got, ref, "float32", f"fp32 gemm {batch}x{m}x{k}x{n} kmajor {kmajor}")
 
 
 @pytest.mark.parametrize("m,k,n,bn,kmajor,batch", [
