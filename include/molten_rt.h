@@ -159,7 +159,9 @@ int molten_encode_tma_2d(void* tmap, int dtype, const void* base,
  * (allocated on first use, then reused). */
 int molten_status_word(int device, int** dev_ptr);
 
-/* Read (and when reset != 0 clear) the device error word; synchronises. */
+/* Read (and when reset != 0 clear) the device error word; synchronises.
+ * The value also carries the bits of molten_scores_softmax_bf16_noalloc's own
+ * word on that device (that entry point may not allocate this one). */
 int molten_read_status(int device, int* value, int reset);
 
 /* Allocation-free attention-score rows (no counterpart in the reference):
@@ -173,7 +175,9 @@ int molten_read_status(int device, int* value, int reset);
  * (MOLTEN_ERR_INVALID otherwise).  Calls share that array: calls that overlap
  * on the GPU race.  n and kdim must be multiples of 8, pointers 16-byte
  * aligned.  The first call on a device resolves the array's address, so make
- * it before any stream capture.  Runs on the current device and `stream`. */
+ * it before any stream capture.  Runs on the current device and `stream`.
+ * A bounded wait that runs out inside it is reported by molten_read_status,
+ * as for every other kernel; its status bits stay set until read with reset. */
 #define MOLTEN_NOALLOC_SCORES_MAX_ELEMENTS (8LL * 1024 * 1024)
 int molten_scores_softmax_bf16_noalloc(const void* q, const void* k, void* out,
                                        long long m, long long n, long long kdim,

@@ -20,13 +20,16 @@
 //   * The first call on a device resolves the arrays' device addresses with
 //     cudaGetSymbolAddress and sets the GEMM kernel's shared-memory limit;
 //     make that first call before any stream capture begins.
+//   * A bounded wait that runs out inside the GEMM sets a bit in this file's
+//     status word, which stays set until it is read: molten_read_status
+//     reports it together with the runtime's own word (and clears both when
+//     asked to), so callers check these calls the same way as any other.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstring>
 #include <mutex>
 #include <string>
-#include <vector>
 
 #include "molten_rt.h"
 #include "molten/gemm_sm100.cuh"
@@ -42,7 +45,7 @@ constexpr int kBN = 128, kStages = 6;
 typedef molten::GemmLayout<128, kBN, 64, kStages, 16> ScoresLayout;
 
 // The scratch: the fp32 score rows between the two kernels, and the GEMM's
-// bounded-wait error word (cleared by every call).
+// bounded-wait error word (element 0; zero at load, sticky until read).
 static __device__ __align__(256) float g_scores_scratch[kMaxElements];
 static __device__ __align__(256) int g_scores_status[64];
 
@@ -120,8 +123,12 @@ struct DeviceSetup {
   int sms = 0;
 };
 
+// One slot per device ordinal, in storage that never moves: a pointer
+// handed out by setup_device stays valid while other threads set up other
+// devices.
+constexpr int kMaxDevices = 64;
 std::mutex g_mu;
-std::vector<DeviceSetup> g_setup;
+DeviceSetup g_setup[kMaxDevices];
 
 int fail(int code, const std::string& msg) {
   molten_internal_set_error(msg.c_str());       // read back with molten_last_error()
@@ -136,8 +143,10 @@ int cuda_err(cudaError_t e, const char* what) {
 // scratch arrays (in host code their names are only host-side stand-ins),
 // the SM count and the GEMM kernel's dynamic shared-memory limit.
 int setup_device(int dev, DeviceSetup** out) {
+  if (dev < 0 || dev >= kMaxDevices)
+    return fail(MOLTEN_ERR_INVALID, "device ordinal " + std::to_string(dev) + " beyond " +
+                                        std::to_string(kMaxDevices));
   std::lock_guard<std::mutex> lock(g_mu);
-  if ((int)g_setup.size() <= dev) g_setup.resize(dev + 1);
   DeviceSetup& d = g_setup[dev];
   if (!d.ready) {
     cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&d.scratch), g_scores_scratch);
@@ -156,6 +165,30 @@ int setup_device(int dev, DeviceSetup** out) {
 }
 
 }  // namespace
+
+// Read (and when reset != 0 clear) this file's status word on `device`;
+// 0 when no allocation-free call ever ran there.  Called by
+// molten_read_status, which ORs the value into the runtime's own word.
+int molten_internal_noalloc_status(int device, int* value, int reset) {
+  *value = 0;
+  if (device < 0 || device >= kMaxDevices) return MOLTEN_OK;
+  int* word = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!g_setup[device].ready) return MOLTEN_OK;
+    word = g_setup[device].status;
+  }
+  int prev = 0;
+  cudaError_t e = cudaGetDevice(&prev);
+  if (e != cudaSuccess) return cuda_err(e, "cudaGetDevice");
+  if (prev != device && (e = cudaSetDevice(device)) != cudaSuccess)
+    return cuda_err(e, "cudaSetDevice");
+  e = cudaMemcpy(value, word, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && reset && *value) e = cudaMemset(word, 0, sizeof(int));
+  if (prev != device) cudaSetDevice(prev);
+  if (e != cudaSuccess) return cuda_err(e, "reading the allocation-free status word");
+  return MOLTEN_OK;
+}
 
 extern "C" int molten_scores_softmax_bf16_noalloc(const void* q, const void* k, void* out,
                                                   long long m, long long n, long long kdim,
@@ -191,8 +224,6 @@ extern "C" int molten_scores_softmax_bf16_noalloc(const void* q, const void* k, 
   args.k = kdim;
   args.status = d->status;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  e = cudaMemsetAsync(d->status, 0, sizeof(int), st);
-  if (e != cudaSuccess) return cuda_err(e, "clearing the status word");
   const long long tiles = ((m + 127) / 128) * ((n + kBN - 1) / kBN);
   const unsigned grid = (unsigned)(tiles < d->sms ? tiles : d->sms);
   scores_gemm_noalloc<<<grid, dim3(128, 2), ScoresLayout::SMEM_BYTES, st>>>(args);

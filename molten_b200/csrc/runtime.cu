@@ -172,6 +172,9 @@ std::vector<int*> g_status;
 // molten_last_error() (C++ linkage: not part of the C ABI).
 void molten_internal_set_error(const char* msg) { g_last_error = msg ? msg : ""; }
 
+// The allocation-free entry point's own wait-status word (noalloc_scores.cu).
+int molten_internal_noalloc_status(int device, int* value, int reset);
+
 extern "C" {
 
 int molten_version(void) { return 101; }
@@ -465,6 +468,12 @@ int molten_read_status(int device, int* value, int reset) {
     e = cudaMemset(p, 0, sizeof(int));
     if (e != cudaSuccess) return cuda_fail(e, "clearing the status word");
   }
+  // the allocation-free entry point keeps its own word (it may not allocate
+  // this one); its bits are reported here too
+  int extra = 0;
+  rc = molten_internal_noalloc_status(device, &extra, reset);
+  if (rc) return rc;
+  *value |= extra;
   return MOLTEN_OK;
 }
 

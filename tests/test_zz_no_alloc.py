@@ -7,15 +7,18 @@ must not allocate after start-up.  For them the library offers one entry
 point that keeps its fp32 intermediate (the Q @ K scores between the GEMM and
 the row softmax) in a fixed device array instead of asking for memory.
 
-Checked here through the C ABI: two calls in a row match the regular path --
-the generated GEMM + row-softmax kernels launched with molten_launch, whose
-intermediate comes from the caller's allocator -- within the bf16 parity bar
-of the other GPU tests, and a call larger than the array is refused before
-anything is launched.  This file runs last so that a failure here cannot
-hide the results of the other tests.
+Checked here through the C ABI: two calls in a row match the oracle (the CPU
+restatement of the reference's softmax(matmul) semantics) and the regular
+path -- the generated GEMM + row-softmax kernels launched with molten_launch,
+whose intermediate comes from the caller's allocator -- within the bf16
+parity bar of the other GPU tests; no bounded wait ran out (the status bits
+molten_read_status reports); and a call larger than the array is refused
+before anything is launched.  This file runs last so that a failure here
+cannot hide the results of the other tests.
 """
 import ctypes
 
+import numpy as np
 import pytest
 
 torch = pytest.importorskip("torch")
@@ -24,6 +27,7 @@ from molten_b200 import _capi
 from molten_b200.codegen import compile_graph
 from molten_b200.ir import DataflowGraph, TensorShape
 from molten_b200.runtime import MoltenRuntime
+from oracle import graph_oracle as orc
 from tests._golden import assert_close
 
 pytestmark = pytest.mark.gpu
@@ -53,11 +57,18 @@ def test_noalloc_scores_match_the_regular_path():
             ctypes.c_void_p(q.data_ptr()), ctypes.c_void_p(k.data_ptr()),
             ctypes.c_void_p(out.data_ptr()), m, n, kd, ctypes.c_void_p(stream))
         assert rc == 0, _capi.last_error()
-        ck = rt.compile(compile_graph(scores_graph(m, kd, n), dtype="bfloat16")[0])
+        g = scores_graph(m, kd, n)
+        ck = rt.compile(compile_graph(g, dtype="bfloat16")[0])
         ref = ck(q, k)
         torch.cuda.synchronize()
-        assert_close(out.float().cpu().numpy(), ref.float().cpu().numpy(), "bfloat16",
-                     f"no-alloc scores {m}x{kd}x{n}")
+        assert MoltenRuntime.read_status(0) == 0, "a bounded wait ran out"
+        got = out.float().cpu().numpy()
+        assert_close(got, ref.float().cpu().numpy(), "bfloat16",
+                     f"no-alloc scores {m}x{kd}x{n} vs the regular path")
+        bits = {nm: t.cpu().view(torch.int16).numpy().view(np.uint16) for nm, t in (("q", q), ("k", k))}
+        res = orc.evaluate(g, bits)
+        assert_close(got, res[("f32", g.ops[g._outputs[0]].inputs[0])], "bfloat16",
+                     f"no-alloc scores {m}x{kd}x{n} vs the oracle")
 
 
 def test_noalloc_scores_refuse_sizes_beyond_the_array():
