@@ -54,7 +54,9 @@ def default_cache_dir() -> Path:
     d = PKG_DIR / "_kcache"
     try:
         d.mkdir(exist_ok=True)
-        probe = d / ".w"
+        # a probe per process and thread: concurrent builders must not
+        # remove each other's probe
+        probe = d / f".w.{os.getpid()}.{threading.get_ident()}"
         probe.write_text("")
         probe.unlink()
         return d

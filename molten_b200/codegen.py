@@ -99,6 +99,8 @@ def launch_records(plan: GroupPlan, name: str) -> list:
             rec.update(block=c["block"], rpc=c["rpc"], upt=c["upt"], tiles=c["tiles"], smem=0)
         elif sk.family == "rope":
             rec.update(block=c["block"], vec=c["vec"], slots_per_row=c["spr"], smem=0)
+        elif sk.family == "split3":
+            rec.update(block=c["block"], vec=c["vec"], elements=c["total"], smem=0)
         elif sk.family == "attn":
             rec.update(block=c["threads"], bm=128, bn=c["bn"], stages=c["stages"],
                        smem=c["smem_bytes"], tma_store=c["tma_store"],
@@ -107,6 +109,8 @@ def launch_records(plan: GroupPlan, name: str) -> list:
             rec.update(block=c["threads"], bm=c["bm"], bn=c["bn"], bk=c["bk"],
                        stages=c["stages"], smem=c.get("smem_bytes", 0),
                        cluster=2 if c.get("pair") else 1)
+            if c.get("split3"):
+                rec.update(split3=True)
             if c.get("streamk"):
                 rec.update(streamk=True, grid=c["sk_ctas"],
                            work_floats=c["sk_tiles"] * c["sk_maxseg"] * c["bm"] * c["bn"],
@@ -170,7 +174,7 @@ class CodeGenerator:
 
     def generate_from_plan(self, plan: GroupPlan, name: str, graph=None, group=None):
         from .emit import emit_ew, emit_row, emit_row_tma
-        from .emit_gemm import emit_gemm
+        from .emit_gemm import emit_gemm, emit_split3
         from .emit_rope import emit_rope
         from .emit_attn import emit_attn
         chunks = []
@@ -198,6 +202,8 @@ class CodeGenerator:
             elif sk.family == "rope":
                 chunks.append(emit_rope(sk, entry))
                 block_x = sk.config["block"]
+            elif sk.family == "split3":
+                chunks.append(emit_split3(sk, entry))
             elif sk.family == "attn":
                 chunks.append(emit_attn(sk, entry))
                 block_x, block_y = sk.config["threads"], 1

@@ -138,7 +138,9 @@ __device__ __forceinline__ void gemm2_init(const GemmShared& s, const GemmArgs& 
 
 // The roles.  Epi::apply(args, row, col0, acc[32]) as in gemm_roles.
 // B_KMAJOR: tmap_b describes Bt [N, K] (inner K) with box {64, BN/2}.
-template <class L, bool F16IN, class Epi, bool B_KMAJOR = false>
+// SPLIT3: fp32 operands as stacked bf16 planes, six products per k-block
+// (see gemm_roles in molten/gemm_sm100.cuh).
+template <class L, bool F16IN, class Epi, bool B_KMAJOR = false, bool SPLIT3 = false>
 __device__ __forceinline__ void gemm2_roles(const GemmShared& s, const GemmArgs& args) {
   tc_fence_after();
   const int tid = gemm_tid(), warp = tid / 32, lane = tid % 32;
@@ -149,6 +151,7 @@ __device__ __forceinline__ void gemm2_roles(const GemmShared& s, const GemmArgs&
   const long long NB = (args.n + L::BN - 1) / L::BN;
   const long long T = (args.batch > 1 ? args.batch : 1) * MB * NB;
   const int KB = (int)((args.k + L::BK - 1) / L::BK);
+  const int KSTEPS = SPLIT3 ? kSplit3Products * KB : KB;     // k-blocks per tile
   const long long pair = blockIdx.x / 2, pairs = gridDim.x / 2;
 
   if (warp == 0) {
@@ -159,9 +162,12 @@ __device__ __forceinline__ void gemm2_roles(const GemmShared& s, const GemmArgs&
       for (long long tile = pair; tile < T && !*s.abort_flag; tile += pairs) {
         int m0, n0, h;
         gemm_tile_coords<L>(tile, MB, NB, m0, n0, h);
-        const int a_row = (int)(h * args.m) + m0 + (int)rank * L::CTA_M;
+        const int nb = args.batch > 1 ? args.batch : 1;
         const int b_col = n0 + (int)rank * L::B_COLS;
-        for (int kb = 0; kb < KB; ++kb) {
+        for (int ks = 0; ks < KSTEPS; ++ks) {
+          int kb = ks, pa = 0, pb = 0;
+          if constexpr (SPLIT3) split3_step(ks, KB, kb, pa, pb);
+          const int a_row = (int)((pa * nb + h) * args.m) + m0 + (int)rank * L::CTA_M;
           if (!mbar_wait(bar.empty(st), ph ^ 1u)) { gemm_fail(s, args, kGemmTimeoutEmpty); break; }
           if (*s.abort_flag) break;
           const uint32_t a_dst = smem_u32(s.tiles + st * L::STAGE_BYTES);
@@ -173,12 +179,13 @@ __device__ __forceinline__ void gemm2_roles(const GemmShared& s, const GemmArgs&
           if (rank == 0) mbar_expect_tx(bar.full(st), (uint32_t)(2 * L::STAGE_BYTES));
           pair_tma_load_2d(a_dst, &args.tmap_a, full0, kb * L::BK, a_row);
           if constexpr (B_KMAJOR) {
-            pair_tma_load_2d(b_dst, &args.tmap_b, full0, kb * L::BK, (int)(h * args.n) + b_col);
+            pair_tma_load_2d(b_dst, &args.tmap_b, full0, kb * L::BK,
+                             (int)((pb * nb + h) * args.n) + b_col);
           } else {
 #pragma unroll
             for (int c = 0; c < L::B_COLS / 64; ++c)
               pair_tma_load_2d(b_dst + c * L::B_CHUNK_BYTES, &args.tmap_b, full0, b_col + 64 * c,
-                               (int)(h * args.k) + kb * L::BK);
+                               (int)((pb * nb + h) * args.k) + kb * L::BK);
           }
           ++issued;
           if (++st == (uint32_t)L::STAGES) { st = 0; ph ^= 1u; }
@@ -207,7 +214,7 @@ __device__ __forceinline__ void gemm2_roles(const GemmShared& s, const GemmArgs&
         if (!mbar_wait(bar.acc_empty(b), acc_ph ^ 1u)) { gemm_fail(s, args, kGemmTimeoutAcc); break; }
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(b * L::BN);
-        for (int kb = 0; kb < KB; ++kb) {
+        for (int kb = 0; kb < KSTEPS; ++kb) {
           if (!mbar_wait(bar.full(st), ph)) { gemm_fail(s, args, kGemmTimeoutFull); ok = false; break; }
           tc_fence_after();
           const uint32_t a_base = smem_u32(s.tiles + st * L::STAGE_BYTES);

@@ -150,6 +150,38 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&r)[32]) {
   for (int i = 0; i < 32; ++i) r[i] = __uint_as_float(u[i]);
 }
 
+// ------------------------------------------------------- fp32 by bf16 planes
+// An fp32 value x is split into three bf16 values x0 + x1 + x2 (each the
+// round-to-nearest bf16 of what the previous ones left; 24 significand bits
+// in all).  The product of two such sums is taken as the six terms with
+// plane indices pa + pb <= 2; the three dropped terms and the split's
+// residues are each below 2^-24 of |a b|.  This is the bf16x3 scheme of
+// Henry, Tang and Heinecke, "Leveraging the bfloat16 Artificial Intelligence
+// Datatype For Higher-Precision Computations" (ARITH 2019).
+constexpr int kSplit3Products = 6;
+// K step ks of the six-product loop -> (k-block, A plane, B plane); the
+// products run from the smallest terms to x0 * y0.
+__device__ __forceinline__ void split3_step(int ks, int KB, int& kb, int& pa, int& pb) {
+  const int j = ks / KB;
+  kb = ks - j * KB;
+  // j:  0      1      2      3      4      5
+  //    (2,0)  (1,1)  (0,2)  (1,0)  (0,1)  (0,0)
+  pa = (0x001012 >> (4 * j)) & 0xF;
+  pb = (0x010210 >> (4 * j)) & 0xF;
+}
+
+// x -> (x0, x1, x2).  A finite x whose x0 overflows (|x| above the largest
+// bf16, ~3.39e38) becomes an infinity; an infinity or NaN is carried by x0
+// alone, so products with it are the infinity or NaN of fp32 arithmetic.
+__device__ __forceinline__ void split3_value(float x, bf16& x0, bf16& x1, bf16& x2) {
+  x0 = __float2bfloat16_rn(x);
+  const float h0 = __bfloat162float(x0);
+  const float r1 = isfinite(h0) ? x - h0 : 0.0f;      // exact
+  x1 = __float2bfloat16_rn(r1);
+  const float r2 = r1 - __bfloat162float(x1);          // exact
+  x2 = __float2bfloat16_rn(r2);
+}
+
 // ------------------------------------------------------------ the engine
 // PRO_: an RMSNorm prologue (see gemm_roles): 4 more warps, a "ready"
 // barrier per stage, a double-buffered per-row 1/rms and its barriers.
@@ -276,6 +308,106 @@ __device__ __forceinline__ void gemm_init(const GemmShared& s, const GemmArgs& a
   tc_fence_before();
 }
 
+// ---------------------------------------------- SPLIT3: promoted accumulation
+// The tensor core's fp32 accumulation loses accuracy with the length of the
+// chain it sums (measured on the six-product fp32 GEMM: 1.4e-6 of max|C| at
+// K = 1024, 4.6e-6 at K = 4096).  So the SPLIT3 K loop is cut into chunks of
+// kSplit3Chunk k-steps: the MMA issuer starts a fresh accumulator (the two
+// TMEM buffers alternate per chunk) and the epilogue warps add each chunk
+// into fp32 registers (round to nearest), one BN-column row per thread.
+constexpr int kSplit3Chunk = 4;
+
+template <class L, bool B_KMAJOR>
+__device__ __forceinline__ void gemm_split3_mma(const GemmShared& s, const GemmArgs& args,
+                                                uint32_t tmem, long long T, int KSTEPS) {
+  constexpr uint32_t IDESC = umma_idesc<L::BM, L::BN, false, B_KMAJOR>();
+  const Bars<L> bar(s);
+  uint32_t st = 0, ph = 0;
+  long long chunk = 0;
+  bool ok = true;
+  for (long long tile = blockIdx.x; tile < T && ok && !*s.abort_flag; tile += gridDim.x) {
+    for (int c0 = 0; c0 < KSTEPS && ok; c0 += kSplit3Chunk, ++chunk) {
+      const int b = (int)(chunk & 1);
+      const uint32_t acc_ph = (uint32_t)((chunk >> 1) & 1);
+      if (!mbar_wait(bar.acc_empty(b), acc_ph ^ 1u)) { gemm_fail(s, args, kGemmTimeoutAcc); ok = false; break; }
+      tc_fence_after();
+      const uint32_t d = tmem + (uint32_t)(b * L::BN);
+      const int c1 = (c0 + kSplit3Chunk < KSTEPS) ? c0 + kSplit3Chunk : KSTEPS;
+      for (int ks = c0; ks < c1; ++ks) {
+        if (!mbar_wait(bar.full(st), ph)) { gemm_fail(s, args, kGemmTimeoutFull); ok = false; break; }
+        tc_fence_after();
+        const uint32_t a_base = smem_u32(s.tiles + st * L::STAGE_BYTES);
+        const uint32_t b_base = a_base + L::A_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < L::BK / 16; ++kk) {
+          const uint64_t ad = umma_desc(a_base + 32u * kk, 16u, 1024u);
+          const uint64_t bd = B_KMAJOR
+              ? umma_desc(b_base + 32u * kk, 16u, 1024u)
+              : umma_desc(b_base + 2048u * kk, (uint32_t)L::B_CHUNK_BYTES, 1024u);
+          umma_f16(d, ad, bd, IDESC, ((ks - c0) | kk) != 0 ? 1u : 0u);
+        }
+        umma_commit(bar.empty(st));
+        if (++st == (uint32_t)L::STAGES) { st = 0; ph ^= 1u; }
+      }
+      if (ok) umma_commit(bar.acc_full(b));
+    }
+  }
+  // all MMAs this thread issued must finish before TMEM is released
+  umma_commit(bar.done());
+  if (!mbar_wait(bar.done(), 0u)) { if (args.status) atomicOr(args.status, kGemmTimeoutDrain); }
+}
+
+template <class L, class Epi>
+__device__ __forceinline__ void gemm_split3_epilogue(const GemmShared& s, const GemmArgs& args,
+                                                     uint32_t tmem, long long T, int KSTEPS,
+                                                     long long MB, long long NB) {
+  static_assert(L::BN == 128, "one 128-column accumulator row per thread");
+  const int warp = gemm_tid() / 32, lane = gemm_tid() % 32;
+  const int quarter = warp % 4;                  // TMEM lanes 32*quarter .. +31
+  const Bars<L> bar(s);
+  long long chunk = 0;
+  bool ok = true;
+  for (long long tile = blockIdx.x; tile < T && ok; tile += gridDim.x) {
+    float sum[L::BN];
+#pragma unroll
+    for (int q = 0; q < L::BN; ++q) sum[q] = 0.0f;
+#pragma unroll 1
+    for (int c0 = 0; c0 < KSTEPS; c0 += kSplit3Chunk, ++chunk) {
+      const int b = (int)(chunk & 1);
+      const uint32_t acc_ph = (uint32_t)((chunk >> 1) & 1);
+      const bool got = mbar_wait(bar.acc_full(b), acc_ph);
+      if (!__all_sync(0xffffffffu, got ? 1 : 0)) {
+        if (lane == 0) gemm_fail(s, args, kGemmTimeoutAcc);
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < L::BN / 32; ++c) {
+        float part[32];
+        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * L::BN + c * 32), part);
+#pragma unroll
+        for (int q = 0; q < 32; ++q) sum[32 * c + q] += part[q];
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar.acc_empty(b));
+    }
+    if (!ok) break;
+    int m0, n0, h;
+    gemm_tile_coords<L>(tile, MB, NB, m0, n0, h);
+    const long long mrow = (long long)m0 + quarter * 32 + lane;   // row of problem h
+    const long long row = (long long)h * args.m + mrow;           // row of stacked C
+#pragma unroll
+    for (int c = 0; c < L::BN / 32; ++c) {
+      const long long col0 = (long long)n0 + 32 * c;
+      if (col0 < args.n && mrow < args.m)
+        Epi::apply(args, row, col0, *reinterpret_cast<const float(*)[32]>(&sum[32 * c]));
+    }
+    if (__any_sync(0xffffffffu, *s.abort_flag ? 1 : 0)) break;
+  }
+}
+
 // The three roles.  Epi::apply(args, row, col0, acc[32]) writes C[row, col0..col0+31]
 // (row of the stacked C, always a valid row; columns from col0 < n).
 // B_KMAJOR: tmap_b describes Bt [N, K] (inner K) with box {64, BN}; a stage
@@ -289,7 +421,13 @@ __device__ __forceinline__ void gemm_init(const GemmShared& s, const GemmArgs& a
 // the stage's "ready" barrier, which the MMA waits for instead of "full".
 // After a tile's K loop they publish 1/rms per row; the epilogue scales the
 // accumulator rows by it.
-template <class L, bool F16IN, class Epi, bool B_KMAJOR = false, class Pro = NoPrologue>
+// SPLIT3: fp32 operands given as three bf16 planes each (x ~ x0 + x1 + x2,
+// split3_planes), stacked by rows: A planes [3 * batch*m, k], B planes
+// [3 * batch*k, n] (or Bt planes [3 * batch*n, k]).  The K loop runs over the
+// six products with plane indices pa + pb <= 2 (smallest first), so the
+// accumulator holds A @ B to about fp32 accuracy.
+template <class L, bool F16IN, class Epi, bool B_KMAJOR = false, class Pro = NoPrologue,
+          bool SPLIT3 = false>
 __device__ __forceinline__ void gemm_roles(const GemmShared& s, const GemmArgs& args) {
   tc_fence_after();
   const int tid = gemm_tid(), warp = tid / 32, lane = tid % 32;
@@ -299,6 +437,7 @@ __device__ __forceinline__ void gemm_roles(const GemmShared& s, const GemmArgs& 
   const long long NB = (args.n + L::BN - 1) / L::BN;
   const long long T = (args.batch > 1 ? args.batch : 1) * MB * NB;
   const int KB = (int)((args.k + L::BK - 1) / L::BK);
+  const int KSTEPS = SPLIT3 ? kSplit3Products * KB : KB;     // k-blocks per tile
   // Batched problems are stacked: A [batch*m, k], B [batch*k, n] (or
   // Bt [batch*n, k]), C [batch*m, n].  A tile of problem h that runs past its
   // m rows (or n columns) reads the next problem's rows; those products land
@@ -313,21 +452,34 @@ __device__ __forceinline__ void gemm_roles(const GemmShared& s, const GemmArgs& 
       for (long long tile = blockIdx.x; tile < T && !*s.abort_flag; tile += gridDim.x) {
         int m0, n0, h;
         gemm_tile_coords<L>(tile, MB, NB, m0, n0, h);
-        const int a_row = (int)(h * args.m) + m0;
-        for (int kb = 0; kb < KB; ++kb) {
+        const int nb = args.batch > 1 ? args.batch : 1;
+        for (int ks = 0; ks < KSTEPS; ++ks) {
+          int kb = ks, pa = 0, pb = 0;
+          if constexpr (SPLIT3) split3_step(ks, KB, kb, pa, pb);
+          const int a_row = (int)((pa * nb + h) * args.m) + m0;
           if (!mbar_wait(bar.empty(st), ph ^ 1u)) { gemm_fail(s, args, kGemmTimeoutEmpty); break; }
           if (*s.abort_flag) break;
+#ifdef MOLTEN_TEST_SKIP_KSTEP
+          // Failure-detection test builds only: k-step MOLTEN_TEST_SKIP_KSTEP
+          // of this CTA's first tile is neither armed nor copied, so the MMA
+          // issuer's bounded wait for that stage runs out.
+          if (tile == (long long)blockIdx.x && ks == MOLTEN_TEST_SKIP_KSTEP) {
+            if (++st == (uint32_t)L::STAGES) { st = 0; ph ^= 1u; }
+            continue;
+          }
+#endif
           const uint32_t a_dst = smem_u32(s.tiles + st * L::STAGE_BYTES);
           const uint32_t b_dst = a_dst + L::A_BYTES;
           mbar_expect_tx(bar.full(st), (uint32_t)L::STAGE_BYTES);
           tma_load_2d(a_dst, &args.tmap_a, bar.full(st), kb * L::BK, a_row);
           if constexpr (B_KMAJOR) {
-            tma_load_2d(b_dst, &args.tmap_b, bar.full(st), kb * L::BK, (int)(h * args.n) + n0);
+            tma_load_2d(b_dst, &args.tmap_b, bar.full(st), kb * L::BK,
+                        (int)((pb * nb + h) * args.n) + n0);
           } else {
 #pragma unroll
             for (int c = 0; c < L::BN / 64; ++c)
               tma_load_2d(b_dst + c * L::B_CHUNK_BYTES, &args.tmap_b, bar.full(st), n0 + 64 * c,
-                          (int)(h * args.k) + kb * L::BK);
+                          (int)((pb * nb + h) * args.k) + kb * L::BK);
           }
           ++issued;
           if (++st == (uint32_t)L::STAGES) { st = 0; ph ^= 1u; }
@@ -344,7 +496,9 @@ __device__ __forceinline__ void gemm_roles(const GemmShared& s, const GemmArgs& 
     }
   } else if (warp == 1) {
     // ----------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    if (SPLIT3 && lane == 0) {
+      gemm_split3_mma<L, B_KMAJOR>(s, args, tmem, T, KSTEPS);
+    } else if (lane == 0) {
       constexpr uint32_t IDESC = umma_idesc<L::BM, L::BN, F16IN, B_KMAJOR>();
       uint32_t st = 0, ph = 0;
       long long i = 0;
@@ -355,7 +509,7 @@ __device__ __forceinline__ void gemm_roles(const GemmShared& s, const GemmArgs& 
         if (!mbar_wait(bar.acc_empty(b), acc_ph ^ 1u)) { gemm_fail(s, args, kGemmTimeoutAcc); break; }
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(b * L::BN);
-        for (int kb = 0; kb < KB; ++kb) {
+        for (int kb = 0; kb < KSTEPS; ++kb) {
           const uint32_t in_bar = Pro::ENABLED ? bar.ready(st) : bar.full(st);
           if (!mbar_wait(in_bar, ph)) { gemm_fail(s, args, kGemmTimeoutFull); ok = false; break; }
           tc_fence_after();
@@ -446,6 +600,10 @@ __device__ __forceinline__ void gemm_roles(const GemmShared& s, const GemmArgs& 
     }
   } else if (warp >= L::EPI_WARP0 && warp < L::EPI_WARP0 + L::EPI_WARPS) {
     // ------------------------------------------------------------- epilogue
+    if constexpr (SPLIT3) {
+      gemm_split3_epilogue<L, Epi>(s, args, tmem, T, KSTEPS, MB, NB);
+      return;
+    }
     const int quarter = warp % 4;                  // TMEM lanes 32*quarter .. +31
     long long i = 0;
     for (long long tile = blockIdx.x; tile < T; tile += gridDim.x, ++i) {

@@ -17,7 +17,9 @@ def emit_gemm(sk: SubKernel, name: str) -> str:
     cfg = sk.config
     BM, BN, BK, ST = cfg["bm"], cfg["bn"], cfg["bk"], cfg["stages"]
     a = sk.operands[sk.a_operand]
-    f16in = "true" if a.dtype == "float16" else "false"
+    split3 = "true" if cfg.get("split3") else "false"
+    # fp32 operands reach the tensor cores as bf16 planes
+    f16in = "true" if a.dtype == "float16" and not cfg.get("split3") else "false"
     values = sk.values
     needed = set(cfg["needed"])
     L = []
@@ -26,6 +28,8 @@ def emit_gemm(sk: SubKernel, name: str) -> str:
     w(f"// Molten sm_100a tcgen05 GEMM + epilogue: {name}")
     w(f"// C[{sk.m}, {sk.n}] = epilogue(A[{sk.m}, {sk.k}] @ B[{sk.k}, {sk.n}]); "
       f"tile {BM}x{BN}x{BK}, {ST} stages" + ("; SM pair (cta_group::2)" if pair else ""))
+    if cfg.get("split3"):
+        w("// fp32 operands as three bf16 planes each (bf16x3: six products per k-block)")
     streamk = bool(cfg.get("streamk"))
     w("#include \"molten/gemm2_sm100.cuh\"" if pair else
       ("#include \"molten/gemm_sk_sm100.cuh\"" if streamk else "#include \"molten/gemm_sm100.cuh\""))
@@ -156,7 +160,7 @@ def emit_gemm(sk: SubKernel, name: str) -> str:
         w(f"  const GemmShared sh = gemm2_carve<Layout_{name}>(smem_raw);")
         w(f"  gemm2_init<Layout_{name}>(sh, args);    // mbarriers, pair TMEM allocation, pair barrier")
         w("  pdl_enter();                            // no global access before this")
-        w(f"  gemm2_roles<Layout_{name}, {f16in}, Epilogue_{name}, {kmaj}>(sh, args);")
+        w(f"  gemm2_roles<Layout_{name}, {f16in}, Epilogue_{name}, {kmaj}, {split3}>(sh, args);")
         w("  __syncthreads();")
         w(f"  gemm2_teardown<Layout_{name}>(sh);      // pair barrier, pair TMEM release")
         w("}")
@@ -178,9 +182,48 @@ def emit_gemm(sk: SubKernel, name: str) -> str:
     w("  __syncthreads();")
     kmaj = "true" if cfg.get("b_kmajor") else "false"
     pro_t = f"Prologue_{name}" if pro else "NoPrologue"
-    w(f"  gemm_roles<Layout_{name}, {f16in}, Epilogue_{name}, {kmaj}, {pro_t}>(sh, args);")
+    w(f"  gemm_roles<Layout_{name}, {f16in}, Epilogue_{name}, {kmaj}, {pro_t}, {split3}>(sh, args);")
     w("  __syncthreads();")
     w(f"  gemm_teardown<Layout_{name}>(sh);       // TMEM release")
+    w("}")
+    return "\n".join(L) + "\n"
+
+
+def emit_split3(sk: SubKernel, name: str) -> str:
+    """Kernel writing a GEMM operand as three stacked bf16 planes
+    (x ~ x0 + x1 + x2, molten::split3_value): grid-stride over VEC-element
+    slots, one read of the operand and three 16-byte plane stores per slot."""
+    cfg = sk.config
+    src = sk.operands[0]
+    ct = DTYPE_CTYPE[src.dtype]
+    total, vec = cfg["total"], cfg["vec"]
+    L = []
+    w = L.append
+    w(f"// Molten sm_100a: {name} -- operand {src.name!r} {list(src.shape)} {src.dtype} "
+      f"-> bf16 planes [3, {total}]")
+    w("#include \"molten/gemm_sm100.cuh\"")
+    w("#include \"molten/row_engine.cuh\"")
+    w("")
+    w("using namespace molten;")
+    w("")
+    w(f"extern \"C\" __global__ void __launch_bounds__({cfg['block']}) "
+      f"{name}(const __grid_constant__ RowArgs args) {{")
+    w("  pdl_enter();")
+    w(f"  constexpr long long TOTAL = {total}LL;")
+    w(f"  constexpr int VEC = {vec};")
+    w(f"  const {ct}* __restrict__ x = static_cast<const {ct}*>(args.in[0]);")
+    w("  bf16* __restrict__ p = static_cast<bf16*>(args.out[0]);")
+    w("  const long long step = (long long)gridDim.x * blockDim.x;")
+    w("  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < TOTAL / VEC; "
+      "i += step) {")
+    w(f"    const Slot<{ct}, VEC> v = load_slot<kLoadStream, {ct}, VEC>(x + i * VEC);")
+    w("    Slot<bf16, VEC> s0, s1, s2;")
+    w("#pragma unroll")
+    w("    for (int e = 0; e < VEC; ++e) split3_value(to_f32(v.v[e]), s0.v[e], s1.v[e], s2.v[e]);")
+    w("    store_slot<kStoreDefault, bf16, VEC>(p + i * VEC, s0);")
+    w("    store_slot<kStoreDefault, bf16, VEC>(p + TOTAL + i * VEC, s1);")
+    w("    store_slot<kStoreDefault, bf16, VEC>(p + 2 * TOTAL + i * VEC, s2);")
+    w("  }")
     w("}")
     return "\n".join(L) + "\n"
 

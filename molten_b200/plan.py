@@ -116,7 +116,20 @@ def plan_group(graph: DataflowGraph, group_op_ids, input_shapes: dict,
                 if o not in mm_operands:
                     storage[o] = "float32"
                 temps[o] = (shapes[o], storage[o])
-        kernels.append(_plan_sub(graph, family, ops, sk_ext, sk_outs, shapes, storage, tune))
+        sub = _plan_sub(graph, family, ops, sk_ext, sk_outs, shapes, storage, tune)
+        if sub.family == "gemm" and sub.config.get("split3"):
+            # fp32 operands: a kernel before the GEMM writes each as three
+            # stacked bf16 planes, which the GEMM's TMA copies read
+            planes = []
+            for idx in (sub.a_operand, sub.b_operand):
+                opd = sub.operands[idx]
+                key = ("split3", opd.op_id)
+                if key not in temps:
+                    temps[key] = ((3,) + tuple(int(d) for d in opd.shape), "bfloat16")
+                    kernels.append(_plan_split3(opd, key))
+                planes.append(key)
+            sub.config["planes"] = planes
+        kernels.append(sub)
 
     return GroupPlan(
         name=name, inputs=inputs,
@@ -125,6 +138,25 @@ def plan_group(graph: DataflowGraph, group_op_ids, input_shapes: dict,
         outputs=list(outs), output_dtypes=[dts[o] for o in outs],
         output_shapes=[shapes[o] for o in outs],
         kernels=kernels, temps=temps)
+
+
+SPLIT3_BLOCK = 256
+
+
+def _plan_split3(opd: Operand, key) -> SubKernel:
+    """The kernel that writes GEMM operand ``opd`` (fp32, or 16-bit next to
+    an fp32 operand) as three bf16 planes x0, x1, x2 with x ~ x0 + x1 + x2,
+    stacked as [3, *shape] (molten/gemm_sm100.cuh, SPLIT3)."""
+    shape = tuple(int(d) for d in opd.shape)
+    cols = shape[-1]
+    rows = prod(shape[:-1]) if len(shape) > 1 else 1
+    src = Operand(index=0, op_id=opd.op_id, name=opd.name, dtype=opd.dtype, shape=shape,
+                  last="vec", row_map="full", row_terms=())
+    out = OutputSpec(index=0, op_id=key, dtype="bfloat16", shape=(3,) + shape, kind="full")
+    sk = SubKernel(family="split3", op_ids=[], operands=[src], outputs=[out], rows=rows, cols=cols)
+    total = rows * cols
+    sk.config = {"block": SPLIT3_BLOCK, "total": total, "vec": 4 if total % 4 == 0 else 1}
+    return sk
 
 
 def _plan_sub(graph, family, ops, ext, outs, shapes, dts, tune) -> SubKernel:
@@ -414,7 +446,11 @@ def _plan_gemm(graph, ops, ext, outs, shapes, dts, tune) -> SubKernel:
     M = int(a_shape[-2]) if batch > 1 else prod(a_shape[:-1])
     if batch > 1 and prologue is not None:
         raise LoweringError("the RMSNorm prologue takes an unbatched B")
-    if max(batch * M, batch * K, batch * N) >= 2 ** 31:
+    # fp32 operands run on the bf16 tensor cores as three bf16 planes each
+    split3 = "float32" in (dts[a_id], dts[b_id])
+    if split3 and prologue is not None:
+        raise LoweringError("the RMSNorm prologue takes 16-bit GEMM operands")
+    if (3 if split3 else 1) * max(batch * M, batch * K, batch * N) >= 2 ** 31:
         raise LoweringError("GEMM rows beyond the 32-bit TMA coordinate range")
     it = shapes[mm]
     for o in ops:
@@ -443,8 +479,8 @@ def _plan_gemm(graph, ops, ext, outs, shapes, dts, tune) -> SubKernel:
             b_idx = operands[-1].index
     if a_id == b_id:
         b_idx = a_idx
-    if dts[a_id] != dts[b_id] or dts[a_id] == "float32":
-        raise LoweringError("the tensor-core GEMM takes bf16 x bf16 or fp16 x fp16 operands")
+    if not split3 and dts[a_id] != dts[b_id]:
+        raise LoweringError("the tensor-core GEMM takes bf16 x bf16, fp16 x fp16 or fp32 operands")
     if prologue is not None:
         w_id = prologue["w_op"]
         w_shape = tuple(int(v) for v in shapes[w_id])
@@ -470,8 +506,15 @@ def _plan_gemm(graph, ops, ext, outs, shapes, dts, tune) -> SubKernel:
     if any(values[v].avail for v in needed):
         raise LoweringError("GEMM epilogues are elementwise only")
     from .gemm_config import choose_gemm_config
-    sk.config = choose_gemm_config(sk, tune.get("gemm") or {}, batch=batch,
-                                   allow_pair=prologue is None, allow_streamk=prologue is None)
+    gemm_tune = dict(tune.get("gemm") or {})
+    if split3:
+        # the one-SM engine with 128-column tiles: its epilogue warps sum the
+        # promoted accumulator chunks, one 128-column row per thread
+        gemm_tune.update(pair=False, bn=128)
+    sk.config = choose_gemm_config(sk, gemm_tune, batch=batch,
+                                   allow_pair=prologue is None and not split3,
+                                   allow_streamk=prologue is None and not split3)
+    sk.config["split3"] = split3
     sk.config["b_kmajor"] = bool(b_kmajor)
     sk.config["batch"] = int(batch)
     if prologue is not None:

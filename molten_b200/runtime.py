@@ -131,6 +131,15 @@ class _Spec:
             cfg.block[:] = [c["block"], 1, 1]
             cfg.cluster[:] = [1, 1, 1]
             cfg.smem_bytes = 0
+        elif sk.family == "split3":
+            # grid-stride over the operand's VEC-element slots, 8 CTAs per SM
+            torch = _torch()
+            sms = torch.cuda.get_device_properties(device).multi_processor_count
+            slots = -(-c["total"] // c["vec"])
+            cfg.grid[:] = [max(1, min(-(-slots // c["block"]), 8 * sms)), 1, 1]
+            cfg.block[:] = [c["block"], 1, 1]
+            cfg.cluster[:] = [1, 1, 1]
+            cfg.smem_bytes = 0
         elif sk.family == "attn":
             # persistent: one CTA per SM (the tile's shared memory allows one)
             torch = _torch()
@@ -240,21 +249,29 @@ class _Spec:
                 a = self._attn_args(sk, env, di)
             elif sk.family == "gemm":
                 a = _capi.GemmArgs()
-                A = env[sk.operands[sk.a_operand].op_id]
-                B = env[sk.operands[sk.b_operand].op_id]
                 dt = sk.operands[sk.a_operand].dtype
                 nb = sk.config.get("batch", 1)
+                planes = 1
+                if sk.config.get("split3"):
+                    # fp32 operands: the three stacked bf16 planes the split
+                    # kernels before this one wrote
+                    A, B = (env[key] for key in sk.config["planes"])
+                    dt, planes = "bfloat16", 3
+                else:
+                    A = env[sk.operands[sk.a_operand].op_id]
+                    B = env[sk.operands[sk.b_operand].op_id]
                 A2 = A.reshape(-1, A.shape[-1])
-                ctypes.memmove(a.tmap_a, self.tmap(A2, dt, nb * sk.m, sk.k, 64, 128), 128)
+                ctypes.memmove(a.tmap_a, self.tmap(A2, dt, planes * nb * sk.m, sk.k, 64, 128), 128)
                 if sk.config.get("b_kmajor"):
                     # B is the transpose of Bt [(batch x) N, K]: its rows, K-major
                     # (an SM pair's CTA stages BN/2 of them)
                     B2 = B.reshape(-1, B.shape[-1])
                     rows_b = sk.config["bn"] // (2 if sk.config.get("pair") else 1)
-                    ctypes.memmove(a.tmap_b, self.tmap(B2, dt, nb * sk.n, sk.k, 64, rows_b), 128)
+                    ctypes.memmove(a.tmap_b, self.tmap(B2, dt, planes * nb * sk.n, sk.k, 64, rows_b),
+                                   128)
                 else:
                     B2 = B.reshape(-1, B.shape[-1])
-                    ctypes.memmove(a.tmap_b, self.tmap(B2, dt, nb * sk.k, sk.n, 64, 64), 128)
+                    ctypes.memmove(a.tmap_b, self.tmap(B2, dt, planes * nb * sk.k, sk.n, 64, 64), 128)
                 a.m, a.n, a.k = sk.m, sk.n, sk.k
                 a.batch = nb
                 a.status = _capi.status_word(di)
@@ -312,6 +329,10 @@ def _alignment_rules(sk):
     if sk.family == "gemm":
         ins = [16 if o.last == "vec" else DTYPE_SIZE[o.dtype] for o in sk.operands]
         return ins, [16 for _ in sk.outputs]
+    if sk.family == "split3":
+        # VEC-element slots of the operand; plane stores of VEC bf16
+        return ([min(16, c["vec"] * DTYPE_SIZE[sk.operands[0].dtype])],
+                [min(16, 2 * c["vec"])])
     if sk.family == "rope":
         if c["scalar"]:
             return ([DTYPE_SIZE[o.dtype] for o in sk.operands],
@@ -421,7 +442,8 @@ class CompiledKernel:
         plan = spec.plan
         gemm_b = set()
         for sk in plan.kernels:
-            if sk.family == "gemm":
+            if sk.family == "gemm" and not sk.config.get("split3"):
+                # (an fp32 B is read whole by its split kernel: contiguous)
                 gemm_b.add(sk.operands[sk.b_operand].op_id)
         out = []
         for op_id, t in zip(plan.inputs, tensors):

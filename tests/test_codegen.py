@@ -41,10 +41,15 @@ def test_matmul_kernel_source():
     a = g.add_input("a", TS([64, 128]))
     b = g.add_input("b", TS([128, 64]))
     g.add_output(g.matmul(a, b))
-    k = compile_graph(g, dtype="bfloat16")[0]
+    k = compile_graph(g)[0]                   # the reference's default: fp32
     assert "TILE" in k.source and "__syncthreads" in k.source
     assert "gemm_roles<" in k.source and "molten/gemm_sm100.cuh" in k.source
     assert k.config.block_size_y > 1          # the reference's "matmul" marker
+    # fp32 operands: split into bf16 planes, then the bf16x3 tensor-core GEMM
+    assert [sk.family for sk in k.plan.kernels] == ["split3", "split3", "gemm"]
+    assert k.plan.kernels[2].config["split3"]
+    kb = compile_graph(g, dtype="bfloat16")[0]
+    assert [sk.family for sk in kb.plan.kernels] == ["gemm"]
 
 
 def test_rms_norm_kernel_and_transformer_block():
@@ -62,11 +67,15 @@ def test_rms_norm_kernel_and_transformer_block():
     q = g.add_input("q", TS([4, 512]))
     k = g.add_input("k", TS([512, 4]))
     g.add_output(g.softmax(g.matmul(q, k)))
-    ks = compile_graph(g, dtype="bfloat16")
+    ks = compile_graph(g)
     assert len(ks) >= 1 and all(k.source and k.name for k in ks)
-    # MATMUL -> SOFTMAX is one fusion group run as GEMM + row kernel
+    # MATMUL -> SOFTMAX is one fusion group run as GEMM + row kernel (fp32:
+    # after the kernels that split q and k into bf16 planes)
     fams = [sk.family for sk in ks[1].plan.kernels]
-    assert fams == ["gemm", "row"] and "_k0" in ks[1].source and "_k1" in ks[1].source
+    assert fams == ["split3", "split3", "gemm", "row"] and "_k0" in ks[1].source \
+        and "_k3" in ks[1].source
+    fams = [sk.family for sk in compile_graph(g, dtype="bfloat16")[1].plan.kernels]
+    assert fams == ["gemm", "row"]
 
 
 def test_names_follow_reference_rule():
@@ -270,7 +279,7 @@ def test_attention_score_unfused_plan(tmp_path):
     gemm, row = k.plan.kernels
     assert gemm.family == "gemm" and gemm.config["b_kmajor"] and (gemm.m, gemm.n, gemm.k) == (256, 512, 128)
     assert row.family == "row"
-    assert ", true, NoPrologue>(sh, args)" in k.source
+    assert ", true, NoPrologue, false>(sh, args)" in k.source
     assert build_cubin(k.source, k.name, tmp_path).stat().st_size > 1000
 
 
@@ -317,10 +326,30 @@ def test_rope_after_rmsnorm_splits_the_group():
     assert k.name == "molten_fused_rms_div_mul_rotate"
 
 
-def test_float32_gemm_is_rejected():
+def test_float32_gemm_runs_as_bf16_planes():
+    """fp32 GEMM operands (the reference's default dtype) are split into
+    three bf16 planes by a kernel each, then the tensor-core GEMM takes the
+    six plane products; an fp32 x bf16 pair is split too, bf16 x fp16 is not
+    a GEMM the tensor cores take, and the RMSNorm prologue wants 16-bit x."""
     g = graphs.gemm_bias_gelu(64, 64, 64, dtype="float32")
+    (k,) = compile_graph(g, dtype="float32")
+    split_a, split_b, gemm = k.plan.kernels
+    assert (split_a.family, split_b.family, gemm.family) == ("split3", "split3", "gemm")
+    assert gemm.config["split3"] and not gemm.config["streamk"]
+    assert k.plan.temps[gemm.config["planes"][0]] == ((3, 64, 64), "bfloat16")
+    assert "split3_value" in k.source and ", true>(sh, args)" in k.source
+    gen = CodeGenerator()
+    grp = FusionEngine().fuse(g)[0]
+    mixed = gen.generate(g, grp, {0: (64, 64), 1: (64, 64), 2: (64,)},
+                         {0: "float32", 1: "bfloat16", 2: "float32"})
+    assert [sk.family for sk in mixed.plan.kernels] == ["split3", "split3", "gemm"]
     with pytest.raises(LoweringError):
-        compile_graph(g, dtype="float32")
+        gen.generate(g, grp, {0: (64, 64), 1: (64, 64), 2: (64,)},
+                     {0: "bfloat16", 1: "float16", 2: "float32"})
+    gn = graphs.rmsnorm_gemm(64, 64, 64, dtype="float32")
+    with pytest.raises(LoweringError):
+        CodeGenerator(dtype="float32", tune={"gemm": {"prologue": True}}).generate(
+            gn, FusionEngine().fuse(gn)[0])
 
 
 def _all_pattern_sources():
@@ -333,6 +362,7 @@ def _all_pattern_sources():
         ("softmax_causal_bf16", graphs.softmax(causal=True), "bfloat16"),
         ("softmax_long", graphs.softmax((4096, 32768), causal=True), "float32"),
         ("chain", graphs.chain(), "bfloat16"),
+        ("gemm_f32", graphs.gemm_bias_gelu(256, 512, 384, dtype="float32"), "float32"),
         ("gemm", graphs.gemm_bias_gelu(), "bfloat16"),
     ]:
         out.append((name, compile_graph(g, dtype=dt)[0]))
