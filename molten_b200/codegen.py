@@ -101,6 +101,9 @@ def launch_records(plan: GroupPlan, name: str) -> list:
             rec.update(block=c["block"], vec=c["vec"], slots_per_row=c["spr"], smem=0)
         elif sk.family == "split3":
             rec.update(block=c["block"], vec=c["vec"], elements=c["total"], smem=0)
+        elif sk.family == "causal":
+            rec.update(block=c["threads"], zero_tiles_per_row=c["zt"], zero_tile_cols=c["zcols"],
+                       grid=sk.rows * (1 + c["zt"]), smem=0)
         elif sk.family == "attn":
             rec.update(block=c["threads"], bm=128, bn=c["bn"], stages=c["stages"],
                        smem=c["smem_bytes"], tma_store=c["tma_store"],
@@ -175,6 +178,7 @@ class CodeGenerator:
     def generate_from_plan(self, plan: GroupPlan, name: str, graph=None, group=None):
         from .emit import emit_ew, emit_row, emit_row_tma
         from .emit_gemm import emit_gemm, emit_split3
+        from .emit_causal import emit_causal
         from .emit_rope import emit_rope
         from .emit_attn import emit_attn
         chunks = []
@@ -204,6 +208,10 @@ class CodeGenerator:
                 block_x = sk.config["block"]
             elif sk.family == "split3":
                 chunks.append(emit_split3(sk, entry))
+            elif sk.family == "causal":
+                chunks.append(emit_causal(sk, entry))
+                smem = max(smem, 4)
+                block_x = sk.config["threads"]
             elif sk.family == "attn":
                 chunks.append(emit_attn(sk, entry))
                 block_x, block_y = sk.config["threads"], 1
@@ -215,7 +223,7 @@ class CodeGenerator:
             fam = sk.family if fam != "gemm" else fam
         if any(sk.family == "gemm" for sk in plan.kernels):
             fam = "gemm"
-        elif any(sk.family == "row" for sk in plan.kernels):
+        elif any(sk.family in ("row", "causal") for sk in plan.kernels):
             fam = "row"
         source = "\n".join(chunks)
         flops, nbytes = estimate(plan)

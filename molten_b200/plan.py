@@ -159,7 +159,78 @@ def _plan_split3(opd: Operand, key) -> SubKernel:
     return sk
 
 
+CAUSAL_THREADS = 256
+CAUSAL_SPLIT_MIN_COLS = 8192      # rows from which the split causal kernel is the default
+CAUSAL_ZERO_SLOTS = 4             # 16-byte zero stores per thread in one zero tile
+CAUSAL_INTERLEAVE = True          # launch order: each row CTA next to its zero tiles
+
+
+def _plan_causal_softmax(graph, ops, ext, outs, shapes, dts, tune) -> Optional[SubKernel]:
+    """softmax(x + causal_mask) over the last dim, with nothing else in the
+    group, as the split causal kernel (molten/causal_softmax.cuh): row CTAs
+    for the visible logits, zero-tile CTAs for the masked rest.  None when
+    the group is anything else or the split is not chosen."""
+    from .lowering import _reduces_last_dim
+    if len(ops) != 2 or len(outs) != 1:
+        return None
+    add, smx = (graph.ops[o] for o in ops)
+    if add.op_type != OpType.ADD or smx.op_type != OpType.SOFTMAX or outs[0] != ops[1] \
+            or list(smx.inputs) != [ops[0]]:
+        return None
+    masks = [i for i in add.inputs if is_mask_const(graph.ops[i])]
+    xs = [i for i in add.inputs if i not in masks]
+    if len(masks) != 1 or len(xs) != 1 or xs[0] not in ext:
+        return None
+    x_id, mask = xs[0], graph.ops[masks[0]]
+    shape = tuple(int(d) for d in shapes[x_id])
+    if not shape or tuple(shapes[ops[1]]) != shape or not _reduces_last_dim(smx, len(shape)):
+        return None
+    dt = dts[x_id]
+    if dt not in ("float32", "bfloat16", "float16") or dts[ops[1]] != dt:
+        return None
+    cols = shape[-1]
+    rows = prod(shape[:-1]) if len(shape) > 1 else 1
+    esz = DTYPE_SIZE[dt]
+    period = int(mask.attrs.get("period") or cols)
+    offset = int(mask.attrs.get("offset") or 0)
+    if (cols * esz) % 16 or period < 1 or offset < 0:
+        return None
+    o = tune.get("row") or {}
+    # chosen by itself for long rows unless a tune asks for the row engine's
+    # own forms
+    forced = any(k in o for k in ("stream", "zero_tail", "bulk", "engine", "tpc", "cl"))
+    if not o.get("causal_split", cols >= CAUSAL_SPLIT_MIN_COLS and rows >= 148 and not forced):
+        return None
+    vec = 16 // esz
+    zcols = CAUSAL_THREADS * vec * int(o.get("causal_zero_slots", CAUSAL_ZERO_SLOTS))
+    zt = -(-cols // zcols) if cols >= CAUSAL_SPLIT_MIN_COLS else 0
+    zt = int(o.get("causal_zero_tiles", zt))
+    if zt > 0 and zt * zcols < cols:
+        # fewer tiles than asked-for tile widths: widen them to cover the row
+        zcols = -(-cols // (zt * vec)) * vec
+    interleave = bool(o.get("causal_interleave", CAUSAL_INTERLEAVE)) and zt > 0
+    if rows * (1 + zt) >= 2 ** 31:
+        return None
+    src = graph.ops[x_id]
+    opd = Operand(index=0, op_id=x_id, name=src.name or f"op{x_id}", dtype=dt, shape=shape,
+                  last="vec", row_map="full", row_terms=())
+    out = OutputSpec(index=0, op_id=ops[1], dtype=dt, shape=shape, kind="full")
+    sk = SubKernel(family="causal", op_ids=list(ops), operands=[opd], outputs=[out],
+                   rows=rows, cols=cols)
+    sk.precise = dt == "float32"
+    sk.config = {"threads": CAUSAL_THREADS, "vec": vec, "zt": zt, "zcols": zcols,
+                 "period": period, "offset": offset, "precise": sk.precise,
+                 "interleave": interleave,
+                 # 32-byte zero stores when every row starts on a 32-byte boundary
+                 "w32": bool(o.get("causal_w32", True)) and (cols * esz) % 32 == 0}
+    return sk
+
+
 def _plan_sub(graph, family, ops, ext, outs, shapes, dts, tune) -> SubKernel:
+    if family in ("row", "ew"):
+        cs = _plan_causal_softmax(graph, ops, ext, outs, shapes, dts, tune)
+        if cs is not None:
+            return cs
     if family == "gemm":
         return _plan_gemm(graph, ops, ext, outs, shapes, dts, tune)
     if family == "attn":

@@ -131,6 +131,12 @@ class _Spec:
             cfg.block[:] = [c["block"], 1, 1]
             cfg.cluster[:] = [1, 1, 1]
             cfg.smem_bytes = 0
+        elif sk.family == "causal":
+            # one CTA per row (visible logits) + zero tiles
+            cfg.grid[:] = [sk.rows * (1 + c["zt"]), 1, 1]
+            cfg.block[:] = [c["threads"], 1, 1]
+            cfg.cluster[:] = [1, 1, 1]
+            cfg.smem_bytes = 0
         elif sk.family == "split3":
             # grid-stride over the operand's VEC-element slots, 8 CTAs per SM
             torch = _torch()
@@ -234,7 +240,9 @@ class _Spec:
         dev = tensors[0].device
         di = dev.index if dev.index is not None else torch.cuda.current_device()
         if stream is None:
-            stream = torch.cuda.current_stream(dev).cuda_stream
+            # the caller's current stream on that device (the raw handle:
+            # torch.cuda.current_stream() costs several microseconds a call)
+            stream = torch._C._cuda_getCurrentRawStream(di)
         env = dict(zip(plan.inputs, tensors))
         if outs is None:
             outs = [torch.empty(s, dtype=d, device=dev)
@@ -329,6 +337,9 @@ def _alignment_rules(sk):
     if sk.family == "gemm":
         ins = [16 if o.last == "vec" else DTYPE_SIZE[o.dtype] for o in sk.operands]
         return ins, [16 for _ in sk.outputs]
+    if sk.family == "causal":
+        # 16-byte slots in and out; 32-byte zero stores need 32-byte rows
+        return [16], [32 if c.get("w32") else 16]
     if sk.family == "split3":
         # VEC-element slots of the operand; plane stores of VEC bf16
         return ([min(16, c["vec"] * DTYPE_SIZE[sk.operands[0].dtype])],
@@ -476,7 +487,7 @@ class CompiledKernel:
         (1-D, or all leading dims 1), and every sub-kernel is a row,
         elementwise or GEMM kernel (rows of the GEMM = rows of A); else None."""
         plan = self.kernel.plan
-        if any(sk.family not in ("row", "ew", "gemm") for sk in plan.kernels):
+        if any(sk.family not in ("row", "ew", "gemm", "causal") for sk in plan.kernels):
             return None
         if any(len(s) != 2 for s in plan.output_shapes):
             return None

@@ -121,7 +121,8 @@ def test_long_rows_use_a_cluster():
     sk = k.plan.kernels[0]
     assert sk.config["cl"] > 1 and k.config.cluster_x == sk.config["cl"]
     for causal in (False, True):
-        k = compile_graph(graphs.softmax((4096, 32768), causal=causal))[0]
+        g = graphs.softmax((4096, 32768), causal=causal)
+        k = CodeGenerator(tune={"row": {"causal_split": False}}).generate(g, FusionEngine().fuse(g)[0])
         sk = k.plan.kernels[0]
         assert (sk.config["tpc"], sk.config["cl"], sk.config["block"]) == (1024, 1, 1024)
         assert k.config.cluster_x == 1 and not sk.config.get("stream")
@@ -144,11 +145,15 @@ def test_silu_of_the_gate_is_computed_in_the_reduction_pass():
 def test_causal_zero_tail_selection():
     """Bulk zero stores for the masked row tails of a causal softmax: in the
     register form with one team of >= 256 threads per CTA, not in the
-    bulk-staged stream form, not for short rows (several rows per CTA)."""
-    src = compile_graph(graphs.softmax((4096, 32768), causal=True))[0].source
+    bulk-staged stream form, not for short rows (several rows per CTA).
+    (Long causal rows default to the split causal kernel; the row engine's
+    forms are asked for here.)"""
+    def row_engine(g, dt="float32"):
+        gen = CodeGenerator(dtype=dt, tune={"row": {"causal_split": False}})
+        return gen.generate(g, FusionEngine().fuse(g)[0]).source
+    src = row_engine(graphs.softmax((4096, 32768), causal=True))
     assert "bulk_zero_tail" in src and "bulk_zero_drain" in src and "zero_shared_for_bulk" in src
-    src = compile_graph(graphs.softmax((4096, 32768), dtype="bfloat16", causal=True),
-                        dtype="bfloat16")[0].source
+    src = row_engine(graphs.softmax((4096, 32768), dtype="bfloat16", causal=True), "bfloat16")
     assert "bulk_zero_tail" not in src and "store_zero_slot" in src
     src = compile_graph(graphs.softmax((65536, 2048), causal=True))[0].source
     assert "bulk_zero_tail" not in src
@@ -487,3 +492,30 @@ def test_stream_k_plan():
     # when each CTA has at least one tile's worth of k-blocks
     assert stream_k_max_segments(100, 64, 148) <= 3
     assert stream_k_max_segments(148, 10, 148) == 1
+
+
+def test_causal_softmax_split_plan():
+    """softmax(x + causal_mask) over long rows plans as the split causal
+    kernel (row CTAs + zero tiles); short rows, explicit row-engine tunes,
+    masks that could hide a whole row, and anything else in the group keep
+    the row engine."""
+    g = graphs.softmax((4096, 32768), dtype="bfloat16", causal=True)
+    (k,) = compile_graph(g, dtype="bfloat16")
+    (sk,) = k.plan.kernels
+    assert sk.family == "causal" and sk.config["zt"] == 4 and sk.config["zcols"] == 8192
+    assert "causal_softmax_cta<bf16, 256, 32768LL, 32768LL, 0LL, 4, 8192LL, false, true, true>" in k.source
+    assert k.config.family == "row" and k.config.shared_mem_bytes > 0
+    k32 = compile_graph(graphs.softmax((4096, 32768), causal=True))[0]
+    assert k32.plan.kernels[0].config["zt"] == 8 and k32.plan.kernels[0].config["precise"]
+    assert compile_graph(graphs.softmax((32, 2048, 2048), dtype="bfloat16", causal=True),
+                         dtype="bfloat16")[0].plan.kernels[0].family == "row"
+    gen = CodeGenerator(dtype="bfloat16", tune={"row": {"stream": 3}})
+    assert gen.generate(g, FusionEngine().fuse(g)[0]).plan.kernels[0].family == "row"
+    gn = DataflowGraph("neg")
+    x = gn.add_input("x", TS([4096, 32768]), dtype="bfloat16")
+    gn.add_output(gn.softmax(gn.add(x, gn.causal_mask(offset=-1)), -1))
+    assert compile_graph(gn, dtype="bfloat16")[0].plan.kernels[0].family == "row"
+    gs = DataflowGraph("scaled")
+    x = gs.add_input("x", TS([4096, 32768]), dtype="bfloat16")
+    gs.add_output(gs.softmax(gs.add(gs.mul(x, gs.add_constant("half", 0.5)), gs.causal_mask()), -1))
+    assert compile_graph(gs, dtype="bfloat16")[0].plan.kernels[0].family == "row"

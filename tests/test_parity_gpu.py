@@ -482,8 +482,8 @@ def test_stream_row_engine(kind, rows, cols, dtype, tune):
 
 
 @pytest.mark.parametrize("rows,cols,dtype,tune", [
-    (333, 8192, "float32", {}),
-    (4100, 32768, "float32", {}),
+    (333, 8192, "float32", {"zero_tail": True}),
+    (4100, 32768, "float32", {"zero_tail": True}),
     (300, 32768, "bfloat16", {"tpc": 1024, "cl": 1, "zero_tail": True}),
 ])
 def test_causal_zero_tail(rows, cols, dtype, tune):
@@ -519,6 +519,64 @@ def test_causal_zero_tail(rows, cols, dtype, tune):
                           for r in pick])
     got = as_f32(out[torch.as_tensor(pick, device=DEV)])
     assert_close(got, ref, dtype, f"zero tail {rows}x{cols} {dtype}")
+    half = rows // 2 + 1
+    outs = [ck(x[a:b], row_offset=a) for a, b in ((0, half), (half, rows))]
+    torch.cuda.synchronize()
+    bits = (lambda t: t.view(torch.int16)) if out.dtype != torch.float32 else \
+        (lambda t: t.view(torch.int32))
+    assert torch.equal(bits(torch.cat(outs)), bits(out))
+
+
+@pytest.mark.parametrize("rows,cols,dtype,period,offset,tune", [
+    (4100, 32768, "float32", None, 0, {}),
+    (333, 8192, "bfloat16", None, 0, {}),
+    (700, 8192, "float16", None, 0, {}),
+    (1000, 16384, "bfloat16", 5000, 3, {}),
+    (160, 8200, "bfloat16", None, 0, {"causal_split": True}),          # a ragged last zero tile
+    (300, 2048, "bfloat16", None, 0, {"causal_split": True}),          # row CTAs store the zeros
+    (257, 4096, "float32", 1000, 0, {"causal_split": True, "causal_zero_tiles": 3}),
+    (229, 8196, "float32", None, 0, {"causal_split": True, "causal_zero_tiles": 2}),   # 16-byte rows
+    (333, 8200, "bfloat16", None, 0, {"causal_split": True, "causal_interleave": False}),
+])
+def test_causal_split(rows, cols, dtype, period, offset, tune):
+    """The split causal softmax (row CTAs for the visible logits, zero-tile
+    CTAs for the masked rest): matches the oracle on sampled rows at their
+    global rows, every masked element is exactly 0, and two row-offset
+    halves give the same bits."""
+    from molten_b200.codegen import CodeGenerator
+    from molten_b200.ir import DataflowGraph, TensorShape as TS
+    rt = MoltenRuntime(tune={"row": dict(tune)})
+
+    def graph(r):
+        g = DataflowGraph("causal")
+        x = g.add_input("logits", TS([r, cols]), dtype=dtype)
+        g.add_output(g.softmax(g.add(x, g.causal_mask(period=period, offset=offset)), -1))
+        return g
+    g = graph(rows)
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(rows + 3 * cols)
+    x = (3.0 * torch.randn(rows, cols, generator=gen, device=DEV)).to(TORCH_DT[dtype])
+    gk = CodeGenerator(tune=rt.tune).generate(g, FusionEngine().fuse(g)[0], {0: (rows, cols)},
+                                              {0: dtype})
+    (sk,) = gk.plan.kernels
+    assert sk.family == "causal", sk.family
+    ck = rt.compile(gk)
+    out = ck(x)
+    torch.cuda.synchronize()
+    P = period or cols
+    cidx = torch.arange(cols, device=DEV)[None, :]
+    ridx = (torch.arange(rows, device=DEV) % P + offset)[:, None]
+    assert torch.all(out.float()[cidx > ridx] == 0), "masked entries must be exactly 0"
+    pick = _sample_rows(rows, 24)
+    g1 = graph(1)
+    oid = g1.ops[g1._outputs[0]].inputs[0]
+    xn = to_numpy(x)
+    ref = np.concatenate([orc.evaluate(g1, {"logits": xn[r:r + 1]}, row_offset=int(r))[("f32", oid)]
+                          for r in pick])
+    assert_close(as_f32(out[torch.as_tensor(pick, device=DEV)]), ref, dtype,
+                 f"causal split {rows}x{cols} {dtype} P {period} off {offset} {tune}")
+    sums = out.double().sum(dim=1)
+    assert torch.all((sums - 1).abs() < (1e-5 if dtype == "float32" else 2e-2) * max(1, cols ** 0.5 / 8))
     half = rows // 2 + 1
     outs = [ck(x[a:b], row_offset=a) for a, b in ((0, half), (half, rows))]
     torch.cuda.synchronize()
