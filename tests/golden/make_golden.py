@@ -1,9 +1,9 @@
 """Generate the golden fixtures in tests/golden from the reference itself.
 
-Run in a container that has the reference checkout (default
-/root/reference, override with MOLTEN_REFERENCE):
+Run in a container that has the reference checkout, naming it as the
+argument or in MOLTEN_REFERENCE:
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py REFERENCE_CHECKOUT
 
 It imports the reference's own CPU semantics (``benchmarks/ops.py``) and its
 front end (``molten/ir.py``, ``molten/fusion.py``, ``molten/compiler.py``)
@@ -32,7 +32,7 @@ import torch
 import torch.nn.functional as F
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("MOLTEN_REFERENCE", "/root/reference"))
+REF = None      # the reference checkout, set by main() from argv / MOLTEN_REFERENCE
 
 
 def _load(name, path):
@@ -338,6 +338,11 @@ def make_fusion(ir, fusion, compiler):
 
 
 def main():
+    global REF
+    arg = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("MOLTEN_REFERENCE")
+    if not arg:
+        sys.exit("usage: make_golden.py REFERENCE_CHECKOUT (or set MOLTEN_REFERENCE)")
+    REF = Path(arg)
     ops, ir, fusion, compiler = reference_modules()
     torch.manual_seed(0)
     make_numeric(ops)
