@@ -411,8 +411,14 @@ def run_molten(args, w):
 
     peaks, peaks_kind = load_peaks()
     achieved = work / (ms * 1e-3) / scale                  # this rank's kernel, per launch
+    burst = None
     if is_gemm:
-        peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+        # the K timed launches follow a >= 1 s soak under the power cap: the
+        # sustained cuBLAS figure is the like-for-like denominator; the burst
+        # figure's fraction is reported beside it
+        burst = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+        sustained = peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
+        peak = sustained if args.soak >= 1.0 else burst
         roof = {"bound": "tensor", "unit": "TFLOP/s"}
     else:
         peak = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
@@ -427,9 +433,14 @@ def run_molten(args, w):
                 traffic = json.load(f).get(w_local.name if not is_gemm else w.name)
     except (OSError, ValueError):
         traffic = None
+    src = f"{peaks_kind} (MEASURED_PEAKS.json)" if peaks_kind == "measured" else "fallback"
+    if is_gemm:
+        src += (" cuBLAS bf16 sustained, after a %.1f s soak" % args.soak if peak != burst
+                else " cuBLAS bf16 burst")
     roof.update({"achieved": achieved, "peak": peak, "frac": achieved / peak,
-                 "traffic": traffic, "peak_source": f"{peaks_kind} (MEASURED_PEAKS.json)"
-                 if peaks_kind == "measured" else "fallback"})
+                 "traffic": traffic, "peak_source": src})
+    if burst is not None:
+        roof["frac_of_burst"] = achieved / burst
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1

@@ -234,6 +234,23 @@ class _Spec:
         a.status = _capi.status_word(device)
         return a
 
+    def _row_template(self, i: int, device: int) -> bytes:
+        """molten_row_args of row-type kernel i with its per-shape fields set
+        (rows, cols, the status word where the kernel has bounded waits),
+        as bytes that each call copies and fills with pointers."""
+        key = ("row_args", i, device)
+        tpl = self._cfgs.get(key)
+        if tpl is None:
+            sk = self.plan.kernels[i]
+            a = _capi.RowArgs()
+            a.rows, a.cols = sk.rows, sk.cols
+            if (sk.config.get("engine") == "tma" or sk.config.get("stream")
+                    or sk.config.get("cl", 1) > 1):
+                a.status = _capi.status_word(device)
+            tpl = bytes(a)
+            self._cfgs[key] = tpl
+        return tpl
+
     def run(self, tensors, outs, stream: Optional[int], row_offset: int):
         torch = _torch()
         plan = self.plan
@@ -287,11 +304,7 @@ class _Spec:
                     work, count = self.stream_k_workspace(i, di)
                     a.work, a.tile_count = work.data_ptr(), count.data_ptr()
             else:
-                a = _capi.RowArgs()
-                a.rows, a.cols = sk.rows, sk.cols
-                if (sk.config.get("engine") == "tma" or sk.config.get("stream")
-                        or sk.config.get("cl", 1) > 1):
-                    a.status = _capi.status_word(di)
+                a = _capi.RowArgs.from_buffer_copy(self._row_template(i, di))
             a.row_offset = row_offset
             ins_al, outs_al = self.align[i]
             if sk.family == "attn":
@@ -305,18 +318,19 @@ class _Spec:
                                             f"{self.entries[i].decode()} requires")
                 mod.launch(self.entries[i], cfg, a, stream)
                 continue
+            inp, outp = a.inp, a.out        # (one array view each, not one per access)
             for opd, al in zip(sk.operands, ins_al):
                 p = env[opd.op_id].data_ptr()
                 if p % al:
                     raise _capi.MoltenError(f"input {opd.name!r} at {p:#x} is not {al}-byte aligned "
                                             f"as kernel {self.entries[i].decode()} requires")
-                a.inp[opd.index] = p
+                inp[opd.index] = p
             for o, al in zip(sk.outputs, outs_al):
                 p = env[o.op_id].data_ptr()
                 if p % al:
                     raise _capi.MoltenError(f"output at {p:#x} is not {al}-byte aligned "
                                             f"as kernel {self.entries[i].decode()} requires")
-                a.out[o.index] = p
+                outp[o.index] = p
             mod.launch(self.entries[i], cfg, a, stream)
         return outs
 
@@ -406,7 +420,8 @@ class CompiledKernel:
             if t.device != dev:
                 raise RuntimeError(f"{self.name}: all inputs must be on {dev}, got {t.device}")
         spec = self._spec_for(prepared)
-        prepared = self._conform(spec, prepared)
+        if not all(t.is_contiguous() for t in prepared):
+            prepared = self._conform(spec, prepared)
         if out is not None:
             outs = list(out) if isinstance(out, (list, tuple)) else [out]
             self._check_outs(spec, outs, dev)
@@ -416,9 +431,11 @@ class CompiledKernel:
         return res[0] if len(res) == 1 else tuple(res)
 
     # -- specialisation -------------------------------------------------
-    def _signature(self, tensors):
+    @staticmethod
+    def _signature(tensors):
+        # (torch.Size hashes and compares as the tuple of its dims)
         aligned = all(t.data_ptr() % 16 == 0 for t in tensors)
-        return tuple((str(t.dtype), tuple(t.shape)) for t in tensors) + (aligned,)
+        return tuple([(t.dtype, t.shape) for t in tensors]) + (aligned,)
 
     def _spec_for(self, tensors) -> _Spec:
         sig = self._signature(tensors)
@@ -471,7 +488,7 @@ class CompiledKernel:
         if len(outs) != len(plan.outputs):
             raise RuntimeError(f"expected {len(plan.outputs)} output tensors, got {len(outs)}")
         for t, s, d in zip(outs, plan.output_shapes, spec.out_dtypes):
-            if tuple(t.shape) != tuple(s) or t.dtype != d or t.device != dev or not t.is_contiguous():
+            if t.shape != tuple(s) or t.dtype != d or t.device != dev or not t.is_contiguous():
                 raise RuntimeError(f"output must be a contiguous {d} tensor of shape {tuple(s)} "
                                    f"on {dev}")
 
@@ -635,7 +652,7 @@ class MoltenRuntime:
                             _module=str(cubin), kernel=kernel, runtime=self)
         sig = None
         if kernel.plan is not None:
-            sig = tuple((str(_torch_dtype(d)), tuple(s))
+            sig = tuple((_torch_dtype(d), tuple(s))
                         for d, s in zip(kernel.plan.input_dtypes, kernel.plan.input_shapes)) + (True,)
             ck._specs[sig] = _Spec(kernel, cubin)
         self._compiled[key] = ck
