@@ -102,8 +102,9 @@ def launch_records(plan: GroupPlan, name: str) -> list:
         elif sk.family == "split3":
             rec.update(block=c["block"], vec=c["vec"], elements=c["total"], smem=0)
         elif sk.family == "causal":
+            zp = c.get("zpersist", 0)
             rec.update(block=c["threads"], zero_tiles_per_row=c["zt"], zero_tile_cols=c["zcols"],
-                       grid=sk.rows * (1 + c["zt"]), smem=0)
+                       zero_ctas=zp, grid=sk.rows + (zp if zp else sk.rows * c["zt"]), smem=0)
         elif sk.family == "attn":
             rec.update(block=c["threads"], bm=128, bn=c["bn"], stages=c["stages"],
                        smem=c["smem_bytes"], tma_store=c["tma_store"],

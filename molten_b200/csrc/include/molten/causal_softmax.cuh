@@ -67,25 +67,72 @@ __device__ __forceinline__ void cs_update(float& m, float& s, const float (&f)[V
   s = acc;
 }
 
-// INTERLEAVE: CTA b is part b % (1 + ZT) of row b / (1 + ZT) (part 0 the
-// visible logits, part z > 0 zero tile z - 1), so the zero stream runs
-// alongside the row CTAs instead of after them.  W32: rows start on 32-byte
-// boundaries (the output pointer is 32-byte aligned and a row is a multiple
-// of 32 bytes), so zero tiles store 32 bytes at a time.
+// Zero tile zt of `row`: its columns from the first fully masked slot on.
+template <typename T, int THREADS, long long COLS, long long P, long long OFF,
+          long long ZCOLS, bool W32>
+__device__ __forceinline__ void causal_zero_tile(T* __restrict__ out, long long row_offset,
+                                                 unsigned row, int zt) {
+  constexpr int VEC = 16 / (int)sizeof(T);
+  const long long vl = (row_offset + (long long)row) % P + OFF + 1;
+  const int v = (int)(vl < COLS ? vl : COLS);
+  const int vs = (v + VEC - 1) / VEC;
+  T* o = out + (long long)row * COLS;
+  const int c0 = zt * (int)ZCOLS;
+  const int c1 = (c0 + (int)ZCOLS < (int)COLS) ? c0 + (int)ZCOLS : (int)COLS;
+  int c = (vs * VEC > c0) ? vs * VEC : c0;           // first fully masked column here
+  if constexpr (W32) {
+    constexpr int V2 = 2 * VEC;                       // elements per 32-byte store
+    if (c < c1 && (c % V2) != 0) {                   // a leading 16-byte slot
+      if (threadIdx.x == 0) store_zero_slot<kStoreDefault, T, VEC>(o + c);
+      c += VEC;
+    }
+    int j = c + (int)threadIdx.x * V2;
+    for (; j + V2 <= c1; j += THREADS * V2) store_zero32(o + j);
+    if (j < c1) store_zero_slot<kStoreDefault, T, VEC>(o + j);   // a trailing slot
+  } else {
+    for (int j = c + (int)threadIdx.x * VEC; j < c1; j += THREADS * VEC)
+      store_zero_slot<kStoreDefault, T, VEC>(o + j);
+  }
+}
+
+// Launch orders of the two kinds of CTA:
+//   ZPERSIST > 0: CTAs [0, ZPERSIST) are persistent zero CTAs, each storing
+//                 zero tiles t = b, b + ZPERSIST, ... of all rows' tiles (so
+//                 their stores stream without a CTA launch and a store
+//                 drain per 16 KB), then one CTA per row;
+//   INTERLEAVE:   CTA b is part b % (1 + ZT) of row b / (1 + ZT) (part 0 the
+//                 visible logits, part z > 0 zero tile z - 1);
+//   otherwise:    the row CTAs, then the zero tiles.
+// W32: rows start on 32-byte boundaries (the output pointer is 32-byte
+// aligned and a row is a multiple of 32 bytes), so zero tiles store 32
+// bytes at a time.
 template <typename T, int THREADS, long long COLS, long long P, long long OFF, int ZT,
-          long long ZCOLS, bool PRECISE, bool INTERLEAVE = false, bool W32 = false>
+          long long ZCOLS, bool PRECISE, bool INTERLEAVE = false, bool W32 = false,
+          int ZPERSIST = 0>
 __device__ __forceinline__ void causal_softmax_cta(const RowArgs& args) {
   constexpr int VEC = 16 / (int)sizeof(T);
   static_assert(COLS % VEC == 0, "rows are whole 16-byte slots");
   static_assert(COLS < (1LL << 31) && ZCOLS % VEC == 0, "32-bit column indices");
   static_assert(OFF >= 0 && P >= 1, "every row keeps at least one logit");
   static_assert(!W32 || (COLS * (long long)sizeof(T)) % 32 == 0, "32-byte rows");
+  static_assert(ZPERSIST == 0 || ZT > 0, "persistent zero CTAs store zero tiles");
   const T* __restrict__ x = static_cast<const T*>(args.in[0]);
   T* __restrict__ out = static_cast<T*>(args.out[0]);
   const unsigned b = blockIdx.x;
   unsigned row;
   int zt = -1;                              // >= 0: this CTA is zero tile zt of `row`
-  if constexpr (INTERLEAVE) {
+  if constexpr (ZPERSIST > 0) {
+    if (b < (unsigned)ZPERSIST) {
+      const long long tiles = args.rows * ZT;
+      for (long long t = b; t < tiles; t += ZPERSIST) {
+        const unsigned r = (unsigned)(t / ZT);
+        causal_zero_tile<T, THREADS, COLS, P, OFF, ZCOLS, W32>(out, args.row_offset, r,
+                                                               (int)(t - (long long)r * ZT));
+      }
+      return;
+    }
+    row = b - (unsigned)ZPERSIST;
+  } else if constexpr (INTERLEAVE) {
     row = b / (1u + ZT);
     zt = (int)(b - row * (1u + ZT)) - 1;
   } else if ((long long)b >= args.rows) {
@@ -95,32 +142,15 @@ __device__ __forceinline__ void causal_softmax_cta(const RowArgs& args) {
   } else {
     row = b;
   }
+  if (zt >= 0) {
+    causal_zero_tile<T, THREADS, COLS, P, OFF, ZCOLS, W32>(out, args.row_offset, row, zt);
+    return;
+  }
   // visible logits of the row: v in [1, COLS]
-  long long vl = (args.row_offset + (long long)row) % P + OFF + 1;
+  const long long vl = (args.row_offset + (long long)row) % P + OFF + 1;
   const int v = (int)(vl < COLS ? vl : COLS);
   const int vs = (v + VEC - 1) / VEC;                // slots holding visible logits
   T* o = out + (long long)row * COLS;
-
-  if (zt >= 0) {
-    // ------------------------------------------------------- zero tile
-    const int c0 = zt * (int)ZCOLS;
-    const int c1 = (c0 + (int)ZCOLS < (int)COLS) ? c0 + (int)ZCOLS : (int)COLS;
-    int c = (vs * VEC > c0) ? vs * VEC : c0;           // first fully masked column here
-    if constexpr (W32) {
-      constexpr int V2 = 2 * VEC;                       // elements per 32-byte store
-      if (c < c1 && (c % V2) != 0) {                   // a leading 16-byte slot
-        if (threadIdx.x == 0) store_zero_slot<kStoreDefault, T, VEC>(o + c);
-        c += VEC;
-      }
-      int j = c + (int)threadIdx.x * V2;
-      for (; j + V2 <= c1; j += THREADS * V2) store_zero32(o + j);
-      if (j < c1) store_zero_slot<kStoreDefault, T, VEC>(o + j);   // a trailing slot
-    } else {
-      for (int j = c + (int)threadIdx.x * VEC; j < c1; j += THREADS * VEC)
-        store_zero_slot<kStoreDefault, T, VEC>(o + j);
-    }
-    return;
-  }
 
   // --------------------------------------------------------- visible part
   const T* xr = x + (long long)row * COLS;

@@ -33,6 +33,6 @@ def emit_causal(sk: SubKernel, name: str) -> str:
     w("  pdl_enter();")
     w(f"  causal_softmax_cta<{ct}, {c['threads']}, {sk.cols}LL, {c['period']}LL, {c['offset']}LL, "
       f"{c['zt']}, {c['zcols']}LL, {precise}, {'true' if c.get('interleave') else 'false'}, "
-      f"{'true' if c.get('w32') else 'false'}>(args);")
+      f"{'true' if c.get('w32') else 'false'}, {int(c.get('zpersist', 0))}>(args);")
     w("}")
     return "\n".join(L) + "\n"

@@ -163,6 +163,7 @@ CAUSAL_THREADS = 256
 CAUSAL_SPLIT_MIN_COLS = 8192      # rows from which the split causal kernel is the default
 CAUSAL_ZERO_SLOTS = 4             # 16-byte zero stores per thread in one zero tile
 CAUSAL_INTERLEAVE = True          # launch order: each row CTA next to its zero tiles
+CAUSAL_ZERO_CTAS = 0              # persistent zero CTAs (0: one CTA per zero tile)
 
 
 def _plan_causal_softmax(graph, ops, ext, outs, shapes, dts, tune) -> Optional[SubKernel]:
@@ -209,7 +210,11 @@ def _plan_causal_softmax(graph, ops, ext, outs, shapes, dts, tune) -> Optional[S
         # fewer tiles than asked-for tile widths: widen them to cover the row
         zcols = -(-cols // (zt * vec)) * vec
     interleave = bool(o.get("causal_interleave", CAUSAL_INTERLEAVE)) and zt > 0
+    # persistent zero CTAs (0: one CTA per zero tile)
+    zpersist = int(o.get("causal_zero_ctas", CAUSAL_ZERO_CTAS)) if zt > 0 else 0
     if rows * (1 + zt) >= 2 ** 31:
+        return None
+    if zt > 0 and rows * zt >= 2 ** 40:
         return None
     src = graph.ops[x_id]
     opd = Operand(index=0, op_id=x_id, name=src.name or f"op{x_id}", dtype=dt, shape=shape,
@@ -220,7 +225,7 @@ def _plan_causal_softmax(graph, ops, ext, outs, shapes, dts, tune) -> Optional[S
     sk.precise = dt == "float32"
     sk.config = {"threads": CAUSAL_THREADS, "vec": vec, "zt": zt, "zcols": zcols,
                  "period": period, "offset": offset, "precise": sk.precise,
-                 "interleave": interleave,
+                 "interleave": interleave, "zpersist": zpersist,
                  # 32-byte zero stores when every row starts on a 32-byte boundary
                  "w32": bool(o.get("causal_w32", True)) and (cols * esz) % 32 == 0}
     return sk

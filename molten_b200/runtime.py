@@ -132,8 +132,10 @@ class _Spec:
             cfg.cluster[:] = [1, 1, 1]
             cfg.smem_bytes = 0
         elif sk.family == "causal":
-            # one CTA per row (visible logits) + zero tiles
-            cfg.grid[:] = [sk.rows * (1 + c["zt"]), 1, 1]
+            # one CTA per row (visible logits) + a CTA per zero tile, or
+            # persistent zero CTAs
+            zp = c.get("zpersist", 0)
+            cfg.grid[:] = [sk.rows + (zp if zp else sk.rows * c["zt"]), 1, 1]
             cfg.block[:] = [c["threads"], 1, 1]
             cfg.cluster[:] = [1, 1, 1]
             cfg.smem_bytes = 0

@@ -503,7 +503,7 @@ def test_causal_softmax_split_plan():
     (k,) = compile_graph(g, dtype="bfloat16")
     (sk,) = k.plan.kernels
     assert sk.family == "causal" and sk.config["zt"] == 4 and sk.config["zcols"] == 8192
-    assert "causal_softmax_cta<bf16, 256, 32768LL, 32768LL, 0LL, 4, 8192LL, false, true, true>" in k.source
+    assert "causal_softmax_cta<bf16, 256, 32768LL, 32768LL, 0LL, 4, 8192LL, false, true, true, 0>" in k.source
     assert k.config.family == "row" and k.config.shared_mem_bytes > 0
     k32 = compile_graph(graphs.softmax((4096, 32768), causal=True))[0]
     assert k32.plan.kernels[0].config["zt"] == 8 and k32.plan.kernels[0].config["precise"]

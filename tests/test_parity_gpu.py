@@ -537,6 +537,8 @@ def test_causal_zero_tail(rows, cols, dtype, tune):
     (257, 4096, "float32", 1000, 0, {"causal_split": True, "causal_zero_tiles": 3}),
     (229, 8196, "float32", None, 0, {"causal_split": True, "causal_zero_tiles": 2}),   # 16-byte rows
     (333, 8200, "bfloat16", None, 0, {"causal_split": True, "causal_interleave": False}),
+    (333, 8192, "bfloat16", None, 0, {"causal_split": True, "causal_zero_ctas": 37}),   # persistent
+    (1000, 16384, "float32", 5000, 3, {"causal_split": True, "causal_zero_ctas": 296}),
 ])
 def test_causal_split(rows, cols, dtype, period, offset, tune):
     """The split causal softmax (row CTAs for the visible logits, zero-tile
