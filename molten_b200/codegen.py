@@ -92,7 +92,8 @@ def launch_records(plan: GroupPlan, name: str) -> list:
         c = sk.config
         rec = {"entry": kernel_entry(name, i, len(plan.kernels)), "family": sk.family}
         if sk.family == "row" and c.get("engine") == "tma":
-            rec.update(engine="tma", block=32 * (c["nc"] + 1), stages=c["stages"], smem=c["smem"])
+            rec.update(engine="tma", block=32 * (c["nc"] * c.get("tw", 1) + 1), stages=c["stages"],
+                       smem=c["smem"])
         elif sk.family == "row":
             rec.update(engine="regs", block=c["block"], rpc=c["rpc"], cl=c["cl"], smem=0)
         elif sk.family == "ew":
@@ -195,7 +196,7 @@ class CodeGenerator:
             if sk.family == "row" and sk.config.get("engine") == "tma":
                 chunks.append(emit_row_tma(sk, entry))
                 smem = max(smem, sk.config["smem"])
-                block_x = 32 * (sk.config["nc"] + 1)
+                block_x = 32 * (sk.config["nc"] * sk.config.get("tw", 1) + 1)
             elif sk.family == "row":
                 chunks.append(emit_row(sk, entry))
                 c = sk.config

@@ -840,6 +840,7 @@ def emit_row_tma(sk: SubKernel, name: str) -> str:
     warp per row; reductions are warp shuffles."""
     cfg = sk.config
     VEC, NV, NC, ST = cfg["vec"], cfg["nv"], cfg["nc"], cfg["stages"]
+    TW = int(cfg.get("tw", 1))                     # warps per row (a team)
     staged = list(cfg["staged"])                   # operand indices, stage order
     offs = dict(zip(staged, cfg["stage_offsets"]))
     consts = list(cfg.get("consts", ()))           # per-column operands, copied once
@@ -863,16 +864,27 @@ def emit_row_tma(sk: SubKernel, name: str) -> str:
     w("")
     w("using namespace molten;")
     w("")
-    w(f"extern \"C\" __global__ void __launch_bounds__({32 * (NC + 1)}, 1) "
+    # largest number of values one team reduction combines
+    nred = max([len([r for r in reds[p] if values[r].op == op])
+                for p in reds for op in ("rsum", "rmax", "rmin")] + [1])
+    w(f"extern \"C\" __global__ void __launch_bounds__({32 * (NC * TW + 1)}, 1) "
       f"{name}(const __grid_constant__ RowArgs args) {{")
     w("  pdl_enter();")
     w(f"  constexpr int VEC = {VEC}, NV = {NV}, NC = {NC}, STAGES = {ST}, "
       f"STAGE_BYTES = {cfg['stage_bytes']};")
+    if TW > 1:
+        w(f"  constexpr int TW = {TW}, NRED = {nred};")
     w(f"  constexpr long long COLS = {sk.cols}LL, NVEC = {cfg['nvec']}LL;")
     w(f"  constexpr uint32_t ROW_BYTES = {cfg['row_bytes']}u;")
     w("  extern __shared__ __align__(128) uint8_t smem_raw[];")
     w(f"  const auto ring = row_ring_carve<STAGES, STAGE_BYTES, {CB}>(smem_raw);")
-    w("  row_ring_init(ring, STAGES);")
+    if TW > 1:
+        w("  __shared__ float team_red[NC * 2 * TW * NRED];")
+        w("  __shared__ __align__(8) uint64_t team_bar[NC * 2];")
+        w("  row_ring_init(ring, STAGES, TW);")
+        w("  team_bars_init(smem_u32(team_bar), NC, TW);")
+    else:
+        w("  row_ring_init(ring, STAGES);")
     w("  __syncthreads();")
     w("  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;")
     w("  const long long G = gridDim.x;")
@@ -922,7 +934,12 @@ def emit_row_tma(sk: SubKernel, name: str) -> str:
         w("      return;")
         w("    }")
         w("    const uint32_t cb = ring.consts();")
-    w("    for (long long j = warp - 1; j < nloc; j += NC) {")
+    if TW > 1:
+        w("    const int team = (warp - 1) / TW, tw = (warp - 1) % TW, tl = tw * 32 + lane;")
+        w("    TeamRed tr{team_red + team * (2 * TW * NRED), smem_u32(team_bar) + 16u * team, 0u};")
+        w("    for (long long j = team; j < nloc; j += NC) {")
+    else:
+        w("    for (long long j = warp - 1; j < nloc; j += NC) {")
     w("      const int s = (int)(j % STAGES);")
     w("      const bool got = mbar_wait(ring.full(s), (uint32_t)((j / STAGES) & 1));")
     w("      if (!__all_sync(0xffffffffu, got ? 1 : 0)) {")
@@ -975,7 +992,10 @@ def emit_row_tma(sk: SubKernel, name: str) -> str:
     def slot_loop(targets, body_extra, tail=None, outs=()):
         w("#pragma unroll")
         w("      for (int k = 0; k < NV; ++k) {")
-        w("        const long long j = lane + 32LL * k;")
+        if TW > 1:
+            w("        const long long j = tl + 32LL * TW * k;")
+        else:
+            w("        const long long j = lane + 32LL * k;")
         w("        if (j >= NVEC) break;")
         used_staged, used_glob = set(), set()
         for t in targets:
@@ -1043,7 +1063,14 @@ def emit_row_tma(sk: SubKernel, name: str) -> str:
                   "rmin": "warp_allreduce_min"}[op]
             w("      {")
             w(f"        float red[{len(grp)}] = {{" + ", ".join(f"v{r}" for r in grp) + "};")
-            w(f"        {fn}<{len(grp)}>(red);")
+            if TW > 1:
+                opn = {"rsum": 0, "rmax": 1, "rmin": 2}[op]
+                w(f"        if (!team_allreduce<{opn}, {len(grp)}, TW>(red, tr, tw, lane)) {{")
+                w("          if (lane == 0) row_ring_fail(ring.abort_flag, args.status, kRowTimeoutTeam);")
+                w("          break;")
+                w("        }")
+            else:
+                w(f"        {fn}<{len(grp)}>(red);")
             for i, r in enumerate(grp):
                 w(f"        v{r} = red[{i}];")
             w("      }")
@@ -1065,7 +1092,7 @@ def emit_row_tma(sk: SubKernel, name: str) -> str:
         slot_loop(fin, fin_extra, fin_tail, full_outs)
     for o in sk.outputs:
         if o.kind == "row":
-            w(f"      if (lane == 0) store_scalar(out{o.index}, "
+            w(f"      if ({'tl' if TW > 1 else 'lane'} == 0) store_scalar(out{o.index}, "
               f"{_tma_leaf(sk, sk.out_values[o.index], staged, mat_ready)});")
     w("      __syncwarp();")
     w("      if (lane == 0) mbar_arrive(ring.empty(s));")

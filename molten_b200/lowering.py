@@ -806,7 +806,11 @@ def choose_rope_config(sk: SubKernel, style: str, seq: int, heads: int,
 
 
 SMEM_RING_BUDGET = 220 * 1024
-TMA_MIN_ROWS = 4096      # below this the ring's fill time outweighs its depth
+TMA_MIN_ROWS = 2048      # below this the ring's fill time outweighs its depth
+EW_TMA_MIN_ROWS = 4096   # elementwise groups take the ring from here on
+TMA_MAX_AUTO_STAGES = 14
+TMA_CONSUMER_WARPS = 20  # consumer warps per CTA the team width aims at
+TMA_TEAM_MAX_ROWS = 4096 # reductions over this many rows: one warp per row
 
 
 def choose_row_tma_config(sk: SubKernel, prefetch: set, materialize: dict,
@@ -818,10 +822,12 @@ def choose_row_tma_config(sk: SubKernel, prefetch: set, materialize: dict,
     slots and at least 8 stages in the shared-memory budget.
     """
     o = dict(override or {})
-    # Chosen for long row counts (measured: RMSNorm*SiLU bf16 x 3584 at 8192
-    # rows 91% of HBM peak vs 83% for the register engine, but slower at 2048
-    # rows); never under a vec override, which the runtime uses for inputs
-    # that are not 16-byte aligned -- bulk copies need 16-byte alignment
+    # Chosen from 2048 rows on (measured with teams of warps per row, CUDA-
+    # graph replay, rotated outputs: RMSNorm*SiLU bf16 x 3584 at 8192 rows
+    # 30.0 -> 29.2 us against one warp per row, at 2048 rows 10.0 -> 9.65 us
+    # against the register engine; RMSNorm fp32 2048 x 5120 15.8 -> 14.4 us);
+    # never under a vec override, which the runtime uses for inputs that are
+    # not 16-byte aligned -- bulk copies need 16-byte alignment
     if o.get("engine") in ("regs", "ew") or "vec" in o or not prefetch:
         return None
     if o.get("engine") != "tma" and sk.rows < TMA_MIN_ROWS:
@@ -851,13 +857,36 @@ def choose_row_tma_config(sk: SubKernel, prefetch: set, materialize: dict,
     s_max = o.get("stages") or min(32, (SMEM_RING_BUDGET - coff) // stage_bytes)
     if s_max < o.get("min_stages", 8) and o.get("engine") != "tma":
         return None
-    # Stage s is always consumed by warp s % NC, which needs STAGES % NC == 0:
-    # a warp then meets the stages it owns in order and can never wait on a
+    # Stage s is always consumed by team s % NC, which needs STAGES % NC == 0:
+    # a team then meets the stages it owns in order and can never wait on a
     # phase two ahead of the one in flight (mbarrier parity would alias).
+    # A team is TW warps; NC * TW + 1 warps per CTA.  Unless tuned: the most
+    # stages up to 14 (15 measured slower on RMSNorm*SiLU 8192 x 3584), NC
+    # preferring 7 then 5 teams, and TW for ~20 consumer warps, except one
+    # warp per row for reductions over >= 4096 rows.  Measured with CUDA-
+    # graph replay after a 1.5 s soak under the 1 kW power cap (SM clock
+    # ~1740 MHz), us: RMSNorm fp32 2048 x 5120 15.7 (register engine) ->
+    # 14.6 (5 teams of 4 warps) / 14.5 (of 2); RMSNorm*SiLU bf16 2048 x 3584
+    # 9.9 -> 9.65 (7 teams of 3); 8-op bf16 chain 16384 x 8192 145.8
+    # (elementwise kernel) -> 139.2 (5 teams of 4; of 2: slower than the
+    # elementwise kernel); RMSNorm*SiLU 8192 x 3584 30.0 with one warp per
+    # row, 30.1 with teams of 2, 30.9 with teams of 3 (at full clocks,
+    # before the soak, teams of 3 had been faster: 29.2 vs 30.0).
+    tw_req = int(o["tw"]) if "tw" in o else None
+    if tw_req is not None and (tw_req < 1 or 32 * (tw_req + 1) > 1024):
+        raise LoweringError(f"row ring team of {tw_req} warps does not fit a CTA")
+    one_warp = tw_req == 1 or (tw_req is None and sk.passes > 0 and sk.rows >= TMA_TEAM_MAX_ROWS)
+    if one_warp:
+        # one warp per row: the most stages, 6..8 consumer warps measured best
+        st_cap = max(2, s_max)
+        nc_ranges = [[o["nc"]]] if "nc" in o else [range(8, 5, -1), range(14, 1, -1)]
+    else:
+        st_cap = max(2, s_max if "stages" in o else min(s_max, TMA_MAX_AUTO_STAGES))
+        nc_ranges = [[o["nc"]]] if "nc" in o else [[7, 5, 6, 8, 4, 3, 2, 1]]
+    nc_ranges = [[nc for nc in r if nc * (tw_req or 1) <= 31] for r in nc_ranges]
     best = None
-    nc_ranges = [[o["nc"]]] if "nc" in o else [range(8, 5, -1), range(14, 1, -1)]
-    for ncs in nc_ranges:          # 6..8 consumer warps measured best
-        for st in range(max(2, s_max), 1, -1):
+    for ncs in nc_ranges:
+        for st in range(st_cap, 1, -1):
             for nc in ncs:
                 if st % nc == 0:
                     best = (st, nc)
@@ -869,12 +898,18 @@ def choose_row_tma_config(sk: SubKernel, prefetch: set, materialize: dict,
     if best is None:
         return None
     stages, nc = best
+    if one_warp:
+        tw = 1
+    elif tw_req:
+        tw = tw_req
+    else:
+        tw = max(1, min(31 // nc, round(TMA_CONSUMER_WARPS / nc)))
     nvec = sk.cols // vec
-    nv = -(-nvec // 32)
+    nv = -(-nvec // (32 * tw))
     mat = dict(materialize)
-    if nv * vec * len(mat) > 64:
+    if nv * vec * len(mat) > 64 or not o.get("materialize", True):
         mat = {}                     # recompute instead of holding in registers
-    return {"engine": "tma", "vec": vec, "nvec": nvec, "nv": nv, "nc": nc,
+    return {"engine": "tma", "vec": vec, "nvec": nvec, "nv": nv, "nc": nc, "tw": tw,
             "stages": stages, "stage_bytes": stage_bytes, "staged": staged,
             "stage_offsets": offsets, "consts": consts, "const_offsets": const_offsets,
             "const_bytes": coff,

@@ -11,7 +11,7 @@ from .lowering import (
     choose_row_config, choose_row_tma_config, choose_rope_config, classify_operand,
     rms_prologue, attention_pattern,
     group_boundary, infer_shapes,
-    is_mask_const, prod, promote, split_group, EXPENSIVE,
+    is_mask_const, prod, promote, split_group, EXPENSIVE, EW_TMA_MIN_ROWS,
 )
 
 DEFAULT_SYMBOLIC_DIM = 1024
@@ -297,13 +297,21 @@ def _plan_sub(graph, family, ops, ext, outs, shapes, dts, tune) -> SubKernel:
             sk.config["prefetch"] = sorted(prefetch)
             sk.config["materialize"] = sorted(materialize.items())
     else:
-        # the TMA ring is opt-in here ({"ew": {"engine": "tma"}}): on the
-        # 8-op bf16 chain its few consumer warps are compute-bound (measured
-        # 50% of HBM peak vs 80% for the elementwise kernel)
+        # the TMA ring with teams of warps per row, from EW_TMA_MIN_ROWS rows
+        # with at least 4 stages, or when asked ({"ew": {"engine": "tma"}})
+        # (measured, 8-op bf16 chain 16384 x 8192: 132.6 us as elementwise
+        # kernel, 125.2 us on 5 stages with teams of 4 warps; with one warp
+        # per row the ring's consumers were compute-bound at 50% of HBM)
         prefetch = {o.index for o in sk.operands if o.last == "vec" and o.row_map != "zero"}
         tma = None
         if override.get("engine") == "tma":
             tma = choose_row_tma_config(sk, prefetch, {}, dict(override, min_stages=2))
+        elif (override.get("engine") is None and "vec" not in override
+              and sk.rows >= EW_TMA_MIN_ROWS):
+            tma = choose_row_tma_config(sk, prefetch, {},
+                                        dict(override, engine="tma", min_stages=4))
+            if tma is not None and tma["stages"] < 4:
+                tma = None
         if tma is not None:
             sk.family = "row"
             sk.config = tma

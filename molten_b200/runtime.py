@@ -101,7 +101,7 @@ class _Spec:
             torch = _torch()
             sms = torch.cuda.get_device_properties(device).multi_processor_count
             cfg.grid[:] = [max(1, min(sk.rows, sms)), 1, 1]
-            cfg.block[:] = [32 * (c["nc"] + 1), 1, 1]
+            cfg.block[:] = [32 * (c["nc"] * c.get("tw", 1) + 1), 1, 1]
             cfg.cluster[:] = [1, 1, 1]
             cfg.smem_bytes = c["smem"]
         elif sk.family == "row":

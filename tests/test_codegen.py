@@ -86,17 +86,20 @@ def test_names_follow_reference_rule():
 
 
 @pytest.mark.parametrize("kind,args,fam,engine", [
-    ("rmsnorm", (2048, 5120), "row", "regs"),
-    ("rmsnorm_silu_gate", (2048, 3584), "row", "regs"),
+    ("rmsnorm", (2048, 5120), "row", "tma"),
+    ("rmsnorm", (1024, 5120), "row", "regs"),
+    ("rmsnorm_silu_gate", (2048, 3584), "row", "tma"),
     ("rmsnorm_silu_gate", (8192, 3584), "row", "tma"),
+    ("rmsnorm_silu_gate", (1, 3584), "row", "regs"),
     ("softmax", ((32, 2048, 2048),), "row", "regs"),
     ("chain", (64, 8192), "ew", None),
-    ("chain", (16384, 8192), "ew", None),
+    ("chain", (16384, 8192), "row", "tma"),
     ("gemm_bias_gelu", (8192, 4096, 14336), "gemm", None),
 ])
 def test_families(kind, args, fam, engine):
-    """Pattern family and engine per benchmark graph: long row counts stream
-    through the TMA ring (reductions or not), the rest keep rows in registers."""
+    """Pattern family and engine per benchmark graph: row counts from 2048
+    on (elementwise groups from 4096 on) stream through the TMA ring, the
+    rest keep rows in registers."""
     dt = "float32" if kind in ("rmsnorm", "softmax") else "bfloat16"
     g = graphs.BUILDERS[kind](*args, dtype=dt)
     ks = compile_graph(g, dtype=dt)
@@ -132,14 +135,19 @@ def test_silu_of_the_gate_is_computed_in_the_reduction_pass():
     """RMSNorm * SiLU(gate) in the register engine: silu(gate) depends only on
     the row's own elements, so it is computed next to the sum of squares and
     kept in registers for the output pass."""
-    (k,) = compile_graph(graphs.rmsnorm_silu_gate(2048, 3584), dtype="bfloat16")
+    (k,) = compile_graph(graphs.rmsnorm_silu_gate(1024, 3584), dtype="bfloat16")
     c = k.plan.kernels[0].config
     assert c["engine"] == "regs" and len(c["materialize"]) == 1 and c["materialize"][0][1] == 0
     body = k.source.split("// ---- pass 0")[1].split("// ---- final pass")[0]
     assert "m_silu<" in body and "m_silu<" not in k.source.split("// ---- final pass")[1]
     # a plain RMSNorm has nothing to compute early
-    (k,) = compile_graph(graphs.rmsnorm(2048, 5120))
+    (k,) = compile_graph(graphs.rmsnorm(1024, 5120))
     assert k.plan.kernels[0].config["materialize"] == []
+    # the TMA ring with teams of warps keeps it too (5 slots per lane)
+    (k,) = compile_graph(graphs.rmsnorm_silu_gate(2048, 3584), dtype="bfloat16")
+    c = k.plan.kernels[0].config
+    assert c["engine"] == "tma" and c["tw"] > 1 and len(c["materialize"]) == 1
+    assert "team_allreduce<0, 1, TW>" in k.source
 
 
 def test_causal_zero_tail_selection():

@@ -409,6 +409,62 @@ def test_tma_ring_engine(rows, cols, dtype):
                  f"tma ring {rows}x{cols} {dtype}")
 
 
+TEAM_CASES = [
+    # (graph, rows, cols, dtype, tune): teams of TW warps per row in the ring
+    ("rmsnorm_silu_gate", 300, 1000, "bfloat16", {"row": {"engine": "tma", "tw": 3, "nc": 7}}),
+    ("rmsnorm_silu_gate", 2048, 3584, "bfloat16", {"row": {"engine": "tma", "tw": 1}}),
+    ("rmsnorm_silu_gate", 4099, 3584, "float16", {"row": {"engine": "tma", "tw": 2, "nc": 14}}),
+    ("rmsnorm", 150, 5120, "float32", {"row": {"engine": "tma", "tw": 5, "nc": 2}}),
+    ("rmsnorm", 5000, 64, "float32", {"row": {"engine": "tma", "tw": 2, "nc": 7}}),
+    ("chain", 300, 1024, "bfloat16", {"ew": {"engine": "tma", "tw": 4}}),
+    ("chain", 4096, 2048, "bfloat16", None),
+]
+
+
+@pytest.mark.parametrize("kind,rows,cols,dtype,tune", TEAM_CASES)
+def test_tma_ring_teams(kind, rows, cols, dtype, tune):
+    """The TMA ring with a team of warps per row (reductions combined across
+    the team's warps in shared memory): ragged slot counts, one-warp teams,
+    rows shorter than a team, elementwise groups; checked against the oracle,
+    and two runs are bit-identical."""
+    from molten_b200.codegen import CodeGenerator
+    from molten_b200.fusion import FusionEngine
+    rt = MoltenRuntime(tune=tune)
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(rows * 7 + cols)
+    T = TORCH_DT[dtype]
+    if kind == "chain":
+        g = graphs.chain(rows, cols, dtype=dtype)
+        names = ["x", "r", "a", "b", "s"]
+        tensors = [torch.randn(rows, cols, generator=gen, device=DEV).to(T) for _ in range(2)]
+        tensors += [(2 * torch.rand(cols, generator=gen, device=DEV) - 1).to(T) for _ in range(3)]
+    else:
+        g = graphs.BUILDERS[kind](rows, cols, dtype=dtype)
+        names = ["x", "w", "gate"][:3 if kind == "rmsnorm_silu_gate" else 2]
+        tensors = [torch.randn(rows, cols, generator=gen, device=DEV).to(T),
+                   (1 + 0.1 * torch.randn(cols, generator=gen, device=DEV)).to(T)]
+        if kind == "rmsnorm_silu_gate":
+            tensors.append(torch.randn(rows, cols, generator=gen, device=DEV).to(T))
+    grp = FusionEngine().fuse(g)[0]
+    ins = sorted(i for i, o in g.ops.items() if o.op_type.name == "INPUT")
+    gk = CodeGenerator(tune=tune).generate(g, grp, {i: tuple(t.shape) for i, t in zip(ins, tensors)},
+                                           {i: dtype for i in ins})
+    c = gk.plan.kernels[0].config
+    assert c["engine"] == "tma"
+    if tune:
+        want = (tune.get("row") or tune.get("ew"))
+        assert c["tw"] == want.get("tw", c["tw"])
+    ck = rt.compile(gk)
+    out = ck(*tensors)
+    again = ck(*tensors)
+    torch.cuda.synchronize()
+    assert MoltenRuntime.read_status(0) == 0
+    assert torch.equal(out, again)
+    res = orc.evaluate(g, {n: to_numpy(t) for n, t in zip(names, tensors)})
+    assert_close(as_f32(out), res[("f32", g.ops[g._outputs[0]].inputs[0])], dtype,
+                 f"tma teams {kind} {rows}x{cols} {dtype} {tune}")
+
+
 STREAM_CASES = [
     # (graph, rows, cols, dtype, row tune) -- persistent stream form forced on
     ("softmax", 300, 32768, "bfloat16", {"stream": 3}),
