@@ -156,7 +156,10 @@ class CodeGenerator:
 
     ``fp16=True`` selects fp16 I/O as in the reference; ``dtype`` (an
     addition) selects any of float32 / bfloat16 / float16 for every input
-    whose dtype is not given explicitly.
+    whose dtype is not given explicitly.  ``tune`` overrides the planner's
+    choices per family (``{"row": {...}, "ew": {...}, "gemm": {...}}``);
+    ``tune["defines"]`` lists preprocessor definitions ("NAME" or
+    "NAME=VALUE") placed at the top of the emitted module.
     """
 
     def __init__(self, compute_capability: int = 80, fp16: bool = False,
@@ -189,6 +192,8 @@ class CodeGenerator:
         if ops_txt:
             chunks.append(f"// Fused ops: {ops_txt}")
         chunks.append("// input dtypes: " + json.dumps(plan.input_dtypes))
+        for d in self.tune.get("defines") or ():
+            chunks.append("#define " + str(d).replace("=", " ", 1))
         smem = 0
         block_x, block_y, fam = 256, 1, "ew"
         for i, sk in enumerate(plan.kernels):
