@@ -43,7 +43,7 @@ def parse_args():
     p.add_argument("--workload", default=None)
     p.add_argument("--tune", default=None, help="JSON tile overrides, e.g. '{\"row\": {\"tpc\": 128}}'")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--e2e-chunks", type=int, default=8,
+    p.add_argument("--e2e-chunks", type=int, default=5,
                    help="row blocks whose host<->device copies overlap in the end-to-end step")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0)

@@ -691,7 +691,16 @@ def choose_row_config(sk: SubKernel, prefetch: set, materialize: set,
     if o.get("rpc"):
         rpc = o["rpc"]
     elif tpc >= 32:
-        rpc = max(1, min(8, 256 // tpc))
+        # 256-thread CTAs; softmax rows in 128-thread CTAs, 64 with a causal
+        # mask, whose visible prefixes make rows unequal work (measured with
+        # CUDA-graph replay after a 1 s soak, us, 8 -> 2 warp-rows per CTA:
+        # bf16 65536 x 2048 causal 71.0 -> 68.0, plain 81.3 -> 80.5 (4 per
+        # CTA); fp32 causal, 2-warp rows, 4 -> 1 per CTA 135.1 -> 126.3,
+        # plain 160.0 -> 159.2 (2 per CTA))
+        target = 256
+        if any(v.op == "softmax" for v in sk.values):
+            target = 64 if any(v.op == "mask" for v in sk.values) else 128
+        rpc = max(1, min(8, target // tpc))
     else:
         rpc = max(1, 256 // tpc)
     if tpc < 32 and (tpc * rpc) % 32:
