@@ -61,6 +61,12 @@ _TMA_CODE = {"bfloat16": _capi.DT_BF16, "float16": _capi.DT_F16, "float32": _cap
 # kernel still waits for its predecessor before touching global memory.
 PDL = os.environ.get("MOLTEN_PDL", "1") != "0"
 
+# MOLTEN_DEBUG=1: every call waits for its kernels and reads (and clears)
+# the device's status word, so a bounded wait that ran out, or an
+# asynchronous CUDA error, is raised by the call that caused it instead of
+# surfacing at a later read.  Costs a synchronisation per call.
+DEBUG = os.environ.get("MOLTEN_DEBUG", "0") not in ("", "0")
+
 
 class _Spec:
     """One shape/dtype specialisation of a group, ready to launch."""
@@ -334,6 +340,12 @@ class _Spec:
                                             f"as kernel {self.entries[i].decode()} requires")
                 outp[o.index] = p
             mod.launch(self.entries[i], cfg, a, stream)
+        if DEBUG:
+            torch.cuda.synchronize(di)
+            bits = _capi.read_status(di, True)
+            if bits:
+                raise _capi.MoltenError(f"{self.gk.name}: a bounded wait ran out on device {di} "
+                                        f"(status word {bits:#x})")
         return outs
 
 

@@ -1108,3 +1108,102 @@ def test_wrong_inputs_raise(rt):
         ck(x)
     with pytest.raises(RuntimeError, match="CUDA tensors"):
         ck(x.cpu(), torch.randn(64))
+
+
+GUARD_CASES = [
+    # (label, graph builder, inputs builder, dtype); shapes with ragged tails
+    ("row regs ragged", lambda: graphs.rmsnorm_silu_gate(37, 1004, dtype="bfloat16"), "rms3", "bfloat16"),
+    ("row tma teams", lambda: graphs.rmsnorm_silu_gate(2100, 3584, dtype="bfloat16"), "rms3", "bfloat16"),
+    ("row tma fp32", lambda: graphs.rmsnorm(2051, 5120), "rms2", "float32"),
+    ("softmax causal small CTAs", lambda: graphs.softmax((129, 2048), causal=True), "logits", "float32"),
+    ("softmax causal split", lambda: graphs.softmax((150, 8192), dtype="bfloat16", causal=True),
+     "logits", "bfloat16"),
+    ("softmax stream bulk", lambda: graphs.softmax((151, 32768), dtype="bfloat16"), "logits", "bfloat16"),
+    ("chain ew", lambda: graphs.chain(300, 1000), "chain", "bfloat16"),
+    ("chain tma teams", lambda: graphs.chain(4096, 2048), "chain", "bfloat16"),
+    ("gemm one SM", lambda: graphs.gemm_bias_gelu(300, 256, 520), "gemm", "bfloat16"),
+    ("gemm SM pair", lambda: graphs.gemm_bias_gelu(1100, 256, 1024), "gemm", "bfloat16"),
+    ("gemm stream-K", lambda: graphs.gemm_bias_gelu(64, 2048, 512), "gemm", "bfloat16"),
+    ("gemm fp32 bf16x3", lambda: graphs.gemm_bias_gelu(130, 256, 384, dtype="float32"), "gemm", "float32"),
+    ("attention fused", lambda: graphs.attention_score(200, 300, 64, heads=2), "attn", "bfloat16"),
+    ("rope", lambda: graphs.rope(1, 16, 4, 128), "rope", "bfloat16"),
+]
+
+
+def _guard_inputs(kind, g, dtype, gen):
+    T = TORCH_DT[dtype]
+    shapes = {o.name: tuple(int(d) for d in o.shape.dims) for o in g.ops.values() if o.op_type.name == "INPUT"}
+    names = [g.ops[i].name for i in sorted(i for i, o in g.ops.items() if o.op_type.name == "INPUT")]
+    out = []
+    for nm in names:
+        shp = shapes[nm]
+        if kind == "rope" and nm in ("cos", "sin"):
+            ang = torch.rand(*shp, generator=gen, device=DEV) * 6.283185307179586
+            out.append(torch.cos(ang) if nm == "cos" else torch.sin(ang))
+        elif nm in ("w",):
+            out.append((1 + 0.1 * torch.randn(*shp, generator=gen, device=DEV)).to(T))
+        elif nm == "B":
+            out.append((torch.randn(*shp, generator=gen, device=DEV) / shp[0] ** 0.5).to(T))
+        elif nm in ("a", "b", "s"):
+            out.append((2 * torch.rand(*shp, generator=gen, device=DEV) - 1).to(T))
+        else:
+            scale = 3.0 if kind == "logits" else 1.0
+            out.append((scale * torch.randn(*shp, generator=gen, device=DEV)).to(T))
+    return out
+
+
+@pytest.mark.parametrize("label,build,kind,dtype", GUARD_CASES, ids=[c[0] for c in GUARD_CASES])
+def test_outputs_stay_inside_their_buffers(rt, label, build, kind, dtype):
+    """Guard bands: every kernel family writes its output through a view into
+    a larger buffer whose 4 KB before and after hold random bytes; the bytes
+    must be untouched, the inputs unchanged, and the output equal to a call
+    that allocates its own (ragged tails, split/stream/ring/team forms)."""
+    g = build()
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(len(label) * 97 + 5)
+    tensors = _guard_inputs(kind, g, dtype, gen)
+    before = [t.clone() for t in tensors]
+    (kern,) = compile_graph(g, dtype=dtype)
+    ck = rt.compile(kern)
+    ref = ck(*tensors)
+    torch.cuda.synchronize()
+    nbytes = ref.numel() * ref.element_size()
+    guard = 4096
+    big = torch.randint(0, 256, (guard + nbytes + guard,), dtype=torch.uint8, device=DEV, generator=gen)
+    pattern = big.clone()
+    view = big[guard:guard + nbytes].view(ref.dtype).view(ref.shape)
+    ck(*tensors, out=view)
+    torch.cuda.synchronize()
+    assert MoltenRuntime.read_status(0) == 0
+    assert torch.equal(big[:guard], pattern[:guard]), f"{label}: wrote before its output"
+    assert torch.equal(big[guard + nbytes:], pattern[guard + nbytes:]), f"{label}: wrote past its output"
+    assert torch.equal(view, ref), f"{label}: output through a view differs"
+    for t, b in zip(tensors, before):
+        assert torch.equal(t, b), f"{label}: an input was modified"
+
+
+def test_bad_modules_and_launches_are_refused():
+    """Host-side failure detection with a GPU present: an image that is not
+    a cubin and an unknown kernel name come back as status codes with a
+    message; nothing is launched."""
+    import ctypes
+    from molten_b200 import _capi
+    lib = _capi.load_library()
+    junk = b"this is not an sm_100a cubin " * 64
+    h = ctypes.c_void_p()
+    rc = lib.molten_module_load_data(junk, len(junk), 0, ctypes.byref(h))
+    assert rc != 0 and lib.molten_last_error()
+    rt = MoltenRuntime()
+    ck = rt.compile(compile_graph(graphs.rmsnorm(4, 64))[0])
+    ck(torch.randn(4, 64, device=DEV), torch.ones(64, device=DEV))    # loads the module
+    spec = next(iter(ck._specs.values()))
+    mod = spec.module(0).handle
+    cfg = _capi.LaunchCfg()
+    cfg.grid[:] = [1, 1, 1]
+    cfg.block[:] = [32, 1, 1]
+    cfg.cluster[:] = [1, 1, 1]
+    params = ctypes.create_string_buffer(8)
+    rc = lib.molten_launch(mod, b"no_such_kernel", ctypes.byref(cfg), params, 8, None)
+    assert rc != 0 and b"no_such_kernel" in lib.molten_last_error()
+    torch.cuda.synchronize()
+    assert MoltenRuntime.read_status(0) == 0

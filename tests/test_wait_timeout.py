@@ -66,3 +66,25 @@ def test_gemm_wait_runs_out_and_the_next_launch_is_correct():
     res = orc.evaluate(g, {"A": _bits(A), "B": _bits(B), "bias": _bits(bias)})
     assert_close(out.float().cpu().numpy(), res[("f32", g.ops[g._outputs[0]].inputs[0])],
                  "bfloat16", "GEMM after a timed-out launch")
+
+
+def test_debug_mode_raises_at_the_call(monkeypatch):
+    """MOLTEN_DEBUG: the call whose bounded wait ran out raises, with the
+    status bits in the message, and leaves the word clear for the next call."""
+    from molten_b200 import _capi, runtime
+    m, k, n = 128, 256, 128
+    g = graphs.gemm_bias_gelu(m, k, n)
+    kern = CodeGenerator(dtype="bfloat16", tune={"gemm": {"pair": False, "streamk": False}}) \
+        .generate(g, FusionEngine().fuse(g)[0])
+    A = torch.randn(m, k, device=DEV).to(torch.bfloat16)
+    B = (torch.randn(k, n, device=DEV) / k ** 0.5).to(torch.bfloat16)
+    bias = torch.zeros(n, device=DEV).to(torch.bfloat16)
+    MoltenRuntime.read_status(0, reset=True)
+    monkeypatch.setattr(runtime, "DEBUG", True)
+    broken = _Spec(kern, build_cubin(kern.source, kern.name + "_skipk2", extra_flags=[
+        "-DMOLTEN_WAIT_NS=20000000ull", "-DMOLTEN_TEST_SKIP_KSTEP=2"]))
+    with pytest.raises(_capi.MoltenError, match="bounded wait ran out"):
+        broken.run([A, B, bias], None, None, 0)
+    assert MoltenRuntime.read_status(0) == 0
+    out = MoltenRuntime().compile(kern)(A, B, bias)      # a good call passes the check
+    assert out.shape == (m, n)
