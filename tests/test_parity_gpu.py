@@ -1207,3 +1207,25 @@ def test_bad_modules_and_launches_are_refused():
     assert rc != 0 and b"no_such_kernel" in lib.molten_last_error()
     torch.cuda.synchronize()
     assert MoltenRuntime.read_status(0) == 0
+
+
+@pytest.mark.parametrize("rows,cols,causal,shift,spread", [
+    (300, 2048, False, 1000.0, 20.0),
+    (151, 32768, False, -500.0, 50.0),
+    (160, 8192, True, 250.0, 30.0),
+    (129, 2048, True, 0.0, 40.0),
+])
+def test_fp32_softmax_large_logits(rt, rows, cols, causal, shift, spread):
+    """fp32 softmax takes its exponentials on the EX2 unit as 2^((x - m)
+    log2e): with logits far from zero and widely spread, the result must
+    still meet the fp32 bar against the oracle (subtracting the max first
+    keeps the argument's error proportional to x - m, not to x)."""
+    g = graphs.softmax((rows, cols), causal=causal)
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(rows + cols)
+    x = shift + spread * torch.randn(rows, cols, generator=gen, device=DEV)
+    out, _ = run_graph(rt, g, [x], "float32")
+    torch.cuda.synchronize()
+    res = orc.evaluate(g, {"logits": to_numpy(x)})
+    assert_close(as_f32(out), res[("f32", g.ops[g._outputs[0]].inputs[0])], "float32",
+                 f"softmax fp32 {rows}x{cols} causal={causal} logits {shift}+{spread}N")
