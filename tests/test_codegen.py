@@ -476,6 +476,20 @@ def test_run_host_row_split_rules():
     assert flags(graphs.rope(1, 16, 4, 128), [e(1, 16, 4, 128), e(16, 64), e(16, 64)]) is None
 
 
+def test_host_row_blocks():
+    """Row blocks of a host-buffer call tile the rows in order; the last
+    two are 3/4 and 1/4 of a regular block; no block is empty."""
+    from molten_b200.runtime import host_row_blocks
+    assert host_row_blocks(8192, 5) == [(0, 2048), (2048, 4096), (4096, 6144), (6144, 7680),
+                                        (7680, 8192)]
+    assert host_row_blocks(100, 1) == [(0, 100)] and host_row_blocks(100, 2) == [(0, 50), (50, 100)]
+    for rows in (1, 2, 3, 7, 1000, 8193):
+        for chunks in (1, 2, 3, 4, 5, 8, 16):
+            b = host_row_blocks(rows, chunks)
+            assert b[0][0] == 0 and b[-1][1] == rows and all(r1 > r0 for r0, r1 in b)
+            assert all(b[i][1] == b[i + 1][0] for i in range(len(b) - 1))
+
+
 def test_stream_k_plan():
     """Stream-K for GEMMs with at most half the SMs' worth of tiles, a long
     K and few rows, with at most SK_MAX_PIECES CTAs per tile; the workspace
