@@ -170,12 +170,12 @@ def test_causal_zero_tail_selection():
 
 
 def test_long_16bit_rows_take_the_stream_form():
-    """bf16 rows long enough for a cluster run as one 1024-thread CTA per
-    row in the persistent stream form; fp32 rows as one 1024-thread CTA in
-    the register form."""
+    """bf16 rows long enough for a cluster run as one CTA per row (512
+    threads when 8 slots per thread hold the row) in the persistent stream
+    form; fp32 rows as one 1024-thread CTA in the register form."""
     sk = compile_graph(graphs.softmax((4096, 32768), dtype="bfloat16"), dtype="bfloat16")[0] \
         .plan.kernels[0]
-    assert (sk.config["tpc"], sk.config["cl"], sk.config["stream"]) == (1024, 1, 3)
+    assert (sk.config["tpc"], sk.config["cl"], sk.config["stream"], sk.config["nv"]) == (512, 1, 3, 8)
     assert sk.config["bulk"] and sk.config["smem"] == 3 * 32768 * 2
     sk = compile_graph(graphs.softmax((4096, 32768)))[0].plan.kernels[0]
     assert sk.config["cl"] == 1 and not sk.config.get("stream")
