@@ -897,7 +897,8 @@ def choose_row_tma_config(sk: SubKernel, prefetch: set, materialize: dict,
         nc_ranges = [[o["nc"]]] if "nc" in o else [range(8, 5, -1), range(14, 1, -1)]
     else:
         st_cap = max(2, s_max if "stages" in o else min(s_max, TMA_MAX_AUTO_STAGES))
-        nc_ranges = [[o["nc"]]] if "nc" in o else [[7, 5, 6, 8, 4, 3, 2, 1]]
+        # (4..8 teams over any stage count before fewer teams)
+        nc_ranges = [[o["nc"]]] if "nc" in o else [[7, 5, 6, 8, 4], [3, 2, 1]]
     nc_ranges = [[nc for nc in r if nc * (tw_req or 1) <= 31] for r in nc_ranges]
     best = None
     for ncs in nc_ranges:

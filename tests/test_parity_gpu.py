@@ -1229,3 +1229,52 @@ def test_fp32_softmax_large_logits(rt, rows, cols, causal, shift, spread):
     res = orc.evaluate(g, {"logits": to_numpy(x)})
     assert_close(as_f32(out), res[("f32", g.ops[g._outputs[0]].inputs[0])], "float32",
                  f"softmax fp32 {rows}x{cols} causal={causal} logits {shift}+{spread}N")
+
+
+def _two_pass_graph(rows, cols, dtype):
+    """LayerNorm without affine terms, then shifted by the row max:
+    y = (x - mean(x)) * rsqrt(mean((x - mean(x))^2) + eps); out = y - max(y)
+    -- reductions in three passes (mean; the centred second moment; a max)."""
+    from molten_b200.ir import DataflowGraph, OpType, TensorShape
+    g = DataflowGraph("two_pass")
+    x = g.add_input("x", TensorShape([rows, cols]), dtype=dtype)
+    mu = g.add_op(OpType.MEAN, [x])
+    g.ops[mu].reduction_dim = -1
+    d = g.sub(x, mu)
+    var = g.add_op(OpType.MEAN, [g.mul(d, d)])
+    g.ops[var].reduction_dim = -1
+    y = g.mul(d, g.add_op(OpType.RSQRT, [g.add(var, g.add_constant("eps", 1e-5))]))
+    mx = g.add_op(OpType.MAX, [y])
+    g.ops[mx].reduction_dim = -1
+    g.add_output(g.sub(y, mx))
+    return g
+
+
+@pytest.mark.parametrize("rows,cols,dtype,tune", [
+    (2048, 4096, "float32", None),
+    (2050, 3584, "bfloat16", None),
+    (2048, 4096, "bfloat16", {"row": {"engine": "tma", "tw": 1}}),
+    (300, 2048, "float32", {"row": {"engine": "tma", "tw": 5, "nc": 2}}),
+])
+def test_tma_ring_teams_multi_pass(rows, cols, dtype, tune):
+    """Reductions in several passes (sum, sum, max) on the TMA ring with
+    teams of warps per row: each pass's team reduction alternates between
+    the team's two shared-memory buffers; checked against the oracle."""
+    from molten_b200.codegen import CodeGenerator
+    from molten_b200.fusion import FusionEngine
+    g = _two_pass_graph(rows, cols, dtype)
+    groups = FusionEngine().fuse(g)
+    assert len(groups) == 1
+    gk = CodeGenerator(dtype=dtype, tune=tune).generate(g, groups[0])
+    (sk,) = gk.plan.kernels
+    assert sk.family == "row" and sk.config["engine"] == "tma" and sk.passes == 3
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(rows + cols)
+    x = (0.5 + 2 * torch.randn(rows, cols, generator=gen, device=DEV)).to(TORCH_DT[dtype])
+    ck = MoltenRuntime(tune=tune).compile(gk)
+    out = ck(x)
+    torch.cuda.synchronize()
+    assert MoltenRuntime.read_status(0) == 0
+    res = orc.evaluate(g, {"x": to_numpy(x)})
+    assert_close(as_f32(out), res[("f32", g.ops[g._outputs[0]].inputs[0])], dtype,
+                 f"two-pass ring {rows}x{cols} {dtype} {tune}")
