@@ -12,6 +12,7 @@ from .lowering import (
     rms_prologue, attention_pattern,
     group_boundary, infer_shapes,
     is_mask_const, prod, promote, split_group, EXPENSIVE, EW_TMA_MIN_ROWS,
+    EW_TMA_MIN_ROW_BYTES,
 )
 
 DEFAULT_SYMBOLIC_DIM = 1024
@@ -301,7 +302,10 @@ def _plan_sub(graph, family, ops, ext, outs, shapes, dts, tune) -> SubKernel:
             sk.config["materialize"] = sorted(materialize.items())
     else:
         # the TMA ring with teams of warps per row, from EW_TMA_MIN_ROWS rows
-        # with at least 4 stages, or when asked ({"ew": {"engine": "tma"}})
+        # of at least EW_TMA_MIN_ROW_BYTES per streamed operand with at least
+        # 4 stages, or when asked ({"ew": {"engine": "tma"}}) (measured, the
+        # chain at 4096 x 4096: 19.4 us ring, 20.7 elementwise; 8192 x 2048,
+        # 4 KB rows: 21.2-21.7 ring, 20.5 elementwise)
         # (measured, 8-op bf16 chain 16384 x 8192: 132.6 us as elementwise
         # kernel, 125.2 us on 5 stages with teams of 4 warps; with one warp
         # per row the ring's consumers were compute-bound at 50% of HBM)
@@ -310,7 +314,9 @@ def _plan_sub(graph, family, ops, ext, outs, shapes, dts, tune) -> SubKernel:
         if override.get("engine") == "tma":
             tma = choose_row_tma_config(sk, prefetch, {}, dict(override, min_stages=2))
         elif (override.get("engine") is None and "vec" not in override
-              and sk.rows >= EW_TMA_MIN_ROWS):
+              and sk.rows >= EW_TMA_MIN_ROWS
+              and all(sk.cols * DTYPE_SIZE[sk.operands[i].dtype] >= EW_TMA_MIN_ROW_BYTES
+                      for i in prefetch)):
             tma = choose_row_tma_config(sk, prefetch, {},
                                         dict(override, engine="tma", min_stages=4))
             if tma is not None and tma["stages"] < 4:
