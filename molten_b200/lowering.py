@@ -826,7 +826,8 @@ EW_TMA_MIN_ROWS = 4096   # elementwise groups take the ring from here on ...
 EW_TMA_MIN_ROW_BYTES = 8192  # ... when each streamed operand's row is this long
 TMA_MAX_AUTO_STAGES = 14
 TMA_CONSUMER_WARPS = 20  # consumer warps per CTA the team width aims at
-TMA_TEAM_MAX_ROWS = 4096 # reductions over this many rows: one warp per row
+TMA_TEAM_MAX_ROWS = 4096 # reductions over this many rows: one warp per row,
+TMA_ONE_WARP_MAX_SLOTS = 14  # when a lane holds at most this many slots of it
 
 
 def choose_row_tma_config(sk: SubKernel, prefetch: set, materialize: dict,
@@ -887,11 +888,16 @@ def choose_row_tma_config(sk: SubKernel, prefetch: set, materialize: dict,
     # (elementwise kernel) -> 139.2 (5 teams of 4; of 2: slower than the
     # elementwise kernel); RMSNorm*SiLU 8192 x 3584 30.0 with one warp per
     # row, 30.1 with teams of 2, 30.9 with teams of 3 (at full clocks,
-    # before the soak, teams of 3 had been faster: 29.2 vs 30.0).
+    # before the soak, teams of 3 had been faster: 29.2 vs 30.0) -- one warp
+    # per row only while a lane holds at most 14 slots of it: RMSNorm*SiLU
+    # bf16 x 4096 (16 slots) at 4096 / 8192 rows 21.3 / 40.1 us with one
+    # warp, 18.4 / 35.0 with 6 teams of 4; RMSNorm fp32 8192 x 5120 60.6 vs
+    # 58.4.
     tw_req = int(o["tw"]) if "tw" in o else None
     if tw_req is not None and (tw_req < 1 or 32 * (tw_req + 1) > 1024):
         raise LoweringError(f"row ring team of {tw_req} warps does not fit a CTA")
-    one_warp = tw_req == 1 or (tw_req is None and sk.passes > 0 and sk.rows >= TMA_TEAM_MAX_ROWS)
+    one_warp = tw_req == 1 or (tw_req is None and sk.passes > 0 and sk.rows >= TMA_TEAM_MAX_ROWS
+                               and sk.cols // vec <= 32 * TMA_ONE_WARP_MAX_SLOTS)
     if one_warp:
         # one warp per row: the most stages, 6..8 consumer warps measured best
         st_cap = max(2, s_max)
