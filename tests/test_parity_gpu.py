@@ -417,6 +417,7 @@ TEAM_CASES = [
     ("rmsnorm", 150, 5120, "float32", {"row": {"engine": "tma", "tw": 5, "nc": 2}}),
     ("rmsnorm", 5000, 64, "float32", {"row": {"engine": "tma", "tw": 2, "nc": 7}}),
     ("chain", 300, 1024, "bfloat16", {"ew": {"engine": "tma", "tw": 4}}),
+    ("rmsnorm_silu_gate", 2048, 8192, "bfloat16", None),
     ("chain", 4096, 4096, "bfloat16", None),
     ("chain", 4096, 2048, "bfloat16", {"ew": {"engine": "tma"}}),
 ]
