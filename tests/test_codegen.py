@@ -542,3 +542,34 @@ def test_causal_softmax_split_plan():
     x = gs.add_input("x", TS([4096, 32768]), dtype="bfloat16")
     gs.add_output(gs.softmax(gs.add(gs.mul(x, gs.add_constant("half", 0.5)), gs.causal_mask()), -1))
     assert compile_graph(gs, dtype="bfloat16")[0].plan.kernels[0].family == "row"
+
+
+def test_ring_selection_rules():
+    """TMA-ring choices: teams whose last slot round wastes at most 10%,
+    one warp per row for long row counts of rows of at most 14 slots a
+    lane, elementwise groups only with rows of >= 8 KB, 4..8 teams before
+    fewer, the ring from 6 stages."""
+    def cfg(g, dt="bfloat16", tune=None):
+        (k,) = compile_graph(g, dtype=dt) if tune is None else \
+            [CodeGenerator(dtype=dt, tune=tune).generate(g, FusionEngine().fuse(g)[0])]
+        return k.plan.kernels[0].family, k.plan.kernels[0].config
+    fam, c = cfg(graphs.rmsnorm_silu_gate(8192, 3584))
+    assert (c["engine"], c["nc"], c["tw"], c["stages"]) == ("tma", 7, 1, 14)     # the headline
+    fam, c = cfg(graphs.rmsnorm_silu_gate(2048, 3584))
+    assert (c["engine"], c["nc"], c["tw"]) == ("tma", 7, 3)                      # 7% waste
+    fam, c = cfg(graphs.rmsnorm_silu_gate(2048, 4096))
+    assert (c["nc"], c["tw"]) == (6, 4)                                          # 3 would waste 12.5%
+    fam, c = cfg(graphs.rmsnorm_silu_gate(8192, 4096))
+    assert c["engine"] == "tma" and c["tw"] == 4                                 # 16 slots a lane: teams
+    fam, c = cfg(graphs.rmsnorm_silu_gate(2048, 8192))
+    assert c["engine"] == "tma" and c["stages"] == 6
+    fam, c = cfg(graphs.rmsnorm(2048, 4096), "float32")
+    assert (c["nc"], c["stages"]) == (6, 12)                                     # not 1 team on 13
+    fam, c = cfg(graphs.rmsnorm_silu_gate(1024, 3584))
+    assert c["engine"] == "regs"                                                 # below 2048 rows
+    fam, c = cfg(graphs.chain(4096, 4096))
+    assert fam == "row" and c["engine"] == "tma"                                 # 8 KB rows
+    fam, c = cfg(graphs.chain(8192, 2048))
+    assert fam == "ew"                                                           # 4 KB rows
+    fam, c = cfg(graphs.rmsnorm_silu_gate(2048, 3584), tune={"row": {"tw": 2, "nc": 14}})
+    assert (c["nc"], c["tw"], c["stages"]) == (14, 2, 14)
