@@ -24,6 +24,7 @@ the first call with real tensors.
 from __future__ import annotations
 
 import json
+import re
 from dataclasses import dataclass, field
 from typing import Optional
 
@@ -193,6 +194,8 @@ class CodeGenerator:
             chunks.append(f"// Fused ops: {ops_txt}")
         chunks.append("// input dtypes: " + json.dumps(plan.input_dtypes))
         for d in self.tune.get("defines") or ():
+            if not re.fullmatch(r"[A-Za-z_][A-Za-z0-9_]*(=[A-Za-z0-9_.+\-]+)?", str(d)):
+                raise LoweringError(f"tune define {d!r} is not NAME or NAME=VALUE")
             chunks.append("#define " + str(d).replace("=", " ", 1))
         smem = 0
         block_x, block_y, fam = 256, 1, "ew"
