@@ -573,3 +573,16 @@ def test_ring_selection_rules():
     assert fam == "ew"                                                           # 4 KB rows
     fam, c = cfg(graphs.rmsnorm_silu_gate(2048, 3584), tune={"row": {"tw": 2, "nc": 14}})
     assert (c["nc"], c["tw"], c["stages"]) == (14, 2, 14)
+
+
+def test_fp32_softmax_exponentials():
+    """fp32 softmax: per-element exponentials on the EX2 unit with the max
+    subtracted first, the once-per-thread scale with expf; 16-bit outputs
+    fold the max into one FFMA."""
+    src32 = compile_graph(graphs.softmax((64, 2048)))[0].source
+    assert "fast_exp2((" in src32 and "- lz" in src32 and "expf(lm" in src32
+    src16 = compile_graph(graphs.softmax((64, 2048), dtype="bfloat16"), dtype="bfloat16")[0].source
+    assert "fast_exp2(fmaf(" in src16 and "expf(" not in src16.replace("__expf(", "")
+    # the split causal kernel takes the fast form for every output type
+    k = compile_graph(graphs.softmax((4096, 32768), causal=True))[0]
+    assert k.plan.kernels[0].family == "causal" and not k.plan.kernels[0].config["precise"]
