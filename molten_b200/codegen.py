@@ -272,7 +272,6 @@ class CodeGenerator:
 def declared_graph_shapes(graph: DataflowGraph) -> dict:
     """Shapes of every op from the declared INPUT shapes (symbolic dims get a
     stand-in size); ops whose shape cannot be inferred are left out."""
-    from .ir import BOUNDARY_OPS
     from .lowering import infer_shapes
     symbols: dict = {}
     shapes = {}

@@ -22,7 +22,6 @@ are widened exactly and outputs are rounded once (round to nearest even).
 
 from __future__ import annotations
 
-import math
 from dataclasses import dataclass, field
 from typing import Optional
 

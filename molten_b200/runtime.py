@@ -25,7 +25,6 @@ from __future__ import annotations
 import ctypes
 import hashlib
 import os
-import shutil
 import threading
 from collections import OrderedDict
 from dataclasses import dataclass, field

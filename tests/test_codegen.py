@@ -1,7 +1,6 @@
 """Code generation: reference-compatible surface, pattern families, and
 that every emitted module compiles for sm_100a."""
 import re
-import subprocess
 
 import pytest
 

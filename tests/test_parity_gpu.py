@@ -1005,7 +1005,6 @@ def test_misaligned_pointers_take_the_scalar_path(rt):
 
 
 def test_misaligned_output_is_refused_before_launch(rt):
-    from molten_b200._capi import MoltenError
     g = graphs.rmsnorm(4, 512)
     ck = rt.compile(compile_graph(g)[0])
     x = torch.randn(4, 512, device=DEV)
