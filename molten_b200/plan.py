@@ -537,6 +537,9 @@ def _plan_gemm(graph, ops, ext, outs, shapes, dts, tune) -> SubKernel:
     # B with leading dims: a batch of independent problems stacked in memory
     batch = prod(b_shape[:-2]) if len(b_shape) > 2 else 1
     M = int(a_shape[-2]) if batch > 1 else prod(a_shape[:-1])
+    if min(M, K, N, batch) <= 0:
+        raise LoweringError(f"MATMUL with an empty dimension (M={M}, K={K}, N={N}, batch={batch}) "
+                            "has no sm_100a lowering")
     if batch > 1 and prologue is not None:
         raise LoweringError("the RMSNorm prologue takes an unbatched B")
     # fp32 operands run on the bf16 tensor cores as three bf16 planes each

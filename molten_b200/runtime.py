@@ -272,6 +272,8 @@ class _Spec:
             outs = [torch.empty(s, dtype=d, device=dev)
                     for s, d in zip(plan.output_shapes, self.out_dtypes)]
         env.update(zip(plan.outputs, outs))
+        if all(o.numel() == 0 for o in outs):
+            return outs                      # empty outputs (no rows or no columns): no launch
         for op_id, (s, d) in self.temp_specs.items():
             env[op_id] = torch.empty(s, dtype=d, device=dev)
         mod = self.module(di)
@@ -346,6 +348,13 @@ class _Spec:
                 raise _capi.MoltenError(f"{self.gk.name}: a bounded wait ran out on device {di} "
                                         f"(status word {bits:#x})")
         return outs
+
+
+def _empty_outputs(gk: GeneratedKernel) -> bool:
+    """Every output of this specialisation has no elements (no rows or no
+    columns): calls return empty tensors without a launch."""
+    shapes = gk.plan.output_shapes if gk.plan is not None else []
+    return bool(shapes) and all(any(int(d) == 0 for d in s) for s in shapes)
 
 
 def _attn_tensor_2d(t):
@@ -490,7 +499,8 @@ class CompiledKernel:
                     tune[fam] = dict(tune.get(fam) or {}, vec=1)
             gen = CodeGenerator(dtype=None, tune=tune)
             gk = gen.generate(self.kernel.graph, self.kernel.group, shapes, dtypes)
-        cubin = build_cubin(gk.source, gk.name, self.runtime.cache_dir, self.runtime.verbose)
+        cubin = None if _empty_outputs(gk) else \
+            build_cubin(gk.source, gk.name, self.runtime.cache_dir, self.runtime.verbose)
         spec = _Spec(gk, cubin)
         self._specs[sig] = spec
         return spec
@@ -677,7 +687,9 @@ class MoltenRuntime:
         ck = self._compiled.get(key)
         if ck is not None:
             return ck
-        cubin = build_cubin(kernel.source, kernel.name, self.cache_dir, self.verbose)
+        # a specialisation whose outputs are empty launches nothing: no cubin
+        cubin = None if _empty_outputs(kernel) else \
+            build_cubin(kernel.source, kernel.name, self.cache_dir, self.verbose)
         ck = CompiledKernel(name=kernel.name, source=kernel.source, config=kernel.config,
                             _module=str(cubin), kernel=kernel, runtime=self)
         sig = None
@@ -686,7 +698,7 @@ class MoltenRuntime:
                         for d, s in zip(kernel.plan.input_dtypes, kernel.plan.input_shapes)) + (True,)
             ck._specs[sig] = _Spec(kernel, cubin)
         self._compiled[key] = ck
-        if self.verbose:
+        if self.verbose and cubin is not None:
             print(f"molten: built {cubin.name}")
         return ck
 

@@ -585,3 +585,21 @@ def test_fp32_softmax_exponentials():
     # the split causal kernel takes the fast form for every output type
     k = compile_graph(graphs.softmax((4096, 32768), causal=True))[0]
     assert k.plan.kernels[0].family == "causal" and not k.plan.kernels[0].config["precise"]
+
+
+def test_empty_shapes():
+    """A MATMUL with an empty dimension is refused with a clear error; row
+    and elementwise groups with no rows or no columns compile to a kernel
+    that launches nothing (no cubin is built)."""
+    from molten_b200.lowering import LoweringError
+    from molten_b200.runtime import MoltenRuntime, _empty_outputs
+    for m, k, n in ((0, 256, 512), (64, 0, 512), (64, 256, 0)):
+        with pytest.raises(LoweringError, match="empty dimension"):
+            compile_graph(graphs.gemm_bias_gelu(m, k, n), dtype="bfloat16")
+    for g, dt in ((graphs.rmsnorm_silu_gate(0, 3584), "bfloat16"), (graphs.rmsnorm(4, 0), "float32"),
+                  (graphs.chain(0, 1024), "bfloat16"), (graphs.softmax((0, 2048)), "float32")):
+        (k,) = compile_graph(g, dtype=dt)
+        assert _empty_outputs(k)
+        ck = MoltenRuntime().compile(k)            # no nvcc run for an empty specialisation
+        assert ck._module == "None"
+    assert not _empty_outputs(compile_graph(graphs.rmsnorm(4, 64))[0])

@@ -1279,3 +1279,35 @@ def test_tma_ring_teams_multi_pass(rows, cols, dtype, tune):
     res = orc.evaluate(g, {"x": to_numpy(x)})
     assert_close(as_f32(out), res[("f32", g.ops[g._outputs[0]].inputs[0])], dtype,
                  f"two-pass ring {rows}x{cols} {dtype} {tune}")
+
+
+@pytest.mark.parametrize("kind,shape,dtype", [
+    ("rmsnorm_silu_gate", (0, 3584), "bfloat16"),
+    ("rmsnorm", (4, 0), "float32"),
+    ("softmax", (0, 2048), "float32"),
+    ("chain", (0, 1024), "bfloat16"),
+])
+def test_empty_inputs_give_empty_outputs(rt, kind, shape, dtype):
+    """No rows (or no columns): the call returns an empty output of the
+    right shape and dtype and launches nothing; so does the host-buffer
+    call."""
+    rows, cols = shape
+    T = TORCH_DT[dtype]
+    if kind == "softmax":
+        g, tensors = graphs.softmax((rows, cols), dtype=dtype), [torch.empty(rows, cols, dtype=T, device=DEV)]
+    elif kind == "chain":
+        g = graphs.chain(rows, cols, dtype=dtype)
+        tensors = [torch.empty(rows, cols, dtype=T, device=DEV) for _ in range(2)]
+        tensors += [torch.zeros(cols, dtype=T, device=DEV) for _ in range(3)]
+    else:
+        g = graphs.BUILDERS[kind](rows, cols, dtype=dtype)
+        tensors = [torch.empty(rows, cols, dtype=T, device=DEV), torch.ones(cols, dtype=T, device=DEV)]
+        if kind == "rmsnorm_silu_gate":
+            tensors.append(torch.empty(rows, cols, dtype=T, device=DEV))
+    ck = rt.compile(compile_graph(g, dtype=dtype)[0])
+    out = ck(*tensors)
+    host = ck.run_host(*[t.cpu() for t in tensors], device=0)
+    torch.cuda.synchronize()
+    assert out.shape == (rows, cols) and out.dtype == T and out.device.type == "cuda"
+    assert tuple(host.shape) == (rows, cols) and host.dtype == T
+    assert MoltenRuntime.read_status(0) == 0
